@@ -1,0 +1,230 @@
+/*
+ * rouge-numerics-b200: C ABI of the B200 (sm_100a) implementation of the
+ * rouge-numerics GEMM / convolution / quantization path.
+ *
+ * Two groups of entry points live here.
+ *
+ * 1. Drop-in symbols. Same names, argument order and meaning as the
+ *    reference header software/rouge-numerics/include/rouge/numerics.h.
+ *    They take HOST pointers (row-major, caller-owned), copy to the GPU,
+ *    run the sm_100a kernels and copy back before returning. Invalid
+ *    arguments keep the reference's behaviour: `void` entries return
+ *    without writing, `int` quantizers return 0. A device failure (no GPU,
+ *    launch error, a device-side wait that ran out) is not a silent CPU
+ *    fallback: the call writes nothing further and the status is kept for
+ *    rouge_b200_last_error().
+ *
+ * 2. rouge_b200_* extensions. DEVICE pointers, an explicit cudaStream_t
+ *    passed as `void *stream` (NULL = legacy default stream), explicit
+ *    layouts, fused scales and output types. Every one returns an int
+ *    status (ROUGE_B200_OK == 0, negative on failure). Asynchronous with
+ *    respect to the host unless stated otherwise.
+ *
+ * Nothing here falls back to the CPU: with no usable GPU every entry fails
+ * with ROUGE_B200_ENODEV.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------ */
+/* Types shared with the reference                                          */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces RougeGemmConfig, numerics.h:35-41. Accepted and ignored by the
+ * GPU entries except as a hint; garbage values never cause out-of-bounds
+ * work (the reference normalises them at gemm.cpp:254-275). */
+typedef struct RougeGemmConfig {
+  int tile_m;
+  int tile_n;
+  int tile_k;
+  int unroll;
+  int split_k;
+} RougeGemmConfig;
+
+/* ------------------------------------------------------------------------ */
+/* Status codes and library state                                           */
+/* ------------------------------------------------------------------------ */
+
+#define ROUGE_B200_OK 0
+#define ROUGE_B200_EINVAL (-1)       /* bad pointer, size or enum value */
+#define ROUGE_B200_ENODEV (-2)       /* no CUDA device / not an sm_100 part */
+#define ROUGE_B200_ECUDA (-3)        /* a CUDA runtime call failed */
+#define ROUGE_B200_EUNSUPPORTED (-4) /* shape or alignment outside the kernel's contract */
+#define ROUGE_B200_ETIMEOUT (-5)     /* a bounded device-side wait ran out; results invalid */
+#define ROUGE_B200_ENOMEM (-6)       /* device or pinned allocation failed */
+
+/* Status of the last failing call on this host thread (0 if none since the
+ * last rouge_b200_clear_error). */
+int rouge_b200_last_error(void);
+void rouge_b200_clear_error(void);
+const char *rouge_b200_status_string(int status);
+
+/* Replaces rouge_gemm_isa_variant, numerics.h:331 (gemm.cpp:385-394).
+ * Returns "sm_100a+tcgen05". */
+const char *rouge_gemm_isa_variant(void);
+
+/* Replaces rouge_gemm_default_config, numerics.h:307 (gemm.cpp:281-289).
+ * Returns the reference's default {64,64,32,2,1}; the GPU path ignores it. */
+RougeGemmConfig rouge_gemm_default_config(void);
+
+/* 1 if a device usable by this library (compute capability 10.x) is
+ * present, else 0. */
+int rouge_b200_device_ok(void);
+
+/* Synchronises `stream`, then reads and clears the current device's error
+ * word, which kernels set when a bounded device-side wait runs out.
+ * Returns ROUGE_B200_OK or the failure (e.g. ROUGE_B200_ETIMEOUT). */
+int rouge_b200_sync_status(void *stream);
+
+/* Layout of the B operand of a GEMM. */
+#define ROUGE_B200_B_KN 0 /* B[K][N] row-major (the reference's layout)  */
+#define ROUGE_B200_B_NK 1 /* B[N][K] row-major (column-major B, K-major) */
+
+/* Output element type of a GEMM / conv epilogue. */
+#define ROUGE_B200_OUT_F32 0
+#define ROUGE_B200_OUT_BF16 1 /* RNE, NaN -> 0x7fc0 (fp16.cpp:101-112) */
+#define ROUGE_B200_OUT_I32 2  /* raw int32 accumulators (int8 GEMM only) */
+
+/* ------------------------------------------------------------------------ */
+/* Drop-in scalar format conversions (host functions, identical results)    */
+/* ------------------------------------------------------------------------ */
+
+/* Replace numerics.h:251-252 (fp8.cpp:42-106, 112-114). */
+uint8_t rouge_quantize_e4m3(float f);
+float rouge_dequantize_e4m3(uint8_t u);
+/* Replace numerics.h:293-296 (fp16.cpp:31-121). */
+uint16_t rouge_quantize_f16(float f);
+float rouge_dequantize_f16(uint16_t u);
+uint16_t rouge_quantize_bf16(float f);
+float rouge_dequantize_bf16(uint16_t u);
+
+/* ------------------------------------------------------------------------ */
+/* Drop-in host-pointer entries (synchronous, GPU-backed)                   */
+/* ------------------------------------------------------------------------ */
+
+/* Replaces rouge_quantize_i8_tensor, numerics.h:144-145
+ * (quant_int8.cpp:54-68). Returns 1 on success, 0 on bad arguments or a
+ * device failure. */
+int rouge_quantize_i8_tensor(const float *x, int n, float *scale_out, int8_t *out);
+
+/* Replaces rouge_quantize_i8_channel, numerics.h:146-147
+ * (quant_int8.cpp:72-90). One symmetric scale per row of x[rows][cols]. */
+int rouge_quantize_i8_channel(const float *x, int rows, int cols, float *scales,
+                              int8_t *out);
+
+/* Replace rouge_dequantize_i8_tensor / _channel, numerics.h:150-153
+ * (quant_int8.cpp:145-160). */
+void rouge_dequantize_i8_tensor(const int8_t *q, int n, float scale, float *out);
+void rouge_dequantize_i8_channel(const int8_t *q, int rows, int cols,
+                                 const float *scales, float *out);
+
+/* Replaces rouge_gemm_i8, numerics.h:160-162 (quant_int8.cpp:189-211).
+ * A[M][K] s8, B[K][N] s8 row-major; exact int32 accumulation, then
+ * C[m][n] = ((float)acc * sa) * sb. */
+void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
+                   const float *scales_a, int a_rows, const float *scales_b,
+                   int b_cols, float *C);
+
+/* Replaces rouge_gemm_e4m3, numerics.h:68-69 (fp8.cpp:116-124).
+ * A[M][K], B[K][N] OCP E4M3 codes; C f32 = dec(A) * dec(B), f32 accumulate. */
+void rouge_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B,
+                     float *C, const RougeGemmConfig *cfg);
+
+/* Replace rouge_gemm_f16 / rouge_gemm_bf16, numerics.h:301-304
+ * (fp16.cpp:123-141). A[M][K], B[K][N] half / bf16 codes; C f32. */
+void rouge_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B,
+                    float *C, const RougeGemmConfig *cfg);
+void rouge_gemm_bf16(int M, int N, int K, const uint16_t *A, const uint16_t *B,
+                     float *C, const RougeGemmConfig *cfg);
+
+/* ------------------------------------------------------------------------ */
+/* rouge_b200_* device-pointer extensions                                   */
+/* ------------------------------------------------------------------------ */
+
+/* Per-row symmetric int8 quantization of x[rows][cols] (f32, device).
+ * Bit-exact with quant_int8.cpp:72-90: amax in double, scale =
+ * (float)(amax/127.0) or 1.0f for an all-zero row, code =
+ * clamp(rne((double)x * (1.0/(double)scale)), -127, 127).
+ * scales[rows] f32, out[rows][cols] s8. Requires cols % 4 == 0 and 16-byte
+ * aligned x, 4-byte aligned out. */
+int rouge_b200_quantize_i8_rows(const float *x, int rows, int cols, float *scales,
+                                int8_t *out, void *stream);
+
+/* out[r][c] = (float)q[r][c] * scales[r]   (quant_int8.cpp:151-160).
+ * scales == NULL with scale != 0 uses one scale for the whole tensor
+ * (quant_int8.cpp:145-149). */
+int rouge_b200_dequantize_i8_rows(const int8_t *q, int rows, int cols,
+                                  const float *scales, float scale, float *out,
+                                  void *stream);
+
+/* Per-tensor absolute maximum of x[n] (f32, device) into *amax (device f32).
+ * NaNs are ignored, as std::fabs/operator> ignore them on the host. */
+int rouge_b200_absmax_f32(const float *x, size_t n, float *amax, void *stream);
+
+/* E4M3 codes of x[n] under a per-tensor scale:
+ *   s = amax / 448.0f (1.0f when amax == 0), out[i] = e4m3(x[i] / s),
+ * with the encoder of fp8.cpp:75-106 (RNE, satfinite, |v| < 2^-10 -> +0).
+ * amax is read from device memory (as written by rouge_b200_absmax_f32);
+ * s is written to *scale_out (device f32) when scale_out != NULL. */
+int rouge_b200_quantize_e4m3_scaled(const float *x, size_t n, const float *amax,
+                                    float *scale_out, uint8_t *out, void *stream);
+
+/* absmax + scaled encode in one call (two kernels, no host round trip).
+ * *amax_out (device) receives the tensor's absolute maximum, *scale_out
+ * (device, may be NULL, must differ from amax_out) receives s. */
+int rouge_b200_quantize_e4m3_tensor(const float *x, size_t n, float *amax_out,
+                                    float *scale_out, uint8_t *out, void *stream);
+
+/* Elementwise f32 <-> narrow conversions on device (fp16.cpp:61-112,
+ * fp8.cpp:42-106). */
+int rouge_b200_convert_f32_to_f16(const float *x, size_t n, uint16_t *out, void *stream);
+int rouge_b200_convert_f32_to_bf16(const float *x, size_t n, uint16_t *out, void *stream);
+int rouge_b200_convert_e4m3_to_f32(const uint8_t *x, size_t n, float *out, void *stream);
+
+/* int8 GEMM on tcgen05 (kind::i8), exact int32 accumulation in TMEM.
+ * A[M][K] s8 row-major; B per b_layout (ROUGE_B200_B_KN or _NK).
+ * Epilogue (fused): out_type F32:  C = ((float)acc * sa) * sb
+ *                   out_type BF16: bf16_rne(((float)acc * sa) * sb)
+ *                   out_type I32:  C = acc (scales ignored, may be NULL)
+ * sa = a_rows ? scales_a[m] : scales_a[0]; sb = b_cols ? scales_b[n] : scales_b[0].
+ * ldc = row pitch of C in elements (>= N). Requires K % 16 == 0 and
+ * (for B_KN) N % 16 == 0, 16-byte aligned A/B. */
+int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
+                       int b_layout, const float *scales_a, int a_rows,
+                       const float *scales_b, int b_cols, void *C, int ldc,
+                       int out_type, void *stream);
+
+/* E4M3 GEMM on tcgen05 (kind::f8f6f4), f32 accumulation in TMEM.
+ * C = acc * (scale_a[0] * scale_b[0]) when the scale pointers (device f32
+ * scalars) are non-NULL, else acc. out_type F32 or BF16. Same layout and
+ * alignment rules as rouge_b200_gemm_i8. */
+int rouge_b200_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B,
+                         int b_layout, const float *scale_a, const float *scale_b,
+                         void *C, int ldc, int out_type, void *stream);
+
+/* f16 / bf16 GEMM on tcgen05 (kind::f16), f32 accumulation in TMEM.
+ * is_bf16 selects the input format. C f32 (out_type F32) or bf16.
+ * Requires K % 8 == 0 and (for B_KN) N % 8 == 0. */
+int rouge_b200_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B,
+                        int b_layout, int is_bf16, void *C, int ldc, int out_type,
+                        void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Seeded synthetic inputs (host, multi-threaded)                           */
+/* ------------------------------------------------------------------------ */
+/* Counterparts of the reference's splitmix64 + Box-Muller generator
+ * (rouge_rng_*, numerics.h:237-246): counter-based splitmix64, so a fill is
+ * identical for any thread count. Return 0 (count for _outliers) or -1. */
+int rouge_b200_synth_uniform(uint64_t seed, size_t n, float lo, float hi, float *out);
+int rouge_b200_synth_normal(uint64_t seed, size_t n, float mean, float stddev, float *out);
+long long rouge_b200_synth_outliers(uint64_t seed, size_t n, float frac, float mult, float *x);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif

@@ -1,0 +1,496 @@
+// Dense GEMM on sm_100a tensor cores for the rouge-numerics path:
+//   kind::i8     int8 x int8 -> exact int32 in TMEM   (rouge_gemm_i8, quant_int8.cpp:189-211)
+//   kind::f8f6f4 e4m3 x e4m3 -> f32 in TMEM          (rouge_gemm_e4m3, fp8.cpp:116-124)
+//   kind::f16    f16/bf16 -> f32 in TMEM              (rouge_gemm_f16/bf16, fp16.cpp:123-141)
+//
+// One persistent CTA per SM (grid = min(tiles, SMs)), 256 threads:
+//   warp 0      TMA producer: A and B k-blocks into a STAGES-deep ring of
+//               128-byte-swizzled shared-memory stages (mbarrier full/empty)
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN,
+//               K=32 bytes per instruction) into a TMEM accumulator and
+//               releases each stage with tcgen05.commit
+//   warp 2      TMEM allocator (2 x BN columns: double-buffered accumulator)
+//   warps 4-7   epilogue: tcgen05.ld of their 32 TMEM lanes, fused scale /
+//               dequant / bf16 conversion, predicated global stores; runs
+//               while the MMA warp fills the other accumulator
+// C tile = 128 x BN. Tiles are walked in groups of 16 M-blocks so that the
+// CTAs of one wave share A and B panels in L2.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "formats.cuh"
+#include "ptx.cuh"
+#include "runtime.cuh"
+
+namespace rb200 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBKBytes = 128;   // one swizzle atom row: 128 B of K per stage row
+constexpr int kGroupM = 16;
+constexpr int kGemmThreads = 256;
+
+struct GemmArgs {
+  int M, N, K;
+  int num_m, num_n, num_k, num_tiles;
+  void *C;
+  long long ldc;
+  const float *scales_a;  // int8: per-row or single scale
+  const float *scales_b;  // int8: per-column or single scale
+  int a_rows, b_cols;
+  const float *scale_a;   // e4m3 / f16: per-tensor scale scalars (or null)
+  const float *scale_b;
+  int bf16;               // kind::f16 inputs are bf16
+  int vec_ok;             // C and ldc allow 16-byte vector stores
+  int *err;
+};
+
+template <MmaKind KIND, int BN, bool B_MN>
+struct Cfg {
+  static constexpr int ESIZE = KIND == MmaKind::F16 ? 2 : 1;
+  static constexpr int BK = kBKBytes / ESIZE;       // elements of K per stage
+  static constexpr int UMMA_K = 32 / ESIZE;         // elements of K per instruction
+  static constexpr int A_BYTES = kBM * kBKBytes;
+  static constexpr int B_BYTES = BN * kBKBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int B_CHUNKS = (BN * ESIZE) / kBKBytes;  // 128-byte N chunks (MN-major B)
+  static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
+  static_assert(TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,
+                "TMEM allocation must be a power of two >= 32");
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb, int &nb) {
+  const int group = t / (kGroupM * num_n);
+  const int first_m = group * kGroupM;
+  const int rows_in_group = min(num_m - first_m, kGroupM);
+  const int r = t - group * kGroupM * num_n;
+  mb = first_m + r % rows_in_group;
+  nb = r / rows_in_group;
+}
+
+__device__ __forceinline__ void report(int *err, volatile int *abort, int code) {
+  *abort = 1;
+  if (err) atomicCAS(err, 0, code);
+}
+
+template <MmaKind KIND, int BN, bool B_MN, int OUT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs args) {
+  using C = Cfg<KIND, BN, B_MN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *empty = full + C::STAGES;
+  uint64_t *tfull = empty + C::STAGES;  // [2]
+  uint64_t *tempty = tfull + 2;         // [2]
+  uint64_t *mdone = tempty + 2;         // [1] drain barrier for the abort path
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(mdone, 1);
+    *abort = 0;
+    mbar_init_fence();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
+        if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort)) {
+          report(args.err, abort, ROUGE_B200_ETIMEOUT);
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
+        tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * C::BK, mb * kBM);
+        if constexpr (!B_MN) {
+          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * C::BK, nb * BN);
+        } else {
+#pragma unroll
+          for (int j = 0; j < C::B_CHUNKS; ++j)
+            tma_load_2d(sB + s * C::B_BYTES + j * C::B_CHUNK_BYTES, &tmB, &full[s],
+                        nb * BN + j * (kBKBytes / C::ESIZE), kb * C::BK);
+        }
+      }
+    }
+    if (!ok) {
+      // Let the loads already issued land before the CTA's shared memory is
+      // released: the last STAGES iterations are the only ones in flight.
+      for (int j = (it > C::STAGES ? it - C::STAGES : 0); j < it; ++j) {
+        const volatile int never = 0;
+        mbar_wait(&full[j % C::STAGES], static_cast<uint32_t>(j / C::STAGES) & 1u, &never);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;  // S32 : F32
+    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : 0u;  // S8 / E4M3 / F16
+    const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
+    const uint32_t idesc = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, kBM, BN);
+    int it = 0, local = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x, ++local) {
+      const int slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tempty[slot], (use & 1u) ^ 1u, abort)) {
+        report(args.err, abort, ROUGE_B200_ETIMEOUT);
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
+        if (!mbar_wait(&full[s], round & 1u, abort)) {
+          report(args.err, abort, ROUGE_B200_ETIMEOUT);
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
+        const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BK / C::UMMA_K; ++k) {
+          const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
+          const uint64_t bdesc =
+              B_MN ? smem_desc_sw128(b0 + k * C::UMMA_K * kBKBytes, C::B_CHUNK_BYTES, 1024)
+                   : smem_desc_sw128(b0 + k * 32, 16, 1024);
+          umma<KIND>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        tc_commit(&empty[s]);
+      }
+      if (!ok) break;
+      tc_commit(&tfull[slot]);
+    }
+    if (!ok && issued) {
+      // Drain the MMAs already issued before TMEM is released.
+      const volatile int never = 0;
+      tc_commit(mdone);
+      mbar_wait(mdone, 0u, &never);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    int local = 0;
+    float sab = 1.0f;
+    if constexpr (KIND != MmaKind::I8) {
+      if (args.scale_a && args.scale_b) sab = __fmul_rn(__ldg(args.scale_a), __ldg(args.scale_b));
+    }
+    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      const int slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tfull[slot], use & 1u, abort)) {
+        report(args.err, abort, ROUGE_B200_ETIMEOUT);
+        break;
+      }
+      tc_fence_after_sync();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const bool row_ok = row < args.M;
+      float sa = 1.0f;
+      if constexpr (KIND == MmaKind::I8) {
+        if (OUT != ROUGE_B200_OUT_I32 && row_ok)
+          sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
+      }
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        const int col0 = nb * BN + c;
+        if (col0 >= args.N) break;  // warp-uniform
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), v);
+        tmem_ld_wait_regs(v);
+        if (!row_ok) continue;
+        const bool full_chunk = col0 + 32 <= args.N;
+        if constexpr (OUT == ROUGE_B200_OUT_I32) {
+          int32_t *crow = static_cast<int32_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
+          if (full_chunk && args.vec_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<int4 *>(crow + j) = make_int4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+            #pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) crow[j] = static_cast<int32_t>(v[j]);
+          }
+        } else {
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if constexpr (KIND == MmaKind::I8) {
+              const int col = col0 + j < args.N ? col0 + j : args.N - 1;
+              const float sb = __ldg(args.scales_b + (args.b_cols ? col : 0));
+              // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies
+              f[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
+            } else {
+              f[j] = __fmul_rn(__uint_as_float(v[j]), sab);
+            }
+          }
+          if constexpr (OUT == ROUGE_B200_OUT_F32) {
+            float *crow = static_cast<float *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
+            if (full_chunk && args.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4 *>(crow + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+            } else {
+              #pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) crow[j] = f[j];
+            }
+          } else {  // BF16
+            uint16_t *crow =
+                static_cast<uint16_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
+            if (full_chunk && args.vec_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 w;
+                w.x = encode_bf16(f[j]) | (static_cast<uint32_t>(encode_bf16(f[j + 1])) << 16);
+                w.y = encode_bf16(f[j + 2]) | (static_cast<uint32_t>(encode_bf16(f[j + 3])) << 16);
+                w.z = encode_bf16(f[j + 4]) | (static_cast<uint32_t>(encode_bf16(f[j + 5])) << 16);
+                w.w = encode_bf16(f[j + 6]) | (static_cast<uint32_t>(encode_bf16(f[j + 7])) << 16);
+                *reinterpret_cast<uint4 *>(crow + j) = w;
+              }
+            } else {
+              #pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) crow[j] = encode_bf16(f[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[slot]);
+    }
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+template <MmaKind KIND, int BN, bool B_MN, int OUT>
+int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
+                     cudaStream_t st) {
+  using C = Cfg<KIND, BN, B_MN>;
+  const CUtensorMapDataType dt =
+      C::ESIZE == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap ta, tb;
+  int s = make_tmap_2d(&ta, A, dt, args.K, args.M, static_cast<uint64_t>(lda) * C::ESIZE, C::BK,
+                       kBM);
+  if (s != ROUGE_B200_OK) return s;
+  if (!B_MN)
+    s = make_tmap_2d(&tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK, BN);
+  else
+    s = make_tmap_2d(&tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
+                     kBKBytes / C::ESIZE, C::BK);
+  if (s != ROUGE_B200_OK) return s;
+
+  auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT>;
+  // The shared-memory opt-in is a per-device function attribute.
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    if (s != ROUGE_B200_OK) return s;
+    attr_done.fetch_or(bit);
+  }
+  const int sms = current_sm_count();
+  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
+  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, args);
+  return cuda_status(cudaGetLastError());
+}
+
+template <MmaKind KIND, int BN, bool B_MN>
+int launch_out(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
+               int out_type, cudaStream_t st) {
+  switch (out_type) {
+    case ROUGE_B200_OUT_F32:
+      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_F32>(A, lda, B, ldb, args, st);
+    case ROUGE_B200_OUT_BF16:
+      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_BF16>(A, lda, B, ldb, args, st);
+    default:
+      if constexpr (KIND == MmaKind::I8)
+        return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_I32>(A, lda, B, ldb, args, st);
+      return set_status(ROUGE_B200_EINVAL);
+  }
+}
+
+template <MmaKind KIND>
+int launch_kind(const void *A, long long lda, const void *B, long long ldb, int b_layout,
+                GemmArgs args, int out_type, cudaStream_t st) {
+  // BN = 256 unless that leaves most SMs idle; then 128.
+  const int sms = current_sm_count();
+  const long long tiles256 =
+      static_cast<long long>((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
+  const int bn = tiles256 >= sms ? 256 : 128;
+  args.num_m = (args.M + kBM - 1) / kBM;
+  args.num_n = (args.N + bn - 1) / bn;
+  const int esize = KIND == MmaKind::F16 ? 2 : 1;
+  const int bk = kBKBytes / esize;
+  args.num_k = (args.K + bk - 1) / bk;
+  args.num_tiles = args.num_m * args.num_n;
+  const bool mn = b_layout == ROUGE_B200_B_KN;
+  if (bn == 256)
+    return mn ? launch_out<KIND, 256, true>(A, lda, B, ldb, args, out_type, st)
+              : launch_out<KIND, 256, false>(A, lda, B, ldb, args, out_type, st);
+  return mn ? launch_out<KIND, 128, true>(A, lda, B, ldb, args, out_type, st)
+            : launch_out<KIND, 128, false>(A, lda, B, ldb, args, out_type, st);
+}
+
+int check_common(int M, int N, int K, const void *A, const void *B, const void *Cp, int ldc,
+                 int b_layout, int out_type, int esize) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !Cp || ldc < N) return ROUGE_B200_EINVAL;
+  if (b_layout != ROUGE_B200_B_KN && b_layout != ROUGE_B200_B_NK) return ROUGE_B200_EINVAL;
+  if (out_type != ROUGE_B200_OUT_F32 && out_type != ROUGE_B200_OUT_BF16 &&
+      out_type != ROUGE_B200_OUT_I32)
+    return ROUGE_B200_EINVAL;
+  // TMA: 16-byte aligned bases and row pitches.
+  if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u))
+    return ROUGE_B200_EUNSUPPORTED;
+  if ((static_cast<long long>(K) * esize) % 16) return ROUGE_B200_EUNSUPPORTED;
+  if (b_layout == ROUGE_B200_B_KN && (static_cast<long long>(N) * esize) % 16)
+    return ROUGE_B200_EUNSUPPORTED;
+  return ROUGE_B200_OK;
+}
+
+int vec_ok(const void *Cp, long long ldc, int out_type) {
+  const int es = out_type == ROUGE_B200_OUT_BF16 ? 2 : 4;
+  return ((reinterpret_cast<uintptr_t>(Cp) & 15u) == 0 && (static_cast<long long>(ldc) * es) % 16 == 0)
+             ? 1
+             : 0;
+}
+
+}  // namespace
+
+int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
+                   long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
+                   int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
+  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.err = device_error_word();
+  return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
+int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const uint8_t *B,
+                     long long ldb, int b_layout, const float *scale_a, const float *scale_b,
+                     void *Cp, long long ldc, int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scale_a = scale_a; g.scale_b = scale_b;
+  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.err = device_error_word();
+  return launch_kind<MmaKind::F8F6F4>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
+int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const uint16_t *B,
+                    long long ldb, int b_layout, int is_bf16, void *Cp, long long ldc,
+                    int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.bf16 = is_bf16 ? 1 : 0;
+  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.err = device_error_word();
+  return launch_kind<MmaKind::F16>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
+}  // namespace rb200
+
+using namespace rb200;
+
+extern "C" {
+
+int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, int b_layout,
+                       const float *scales_a, int a_rows, const float *scales_b, int b_cols,
+                       void *C, int ldc, int out_type, void *stream) {
+  int s = check_common(M, N, K, A, B, C, ldc, b_layout, out_type, 1);
+  if (s != ROUGE_B200_OK) return set_status(s);
+  if (out_type != ROUGE_B200_OUT_I32 && (!scales_a || !scales_b)) return set_status(ROUGE_B200_EINVAL);
+  s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
+  return launch_gemm_i8(M, N, K, A, K, B, ldb, b_layout, scales_a, a_rows, scales_b, b_cols, C,
+                        ldc, out_type, as_stream(stream));
+}
+
+int rouge_b200_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B, int b_layout,
+                         const float *scale_a, const float *scale_b, void *C, int ldc,
+                         int out_type, void *stream) {
+  int s = check_common(M, N, K, A, B, C, ldc, b_layout, out_type, 1);
+  if (s != ROUGE_B200_OK) return set_status(s);
+  if (out_type == ROUGE_B200_OUT_I32 || (!scale_a) != (!scale_b)) return set_status(ROUGE_B200_EINVAL);
+  s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
+  return launch_gemm_e4m3(M, N, K, A, K, B, ldb, b_layout, scale_a, scale_b, C, ldc, out_type,
+                          as_stream(stream));
+}
+
+int rouge_b200_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B, int b_layout,
+                        int is_bf16, void *C, int ldc, int out_type, void *stream) {
+  int s = check_common(M, N, K, A, B, C, ldc, b_layout, out_type, 2);
+  if (s != ROUGE_B200_OK) return set_status(s);
+  if (out_type == ROUGE_B200_OUT_I32) return set_status(ROUGE_B200_EINVAL);
+  s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
+  return launch_gemm_f16(M, N, K, A, K, B, ldb, b_layout, is_bf16, C, ldc, out_type,
+                         as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,281 @@
+// Drop-in host-pointer entries with the names and semantics of the
+// reference rouge-numerics C API (software/rouge-numerics/include/rouge/
+// numerics.h). Each call copies its operands into a library-owned device
+// workspace (padding rows where the kernels need 16-byte pitches), runs the
+// sm_100a kernels on the library stream, copies the result back and
+// synchronises. No CPU fallback: on a device failure the output is left
+// unwritten (or partly written) and the status is kept for
+// rouge_b200_last_error().
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "formats.cuh"
+#include "runtime.cuh"
+
+namespace rb200 {
+
+int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8_t *out,
+                         cudaStream_t st);
+int launch_quant_i8_tensor(const float *x, size_t n, float *amax, float *scale_out, int8_t *out,
+                           cudaStream_t st);
+int launch_dequant_i8(const int8_t *q, int rows, int cols, const float *scales, float scale,
+                      float *out, cudaStream_t st);
+int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
+                   long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
+                   int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st);
+int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const uint8_t *B,
+                     long long ldb, int b_layout, const float *scale_a, const float *scale_b,
+                     void *Cp, long long ldc, int out_type, cudaStream_t st);
+int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const uint16_t *B,
+                    long long ldb, int b_layout, int is_bf16, void *Cp, long long ldc,
+                    int out_type, cudaStream_t st);
+
+namespace {
+
+// Carves 256-byte-aligned sub-buffers out of the workspace.
+struct Carve {
+  uint8_t *base;
+  size_t off = 0;
+  explicit Carve(void *b) : base(static_cast<uint8_t *>(b)) {}
+  template <class T>
+  T *take(size_t count) {
+    T *p = reinterpret_cast<T *>(base + off);
+    off += round_up(count * sizeof(T), 256);
+    return p;
+  }
+  static size_t need(size_t bytes) { return round_up(bytes, 256); }
+};
+
+// Copies a host matrix [rows][cols] of `es`-byte elements into a device
+// buffer with row pitch `pitch` elements (zero-filling the padding).
+int h2d_pitched(void *dst, size_t pitch, const void *src, size_t rows, size_t cols, size_t es,
+                cudaStream_t st) {
+  if (pitch == cols)
+    return cuda_status(cudaMemcpyAsync(dst, src, rows * cols * es, cudaMemcpyHostToDevice, st));
+  int s = cuda_status(cudaMemsetAsync(dst, 0, rows * pitch * es, st));
+  if (s != ROUGE_B200_OK) return s;
+  return cuda_status(cudaMemcpy2DAsync(dst, pitch * es, src, cols * es, cols * es, rows,
+                                       cudaMemcpyHostToDevice, st));
+}
+
+int d2h_pitched(void *dst, const void *src, size_t pitch, size_t rows, size_t cols, size_t es,
+                cudaStream_t st) {
+  if (pitch == cols)
+    return cuda_status(cudaMemcpyAsync(dst, src, rows * cols * es, cudaMemcpyDeviceToHost, st));
+  return cuda_status(cudaMemcpy2DAsync(dst, cols * es, src, pitch * es, cols * es, rows,
+                                       cudaMemcpyDeviceToHost, st));
+}
+
+// Ends a drop-in call: waits for the stream and folds in any device-side
+// failure reported by the kernels.
+int finish(cudaStream_t st) {
+  int s = cuda_status(cudaStreamSynchronize(st));
+  if (s != ROUGE_B200_OK) return s;
+  return take_device_error(st);
+}
+
+// Generic float GEMM through the drop-in path. es = element size of A/B;
+// kind 0 = e4m3, 1 = f16, 2 = bf16.
+void gemm_codes_host(int kind, int M, int N, int K, const void *A, const void *B, float *C) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return;  // fp16.cpp:125, fp8.cpp:118
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t es = kind == 0 ? 1 : 2;
+  const size_t align = 16 / es;
+  const size_t Kp = round_up(K, align), Np = round_up(N, align);
+  const size_t need = Carve::need(M * Kp * es) + Carve::need(Kp * Np * es) +
+                      Carve::need(static_cast<size_t>(M) * N * 4);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  Carve cv(ctx->ws);
+  void *dA = cv.take<uint8_t>(M * Kp * es);
+  void *dB = cv.take<uint8_t>(Kp * Np * es);
+  float *dC = cv.take<float>(static_cast<size_t>(M) * N);
+  cudaStream_t st = ctx->stream;
+  if (h2d_pitched(dA, Kp, A, M, K, es, st) != ROUGE_B200_OK) return;
+  if (Kp != static_cast<size_t>(K) || Np != static_cast<size_t>(N)) {
+    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np * es, st)) != ROUGE_B200_OK) return;
+  }
+  if (cuda_status(cudaMemcpy2DAsync(dB, Np * es, B, N * es, N * es, K, cudaMemcpyHostToDevice,
+                                    st)) != ROUGE_B200_OK)
+    return;
+  int s;
+  if (kind == 0)
+    s = launch_gemm_e4m3(M, N, static_cast<int>(Kp), static_cast<const uint8_t *>(dA), Kp,
+                         static_cast<const uint8_t *>(dB), Np, ROUGE_B200_B_KN, nullptr, nullptr,
+                         dC, N, ROUGE_B200_OUT_F32, st);
+  else
+    s = launch_gemm_f16(M, N, static_cast<int>(Kp), static_cast<const uint16_t *>(dA), Kp,
+                        static_cast<const uint16_t *>(dB), Np, ROUGE_B200_B_KN, kind == 2, dC, N,
+                        ROUGE_B200_OUT_F32, st);
+  if (s != ROUGE_B200_OK) return;
+  if (finish(st) != ROUGE_B200_OK) return;  // do not copy a result a kernel failed to finish
+  if (cuda_status(cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost,
+                                  st)) != ROUGE_B200_OK)
+    return;
+  finish(st);
+}
+
+}  // namespace
+}  // namespace rb200
+
+using namespace rb200;
+
+extern "C" {
+
+uint8_t rouge_quantize_e4m3(float f) { return encode_e4m3(f); }
+float rouge_dequantize_e4m3(uint8_t u) { return decode_e4m3(u); }
+uint16_t rouge_quantize_f16(float f) { return encode_f16(f); }
+float rouge_dequantize_f16(uint16_t u) { return decode_f16(u); }
+uint16_t rouge_quantize_bf16(float f) { return encode_bf16(f); }
+float rouge_dequantize_bf16(uint16_t u) { return decode_bf16(u); }
+
+int rouge_quantize_i8_channel(const float *x, int rows, int cols, float *scales, int8_t *out) {
+  if (!x || !scales || !out || rows <= 0 || cols <= 0) return 0;  // quant_int8.cpp:74
+  HostCallContext *ctx = host_context();
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t cp = round_up(cols, 4);
+  const size_t need = Carve::need(rows * cp * 4) + Carve::need(rows * cp) + Carve::need(rows * 4);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return 0;
+  Carve cv(ctx->ws);
+  float *dx = cv.take<float>(rows * cp);
+  int8_t *dq = cv.take<int8_t>(rows * cp);
+  float *ds = cv.take<float>(rows);
+  cudaStream_t st = ctx->stream;
+  if (h2d_pitched(dx, cp, x, rows, cols, 4, st) != ROUGE_B200_OK) return 0;
+  if (launch_quant_i8_rows(dx, rows, static_cast<int>(cp), ds, dq, st) != ROUGE_B200_OK) return 0;
+  if (d2h_pitched(out, dq, cp, rows, cols, 1, st) != ROUGE_B200_OK) return 0;
+  if (cuda_status(cudaMemcpyAsync(scales, ds, rows * 4, cudaMemcpyDeviceToHost, st)) !=
+      ROUGE_B200_OK)
+    return 0;
+  return finish(st) == ROUGE_B200_OK ? 1 : 0;
+}
+
+int rouge_quantize_i8_tensor(const float *x, int n, float *scale_out, int8_t *out) {
+  if (!x || !scale_out || !out || n <= 0) return 0;  // quant_int8.cpp:56
+  HostCallContext *ctx = host_context();
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t need = Carve::need(static_cast<size_t>(n) * 4) + Carve::need(n) + Carve::need(8);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return 0;
+  Carve cv(ctx->ws);
+  float *dx = cv.take<float>(n);
+  int8_t *dq = cv.take<int8_t>(n);
+  float *dsc = cv.take<float>(2);  // [0] amax, [1] scale
+  cudaStream_t st = ctx->stream;
+  if (cuda_status(cudaMemcpyAsync(dx, x, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, st)) !=
+      ROUGE_B200_OK)
+    return 0;
+  if (launch_quant_i8_tensor(dx, n, dsc, dsc + 1, dq, st) != ROUGE_B200_OK) return 0;
+  if (cuda_status(cudaMemcpyAsync(out, dq, n, cudaMemcpyDeviceToHost, st)) != ROUGE_B200_OK) return 0;
+  if (cuda_status(cudaMemcpyAsync(scale_out, dsc + 1, 4, cudaMemcpyDeviceToHost, st)) !=
+      ROUGE_B200_OK)
+    return 0;
+  return finish(st) == ROUGE_B200_OK ? 1 : 0;
+}
+
+void rouge_dequantize_i8_channel(const int8_t *q, int rows, int cols, const float *scales,
+                                 float *out) {
+  if (!q || !scales || !out || rows <= 0 || cols <= 0) return;  // quant_int8.cpp:153
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t cp = round_up(cols, 4);
+  const size_t need = Carve::need(rows * cp) + Carve::need(rows * cp * 4) + Carve::need(rows * 4);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  Carve cv(ctx->ws);
+  int8_t *dq = cv.take<int8_t>(rows * cp);
+  float *dout = cv.take<float>(rows * cp);
+  float *ds = cv.take<float>(rows);
+  cudaStream_t st = ctx->stream;
+  if (h2d_pitched(dq, cp, q, rows, cols, 1, st) != ROUGE_B200_OK) return;
+  if (cuda_status(cudaMemcpyAsync(ds, scales, rows * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+    return;
+  if (launch_dequant_i8(dq, rows, static_cast<int>(cp), ds, 0.0f, dout, st) != ROUGE_B200_OK) return;
+  if (d2h_pitched(out, dout, cp, rows, cols, 4, st) != ROUGE_B200_OK) return;
+  finish(st);
+}
+
+void rouge_dequantize_i8_tensor(const int8_t *q, int n, float scale, float *out) {
+  if (!q || !out || n <= 0) return;  // quant_int8.cpp:147
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t np = round_up(n, 4);
+  const size_t need = Carve::need(np) + Carve::need(np * 4);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  Carve cv(ctx->ws);
+  int8_t *dq = cv.take<int8_t>(np);
+  float *dout = cv.take<float>(np);
+  cudaStream_t st = ctx->stream;
+  if (h2d_pitched(dq, np, q, 1, n, 1, st) != ROUGE_B200_OK) return;
+  if (launch_dequant_i8(dq, 1, static_cast<int>(np), nullptr, scale, dout, st) != ROUGE_B200_OK)
+    return;
+  if (cuda_status(cudaMemcpyAsync(out, dout, static_cast<size_t>(n) * 4, cudaMemcpyDeviceToHost,
+                                  st)) != ROUGE_B200_OK)
+    return;
+  finish(st);
+}
+
+void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, const float *scales_a,
+                   int a_rows, const float *scales_b, int b_cols, float *C) {
+  if (!A || !B || !scales_a || !scales_b || !C) return;  // quant_int8.cpp:192-193
+  if (M <= 0 || N <= 0 || K <= 0) return;
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t Kp = round_up(K, 16), Np = round_up(N, 16);
+  const size_t na = a_rows ? M : 1, nb = b_cols ? N : 1;
+  const size_t need = Carve::need(M * Kp) + Carve::need(Kp * Np) + Carve::need(na * 4) +
+                      Carve::need(nb * 4) + Carve::need(static_cast<size_t>(M) * N * 4);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  Carve cv(ctx->ws);
+  int8_t *dA = cv.take<int8_t>(M * Kp);
+  int8_t *dB = cv.take<int8_t>(Kp * Np);
+  float *dsa = cv.take<float>(na);
+  float *dsb = cv.take<float>(nb);
+  float *dC = cv.take<float>(static_cast<size_t>(M) * N);
+  cudaStream_t st = ctx->stream;
+  if (h2d_pitched(dA, Kp, A, M, K, 1, st) != ROUGE_B200_OK) return;
+  if (Kp != static_cast<size_t>(K) || Np != static_cast<size_t>(N)) {
+    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np, st)) != ROUGE_B200_OK) return;
+  }
+  if (cuda_status(cudaMemcpy2DAsync(dB, Np, B, N, N, K, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+    return;
+  if (cuda_status(cudaMemcpyAsync(dsa, scales_a, na * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+    return;
+  if (cuda_status(cudaMemcpyAsync(dsb, scales_b, nb * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+    return;
+  if (launch_gemm_i8(M, N, static_cast<int>(Kp), dA, Kp, dB, Np, ROUGE_B200_B_KN, dsa, a_rows ? 1 : 0,
+                     dsb, b_cols ? 1 : 0, dC, N, ROUGE_B200_OUT_F32, st) != ROUGE_B200_OK)
+    return;
+  if (finish(st) != ROUGE_B200_OK) return;
+  if (cuda_status(cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost,
+                                  st)) != ROUGE_B200_OK)
+    return;
+  finish(st);
+}
+
+void rouge_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B, float *C,
+                     const RougeGemmConfig *cfg) {
+  (void)cfg;
+  gemm_codes_host(0, M, N, K, A, B, C);
+}
+
+void rouge_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B, float *C,
+                    const RougeGemmConfig *cfg) {
+  (void)cfg;
+  gemm_codes_host(1, M, N, K, A, B, C);
+}
+
+void rouge_gemm_bf16(int M, int N, int K, const uint16_t *A, const uint16_t *B, float *C,
+                     const RougeGemmConfig *cfg) {
+  (void)cfg;
+  gemm_codes_host(2, M, N, K, A, B, C);
+}
+
+}  // extern "C"

@@ -1,0 +1,312 @@
+"""Python binding of librouge_b200.so (the C ABI in include/rouge/numerics_b200.h).
+
+A thin ctypes layer: every function here calls one exported C entry point.
+Device-pointer entries take torch CUDA tensors and the current torch stream;
+host-pointer (drop-in) entries take numpy arrays, exactly as a C caller of
+the reference rouge-numerics API passes host buffers. There is no CPU
+fallback: if the shared library is missing or the GPU path fails, calls
+raise.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.abspath(__file__))
+LIB_DIR = os.path.join(os.path.dirname(PKG_DIR), "lib")
+LIB_PATH = os.path.join(LIB_DIR, "librouge_b200.so")
+REPO_ROOT = os.path.dirname(os.path.dirname(PKG_DIR))
+HEADER = os.path.join(REPO_ROOT, "include", "rouge", "numerics_b200.h")
+
+OK = 0
+EINVAL = -1
+ENODEV = -2
+ECUDA = -3
+EUNSUPPORTED = -4
+ETIMEOUT = -5
+ENOMEM = -6
+
+B_KN = 0
+B_NK = 1
+OUT_F32 = 0
+OUT_BF16 = 1
+OUT_I32 = 2
+
+
+class RougeB200Error(RuntimeError):
+    def __init__(self, fn: str, status: int, msg: str):
+        super().__init__(f"{fn} failed: {status} ({msg})")
+        self.status = status
+
+
+def build() -> None:
+    """Compile librouge_b200.so in-tree (nvcc cross-compiles without a GPU)."""
+    subprocess.run(["make", "-s", "-C", os.path.dirname(PKG_DIR), "-j8"], check=True)
+
+
+_P = C.c_void_p
+_I = C.c_int
+_F = C.c_float
+_SZ = C.c_size_t
+_U64 = C.c_uint64
+
+_SIGS = {
+    "rouge_b200_last_error": (_I, []),
+    "rouge_b200_clear_error": (None, []),
+    "rouge_b200_status_string": (C.c_char_p, [_I]),
+    "rouge_gemm_isa_variant": (C.c_char_p, []),
+    "rouge_b200_device_ok": (_I, []),
+    "rouge_b200_sync_status": (_I, [_P]),
+    "rouge_quantize_e4m3": (C.c_uint8, [_F]),
+    "rouge_dequantize_e4m3": (_F, [C.c_uint8]),
+    "rouge_quantize_f16": (C.c_uint16, [_F]),
+    "rouge_dequantize_f16": (_F, [C.c_uint16]),
+    "rouge_quantize_bf16": (C.c_uint16, [_F]),
+    "rouge_dequantize_bf16": (_F, [C.c_uint16]),
+    "rouge_quantize_i8_tensor": (_I, [_P, _I, _P, _P]),
+    "rouge_quantize_i8_channel": (_I, [_P, _I, _I, _P, _P]),
+    "rouge_dequantize_i8_tensor": (None, [_P, _I, _F, _P]),
+    "rouge_dequantize_i8_channel": (None, [_P, _I, _I, _P, _P]),
+    "rouge_gemm_i8": (None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
+    "rouge_gemm_e4m3": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_gemm_f16": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_gemm_bf16": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_b200_quantize_i8_rows": (_I, [_P, _I, _I, _P, _P, _P]),
+    "rouge_b200_dequantize_i8_rows": (_I, [_P, _I, _I, _P, _F, _P, _P]),
+    "rouge_b200_absmax_f32": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_quantize_e4m3_scaled": (_I, [_P, _SZ, _P, _P, _P, _P]),
+    "rouge_b200_quantize_e4m3_tensor": (_I, [_P, _SZ, _P, _P, _P, _P]),
+    "rouge_b200_convert_f32_to_f16": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_convert_f32_to_bf16": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_convert_e4m3_to_f32": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_gemm_i8": (_I, [_I, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P]),
+    "rouge_b200_gemm_e4m3": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P, _I, _I, _P]),
+    "rouge_b200_gemm_f16": (_I, [_I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P]),
+    "rouge_b200_synth_uniform": (_I, [_U64, _SZ, _F, _F, _P]),
+    "rouge_b200_synth_normal": (_I, [_U64, _SZ, _F, _F, _P]),
+    "rouge_b200_synth_outliers": (C.c_longlong, [_U64, _SZ, _F, _F, _P]),
+}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded shared library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build() or "
+                               f"make -C rouge-v_b200")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def declared_symbols() -> list[str]:
+    """Names of every function declared in include/rouge/numerics_b200.h."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(rouge_\w+)\s*\(", text)))
+
+
+def _check(fn: str, status: int) -> None:
+    if status != OK:
+        msg = lib().rouge_b200_status_string(status).decode()
+        raise RougeB200Error(fn, status, msg)
+
+
+def _stream():
+    import torch
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dp(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _hp(a):
+    return a.ctypes.data_as(_P)
+
+
+# ----------------------------------------------------------------- device API
+
+def quantize_i8_rows(x, scales, out):
+    _check("rouge_b200_quantize_i8_rows", lib().rouge_b200_quantize_i8_rows(
+        _dp(x), x.shape[0], x.shape[1], _dp(scales), _dp(out), _stream()))
+
+
+def dequantize_i8_rows(q, scales, out, scale=0.0):
+    _check("rouge_b200_dequantize_i8_rows", lib().rouge_b200_dequantize_i8_rows(
+        _dp(q), q.shape[0], q.shape[1], _dp(scales), scale, _dp(out), _stream()))
+
+
+def absmax(x, amax):
+    _check("rouge_b200_absmax_f32", lib().rouge_b200_absmax_f32(_dp(x), x.numel(), _dp(amax), _stream()))
+
+
+def quantize_e4m3_scaled(x, amax, scale_out, out):
+    _check("rouge_b200_quantize_e4m3_scaled", lib().rouge_b200_quantize_e4m3_scaled(
+        _dp(x), x.numel(), _dp(amax), _dp(scale_out), _dp(out), _stream()))
+
+
+def quantize_e4m3_tensor(x, amax_out, scale_out, out):
+    _check("rouge_b200_quantize_e4m3_tensor", lib().rouge_b200_quantize_e4m3_tensor(
+        _dp(x), x.numel(), _dp(amax_out), _dp(scale_out), _dp(out), _stream()))
+
+
+def convert_f32_to_f16(x, out):
+    _check("rouge_b200_convert_f32_to_f16", lib().rouge_b200_convert_f32_to_f16(
+        _dp(x), x.numel(), _dp(out), _stream()))
+
+
+def convert_f32_to_bf16(x, out):
+    _check("rouge_b200_convert_f32_to_bf16", lib().rouge_b200_convert_f32_to_bf16(
+        _dp(x), x.numel(), _dp(out), _stream()))
+
+
+def convert_e4m3_to_f32(x, out):
+    _check("rouge_b200_convert_e4m3_to_f32", lib().rouge_b200_convert_e4m3_to_f32(
+        _dp(x), x.numel(), _dp(out), _stream()))
+
+
+def gemm_i8(A, B, b_layout, C_, out_type, scales_a=None, a_rows=1, scales_b=None, b_cols=1):
+    M, K = A.shape
+    N = B.shape[1] if b_layout == B_KN else B.shape[0]
+    _check("rouge_b200_gemm_i8", lib().rouge_b200_gemm_i8(
+        M, N, K, _dp(A), _dp(B), b_layout, _dp(scales_a), a_rows, _dp(scales_b), b_cols,
+        _dp(C_), C_.stride(0), out_type, _stream()))
+
+
+def gemm_e4m3(A, B, b_layout, C_, out_type, scale_a=None, scale_b=None):
+    M, K = A.shape
+    N = B.shape[1] if b_layout == B_KN else B.shape[0]
+    _check("rouge_b200_gemm_e4m3", lib().rouge_b200_gemm_e4m3(
+        M, N, K, _dp(A), _dp(B), b_layout, _dp(scale_a), _dp(scale_b), _dp(C_), C_.stride(0),
+        out_type, _stream()))
+
+
+def gemm_f16(A, B, b_layout, C_, out_type, is_bf16=False):
+    M, K = A.shape
+    N = B.shape[1] if b_layout == B_KN else B.shape[0]
+    _check("rouge_b200_gemm_f16", lib().rouge_b200_gemm_f16(
+        M, N, K, _dp(A), _dp(B), b_layout, int(is_bf16), _dp(C_), C_.stride(0), out_type,
+        _stream()))
+
+
+def sync_status():
+    _check("rouge_b200_sync_status", lib().rouge_b200_sync_status(_stream()))
+
+
+# ------------------------------------------------------------- host drop-in API
+
+def _last_error(fn):
+    st = lib().rouge_b200_last_error()
+    lib().rouge_b200_clear_error()
+    if st != OK:
+        raise RougeB200Error(fn, st, lib().rouge_b200_status_string(st).decode())
+
+
+def host_quantize_i8_channel(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    s = np.empty(rows, np.float32)
+    q = np.empty((rows, cols), np.int8)
+    lib().rouge_b200_clear_error()
+    if lib().rouge_quantize_i8_channel(_hp(x), rows, cols, _hp(s), _hp(q)) != 1:
+        _last_error("rouge_quantize_i8_channel")
+        raise RougeB200Error("rouge_quantize_i8_channel", EINVAL, "returned 0")
+    return q, s
+
+
+def host_quantize_i8_tensor(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    s = np.zeros(1, np.float32)
+    q = np.empty(x.size, np.int8)
+    lib().rouge_b200_clear_error()
+    if lib().rouge_quantize_i8_tensor(_hp(x), x.size, _hp(s), _hp(q)) != 1:
+        _last_error("rouge_quantize_i8_tensor")
+        raise RougeB200Error("rouge_quantize_i8_tensor", EINVAL, "returned 0")
+    return q, float(s[0])
+
+
+def host_dequantize_i8_channel(q: np.ndarray, scales: np.ndarray):
+    q = np.ascontiguousarray(q, np.int8)
+    scales = np.ascontiguousarray(scales, np.float32)
+    out = np.empty(q.shape, np.float32)
+    lib().rouge_b200_clear_error()
+    lib().rouge_dequantize_i8_channel(_hp(q), q.shape[0], q.shape[1], _hp(scales), _hp(out))
+    _last_error("rouge_dequantize_i8_channel")
+    return out
+
+
+def host_dequantize_i8_tensor(q: np.ndarray, scale: float):
+    q = np.ascontiguousarray(q, np.int8).ravel()
+    out = np.empty(q.size, np.float32)
+    lib().rouge_b200_clear_error()
+    lib().rouge_dequantize_i8_tensor(_hp(q), q.size, scale, _hp(out))
+    _last_error("rouge_dequantize_i8_tensor")
+    return out
+
+
+def host_gemm_i8(A, B_kn, sa, a_rows, sb, b_cols, out=None):
+    A = np.ascontiguousarray(A, np.int8)
+    B_kn = np.ascontiguousarray(B_kn, np.int8)
+    sa = np.ascontiguousarray(np.atleast_1d(sa), np.float32)
+    sb = np.ascontiguousarray(np.atleast_1d(sb), np.float32)
+    M, K = A.shape
+    N = B_kn.shape[1]
+    out = np.empty((M, N), np.float32) if out is None else out
+    lib().rouge_b200_clear_error()
+    lib().rouge_gemm_i8(M, N, K, _hp(A), _hp(B_kn), _hp(sa), a_rows, _hp(sb), b_cols, _hp(out))
+    _last_error("rouge_gemm_i8")
+    return out
+
+
+def _host_gemm_codes(name, A, B_kn, dtype):
+    A = np.ascontiguousarray(A, dtype)
+    B_kn = np.ascontiguousarray(B_kn, dtype)
+    M, K = A.shape
+    N = B_kn.shape[1]
+    out = np.empty((M, N), np.float32)
+    lib().rouge_b200_clear_error()
+    getattr(lib(), name)(M, N, K, _hp(A), _hp(B_kn), _hp(out), None)
+    _last_error(name)
+    return out
+
+
+def host_gemm_e4m3(A, B_kn):
+    return _host_gemm_codes("rouge_gemm_e4m3", A, B_kn, np.uint8)
+
+
+def host_gemm_f16(A, B_kn):
+    return _host_gemm_codes("rouge_gemm_f16", A, B_kn, np.uint16)
+
+
+def host_gemm_bf16(A, B_kn):
+    return _host_gemm_codes("rouge_gemm_bf16", A, B_kn, np.uint16)
+
+
+# ------------------------------------------------------------------ synthetic data
+
+def synth_uniform(seed: int, shape, lo: float, hi: float, out=None) -> np.ndarray:
+    out = np.empty(shape, np.float32) if out is None else out
+    assert lib().rouge_b200_synth_uniform(seed, out.size, lo, hi, _hp(out)) == 0
+    return out
+
+
+def synth_normal(seed: int, shape, mean: float, std: float, out=None) -> np.ndarray:
+    out = np.empty(shape, np.float32) if out is None else out
+    assert lib().rouge_b200_synth_normal(seed, out.size, mean, std, _hp(out)) == 0
+    return out
+
+
+def synth_outliers(seed: int, x: np.ndarray, frac: float, mult: float) -> int:
+    return int(lib().rouge_b200_synth_outliers(seed, x.size, frac, mult, _hp(x)))

@@ -1,0 +1,97 @@
+"""C-ABI surface of librouge_b200.so, checked without a GPU: every symbol
+declared in include/rouge/numerics_b200.h is exported, the host-side format
+converters match the oracle, device entries refuse cleanly with no device,
+and the synthetic-data generator is deterministic."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+
+def test_exports_every_declared_symbol(rb):
+    names = rb.declared_symbols()
+    assert len(names) >= 30
+    missing = [n for n in names if not hasattr(rb.lib(), n)]
+    assert not missing, missing
+
+
+def test_drop_in_names_match_reference_header(rb):
+    # The drop-in subset of software/rouge-numerics/include/rouge/numerics.h
+    for n in ("rouge_gemm_i8", "rouge_gemm_e4m3", "rouge_gemm_f16", "rouge_gemm_bf16",
+              "rouge_quantize_i8_tensor", "rouge_quantize_i8_channel",
+              "rouge_dequantize_i8_tensor", "rouge_dequantize_i8_channel",
+              "rouge_quantize_e4m3", "rouge_dequantize_e4m3", "rouge_quantize_f16",
+              "rouge_dequantize_f16", "rouge_quantize_bf16", "rouge_dequantize_bf16",
+              "rouge_gemm_isa_variant", "rouge_gemm_default_config"):
+        assert n in rb.declared_symbols()
+    assert rb.lib().rouge_gemm_isa_variant() == b"sm_100a+tcgen05"
+
+
+def test_host_converters_match_oracle(rb, orc, golden):
+    L = rb.lib()
+    x = golden["fmt_x"]
+    for enc, fmt in ((L.rouge_quantize_e4m3, "e4m3"), (L.rouge_quantize_f16, "f16"),
+                     (L.rouge_quantize_bf16, "bf16")):
+        got = np.array([enc(float(v)) for v in x.tolist()])
+        want = getattr(orc, f"{fmt}_encode")(x)
+        assert (got == want).all(), fmt
+    codes = np.arange(256)
+    got = np.array([L.rouge_dequantize_e4m3(int(c)) for c in codes], np.float32)
+    want = orc.e4m3_decode(codes.astype(np.uint8))
+    nan = np.isnan(want)
+    assert (np.isnan(got) == nan).all()
+    assert (got[~nan].view(np.uint32) == want[~nan].view(np.uint32)).all()
+    h = np.arange(0, 65536, 3)
+    got = np.array([L.rouge_dequantize_f16(int(c)) for c in h], np.float32)
+    want = orc.f16_decode(h.astype(np.uint16))
+    nan = np.isnan(want)
+    assert (np.isnan(got) == nan).all()
+    assert (got[~nan].view(np.uint32) == want[~nan].view(np.uint32)).all()
+
+
+def test_status_strings(rb):
+    L = rb.lib()
+    for st in (rb.OK, rb.EINVAL, rb.ENODEV, rb.ECUDA, rb.EUNSUPPORTED, rb.ETIMEOUT, rb.ENOMEM):
+        assert L.rouge_b200_status_string(st) != b"unknown status"
+
+
+def test_invalid_arguments_are_refused(rb):
+    L = rb.lib()
+    # NULL pointers / bad sizes: no write, EINVAL (reference: silent no-op, quant returns 0)
+    assert L.rouge_b200_gemm_i8(0, 4, 16, None, None, 0, None, 1, None, 1, None, 4, 0, None) == rb.EINVAL
+    assert L.rouge_b200_quantize_i8_rows(None, 4, 4, None, None, None) == rb.EINVAL
+    assert L.rouge_quantize_i8_channel(None, 4, 4, None, None) == 0
+    out = np.full(4, 7, np.float32)
+    L.rouge_gemm_i8(0, 2, 2, None, None, None, 1, None, 1, out.ctypes.data_as(C.c_void_p))
+    assert (out == 7).all()
+
+
+def test_no_cpu_fallback_without_device(rb):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    L = rb.lib()
+    assert L.rouge_b200_device_ok() == 0
+    L.rouge_b200_clear_error()
+    A = np.ones((4, 16), np.int8)
+    B = np.ones((16, 4), np.int8)
+    s = np.ones(4, np.float32)
+    out = np.full((4, 4), -1.0, np.float32)
+    p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    L.rouge_gemm_i8(4, 4, 16, p(A), p(B), p(s), 1, p(s), 1, p(out))
+    assert (out == -1.0).all()                       # nothing computed on the CPU
+    assert L.rouge_b200_last_error() == rb.ENODEV
+    x = np.ones((2, 4), np.float32)
+    assert L.rouge_quantize_i8_channel(p(x), 2, 4, p(s), p(A)) == 0
+
+
+def test_synth_is_deterministic_and_distributed(rb):
+    a = rb.synth_normal(42, (1 << 20,), 0.0, 1.0)
+    b = rb.synth_normal(42, (1 << 20,), 0.0, 1.0)
+    assert (a.view(np.uint32) == b.view(np.uint32)).all()
+    assert abs(a.mean()) < 5e-3 and abs(a.std() - 1.0) < 5e-3
+    u = rb.synth_uniform(0, (1 << 20,), -1.0, 1.0)
+    assert u.min() >= -1.0 and u.max() < 1.0 and abs(u.mean()) < 5e-3
+    x = np.ones(1 << 20, np.float32)
+    n = rb.synth_outliers(1, x, 0.01, 20.0)
+    assert abs(n / x.size - 0.01) < 1e-3 and (x == 20.0).sum() == n

@@ -1,0 +1,83 @@
+"""The drop-in host-pointer entries (same names and semantics as the
+reference numerics.h) against the golden outputs of the reference library,
+on the reference's own test shapes (odd sizes included: the entries pad
+operands internally)."""
+import numpy as np
+import pytest
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+def test_quantize_i8_channel_golden(rb, cuda, golden):
+    q, s = rb.host_quantize_i8_channel(golden["q8_x"])
+    assert (q == golden["q8_codes"]).all()
+    assert (s.view(np.uint32) == golden["q8_scales"].view(np.uint32)).all()
+
+
+def test_quantize_i8_tensor_golden(rb, cuda, golden):
+    q, s = rb.host_quantize_i8_tensor(golden["q8_x"][:20])
+    assert (q == golden["q8t_codes"].ravel()).all()
+    assert np.float32(s) == golden["q8t_scale"]
+
+
+def test_quantize_i8_odd_columns(rb, orc, cuda):
+    rng = np.random.default_rng(4)
+    for shape in ((5, 3), (9, 41), (2, 1)):
+        x = rng.standard_normal(shape).astype(np.float32)
+        q, s = rb.host_quantize_i8_channel(x)
+        oq, os_ = orc.quantize_i8_rows(x)
+        assert (q == oq).all() and (s == os_).all()
+
+
+def test_dequantize_round_trip(rb, orc, cuda, golden):
+    # tests/test_ai.cpp:100-123: per-row error <= half a step
+    x = golden["q8_x"][:3]
+    q, s = rb.host_quantize_i8_channel(x)
+    back = rb.host_dequantize_i8_channel(q, s)
+    assert (back.view(np.uint32) == orc.dequantize_i8_rows(q, s).view(np.uint32)).all()
+    step = np.abs(x).max(axis=1, keepdims=True).astype(np.float64) / 127.0
+    assert (np.abs(x - back) <= step * 0.5 + 1e-6).all()
+    qt, st = rb.host_quantize_i8_tensor(x)
+    bt = rb.host_dequantize_i8_tensor(qt, st)
+    assert (bt == qt.astype(np.float32) * np.float32(st)).all()
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c"])
+def test_gemm_i8_golden(rb, cuda, golden, tag):
+    A, B = golden[f"g8{tag}_A"], golden[f"g8{tag}_B"]
+    C = rb.host_gemm_i8(A, B, golden[f"g8{tag}_sa"], 1, golden[f"g8{tag}_sb"], 1)
+    assert (C.view(np.uint32) == golden[f"g8{tag}_C"].view(np.uint32)).all()
+
+
+def test_gemm_i8_exact_small(rb, cuda):
+    # tests/test_ai.cpp:163-184: llround(C / (sa*sb)) == integer product
+    rng = np.random.default_rng(0xA1)
+    A = rng.integers(-127, 128, (7, 11)).astype(np.int8)
+    B = rng.integers(-127, 128, (11, 5)).astype(np.int8)
+    sa, sb = np.float32(0.013), np.float32(0.021)
+    C = rb.host_gemm_i8(A, B, [sa], 0, [sb], 0)
+    want = A.astype(np.int64) @ B.astype(np.int64)
+    assert (np.rint(C.astype(np.float64) / (float(sa) * float(sb))).astype(np.int64) == want).all()
+
+
+def test_gemm_f16_bf16_golden(rb, cuda, golden):
+    # tests/test_gemm_f16.cpp:61-94: 1e-2 of scale vs the f32 GEMM
+    for a, b, c, fn in (("gh_A16", "gh_B16", "gh_C16", rb.host_gemm_f16),
+                        ("gh_Ab", "gh_Bb", "gh_Cb", rb.host_gemm_bf16)):
+        got = fn(golden[a], golden[b])
+        want = golden[c]
+        assert np.abs(got - want).max() / max(np.abs(want).max(), 1.0) < 1e-5
+        assert rel_l2(got, want) < 1e-2
+
+
+def test_gemm_e4m3_golden_exact(rb, cuda, golden):
+    got = rb.host_gemm_e4m3(golden["ge_A"], golden["ge_B"])
+    assert (got == golden["ge_C"]).all()
+
+
+def test_null_and_empty_are_noops(rb, cuda):
+    out = np.full((4, 4), 3.0, np.float32)
+    rb.lib().rouge_gemm_f16(0, 4, 4, None, None, out.ctypes.data, None)
+    assert (out == 3.0).all()

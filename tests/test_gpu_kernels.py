@@ -1,0 +1,283 @@
+"""GPU parity of the sm_100a kernels, called through the C ABI with device
+pointers, against the CPU oracle on the same seeded inputs.
+
+Integer, code and scale outputs must be bit-exact. Floating-point GEMM
+outputs must be within the north-star tolerance (relative L2 <= 1e-2) and,
+as a kernel-health bound, within 1e-4 of the double-accumulated oracle
+(e4m3/f16 products are exact in f32, so only summation order differs)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+TOL_CONTRACT = 1e-2
+TOL_KERNEL = 1e-4
+
+
+def dev_tensor(a, device):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+
+# ---------------------------------------------------------------- int8 quant
+
+@pytest.mark.parametrize("shape", [(1, 4), (3, 8), (48, 40), (257, 1028), (64, 8192), (16, 12288)])
+def test_quantize_i8_rows(rb, orc, cuda, shape):
+    rng = np.random.default_rng(shape[0] * 7 + shape[1])
+    x = rng.standard_normal(shape).astype(np.float32)
+    x[rng.random(shape) < 0.01] *= 20.0
+    xd = dev_tensor(x, cuda)
+    q = torch.empty(shape, dtype=torch.int8, device=cuda)
+    s = torch.empty(shape[0], dtype=torch.float32, device=cuda)
+    rb.quantize_i8_rows(xd, s, q)
+    rb.sync_status()
+    oq, os_ = orc.quantize_i8_rows(x)
+    assert (q.cpu().numpy() == oq).all()
+    assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
+
+
+def test_quantize_i8_rows_golden(rb, cuda, golden):
+    x = golden["q8_x"]
+    q = torch.empty(x.shape, dtype=torch.int8, device=cuda)
+    s = torch.empty(x.shape[0], dtype=torch.float32, device=cuda)
+    rb.quantize_i8_rows(dev_tensor(x, cuda), s, q)
+    rb.sync_status()
+    assert (q.cpu().numpy() == golden["q8_codes"]).all()
+    assert (s.cpu().numpy().view(np.uint32) == golden["q8_scales"].view(np.uint32)).all()
+
+
+def test_quantize_i8_rows_special_values(rb, orc, cuda):
+    x = np.zeros((6, 16), np.float32)
+    x[1] = np.inf                        # scale inf, codes from NaN products
+    x[2, :4] = [np.inf, -np.inf, 1.0, -1.0]
+    x[3] = 1e-44                         # subnormal row: scale underflows to 0
+    x[4, :3] = [np.nan, 2.0, -3.0]
+    x[5] = -0.0
+    q = torch.empty(x.shape, dtype=torch.int8, device=cuda)
+    s = torch.empty(6, dtype=torch.float32, device=cuda)
+    rb.quantize_i8_rows(dev_tensor(x, cuda), s, q)
+    rb.sync_status()
+    oq, os_ = orc.quantize_i8_rows(x)
+    assert (q.cpu().numpy() == oq).all()
+    assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
+
+
+def test_dequantize_i8_rows(rb, orc, cuda):
+    rng = np.random.default_rng(1)
+    q = rng.integers(-127, 128, (33, 64), dtype=np.int8)
+    s = rng.uniform(1e-3, 1.0, 33).astype(np.float32)
+    out = torch.empty((33, 64), dtype=torch.float32, device=cuda)
+    rb.dequantize_i8_rows(dev_tensor(q, cuda), dev_tensor(s, cuda), out)
+    rb.sync_status()
+    assert (out.cpu().numpy().view(np.uint32) == orc.dequantize_i8_rows(q, s).view(np.uint32)).all()
+
+
+# ---------------------------------------------------------------- formats
+
+def float_space():
+    bits = np.arange(0, 2 ** 32, 61, dtype=np.uint64).astype(np.uint32)
+    dense = np.arange(0x3A000000, 0x3C000000, dtype=np.uint32)  # |x| in [2^-11, 2^-7)
+    return np.concatenate([bits, dense, dense | 0x80000000]).view(np.float32)
+
+
+def test_e4m3_encode_float_space(rb, orc, cuda):
+    # amax = 448 gives s = 1, so the kernel encodes x / 1 = x itself.
+    x = float_space()
+    x = x[: x.size // 16 * 16]
+    amax = torch.tensor([448.0], dtype=torch.float32, device=cuda)
+    s = torch.zeros(1, dtype=torch.float32, device=cuda)
+    out = torch.empty(x.size, dtype=torch.uint8, device=cuda)
+    rb.quantize_e4m3_scaled(dev_tensor(x, cuda), amax, s, out)
+    rb.sync_status()
+    assert s.item() == 1.0
+    got = out.cpu().numpy()
+    want = orc.e4m3_encode(x)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, x[bad[:8]].view(np.uint32)
+
+
+@pytest.mark.parametrize("fmt", ["f16", "bf16"])
+def test_half_encode_float_space(rb, orc, cuda, fmt):
+    x = float_space()
+    out = torch.empty(x.size, dtype=torch.int16, device=cuda)
+    fn = rb.convert_f32_to_f16 if fmt == "f16" else rb.convert_f32_to_bf16
+    fn(dev_tensor(x, cuda), out)
+    rb.sync_status()
+    got = out.cpu().numpy().view(np.uint16)
+    want = getattr(orc, f"{fmt}_encode")(x)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, x[bad[:8]].view(np.uint32)
+
+
+def test_e4m3_decode_all_codes(rb, orc, cuda):
+    c = np.tile(np.arange(256, dtype=np.uint8), 5)
+    out = torch.empty(c.size, dtype=torch.float32, device=cuda)
+    rb.convert_e4m3_to_f32(dev_tensor(c, cuda), out)
+    rb.sync_status()
+    assert (out.cpu().numpy().view(np.uint32) == orc.e4m3_decode(c).view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("n", [1, 17, 1 << 20, (1 << 24) + 13])
+def test_e4m3_per_tensor(rb, orc, cuda, n):
+    rng = np.random.default_rng(n)
+    x = rng.standard_normal(n).astype(np.float32)
+    if n > 20:
+        x[5] = np.nan                    # ignored by the max
+        x[7] = -1e-7                     # far below 2^-10 after scaling: +0
+    xd = dev_tensor(x, cuda)
+    am = torch.empty(2, dtype=torch.float32, device=cuda)
+    out = torch.empty(n, dtype=torch.uint8, device=cuda)
+    if n % 4 == 0:
+        rb.quantize_e4m3_tensor(xd, am[0:1], am[1:2], out)
+    else:  # unaligned sizes go through the scalar tail
+        rb.quantize_e4m3_tensor(xd, am[0:1], am[1:2], out)
+    rb.sync_status()
+    oc, os_, oamax = orc.quantize_e4m3_tensor(x)
+    assert am[0].item() == np.float32(oamax)
+    assert np.float32(am[1].item()) == np.float32(os_)
+    assert (out.cpu().numpy() == oc).all()
+
+
+def test_absmax_all_zero(rb, cuda):
+    x = torch.zeros(1000, dtype=torch.float32, device=cuda)
+    am = torch.full((1,), 5.0, dtype=torch.float32, device=cuda)
+    rb.absmax(x, am)
+    rb.sync_status()
+    assert am.item() == 0.0
+
+
+# ---------------------------------------------------------------- GEMMs
+
+GEMM_SHAPES = [(128, 256, 128), (7, 5, 16), (300, 200, 96), (130, 96, 64), (1024, 1024, 1024),
+               (256, 4096, 512), (4096, 128, 256)]
+
+
+def gemm_operands(rng, M, N, K):
+    A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-127, 128, (N, K), dtype=np.int8)   # [N][K]
+    sa = rng.uniform(1e-3, 2e-2, M).astype(np.float32)
+    sb = rng.uniform(1e-3, 2e-2, N).astype(np.float32)
+    return A, B, sa, sb
+
+
+@pytest.mark.parametrize("shape", GEMM_SHAPES)
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_gemm_i8_int32_exact(rb, orc, cuda, shape, layout):
+    M, N, K = shape
+    if layout == "kn" and N % 16:
+        pytest.skip("B[K][N] needs N % 16 == 0 (16-byte rows)")
+    if K % 16:
+        pytest.skip("K % 16 == 0 required")
+    rng = np.random.default_rng(M * 31 + N * 7 + K)
+    A, B, sa, sb = gemm_operands(rng, M, N, K)
+    Bdev = B if layout == "nk" else np.ascontiguousarray(B.T)
+    lay = rb.B_NK if layout == "nk" else rb.B_KN
+    acc = torch.empty((M, N), dtype=torch.int32, device=cuda)
+    rb.gemm_i8(dev_tensor(A, cuda), dev_tensor(Bdev, cuda), lay, acc, rb.OUT_I32)
+    c = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    rb.gemm_i8(dev_tensor(A, cuda), dev_tensor(Bdev, cuda), lay, c, rb.OUT_F32,
+               dev_tensor(sa, cuda), 1, dev_tensor(sb, cuda), 1)
+    rb.sync_status()
+    oacc, oc = orc.gemm_i8(A, B, True, sa, 1, sb, 1)
+    got = acc.cpu().numpy()
+    assert (got == oacc).all(), np.argwhere(got != oacc)[:5]
+    assert (c.cpu().numpy().view(np.uint32) == oc.view(np.uint32)).all()
+
+
+def test_gemm_i8_bf16_and_scalar_scales(rb, orc, cuda):
+    rng = np.random.default_rng(77)
+    M, N, K = 384, 512, 256
+    A, B, sa, sb = gemm_operands(rng, M, N, K)
+    cb = torch.empty((M, N), dtype=torch.int16, device=cuda)
+    rb.gemm_i8(dev_tensor(A, cuda), dev_tensor(B, cuda), rb.B_NK, cb, rb.OUT_BF16,
+               dev_tensor(sa, cuda), 1, dev_tensor(sb, cuda), 1)
+    c0 = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    rb.gemm_i8(dev_tensor(A, cuda), dev_tensor(B, cuda), rb.B_NK, c0, rb.OUT_F32,
+               dev_tensor(sa[:1], cuda), 0, dev_tensor(sb[:1], cuda), 0)
+    rb.sync_status()
+    _, oc = orc.gemm_i8(A, B, True, sa, 1, sb, 1)
+    assert (cb.cpu().numpy().view(np.uint16) == orc.bf16_encode(oc)).all()
+    _, oc0 = orc.gemm_i8(A, B, True, sa[:1], 0, sb[:1], 0)
+    assert (c0.cpu().numpy().view(np.uint32) == oc0.view(np.uint32)).all()
+
+
+def test_gemm_i8_strided_output(rb, orc, cuda):
+    rng = np.random.default_rng(5)
+    M, N, K = 200, 96, 128
+    A, B, sa, sb = gemm_operands(rng, M, N, K)
+    big = torch.full((M, 160), -7, dtype=torch.int32, device=cuda)
+    rb.gemm_i8(dev_tensor(A, cuda), dev_tensor(B, cuda), rb.B_NK, big[:, 16:16 + N], rb.OUT_I32)
+    rb.sync_status()
+    oacc, _ = orc.gemm_i8(A, B, True)
+    g = big.cpu().numpy()
+    assert (g[:, 16:16 + N] == oacc).all()
+    assert (g[:, :16] == -7).all() and (g[:, 16 + N:] == -7).all()
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 128), (33, 48, 64), (512, 512, 512), (1000, 1200, 640)])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_gemm_e4m3(rb, orc, cuda, shape, layout):
+    M, N, K = shape
+    rng = np.random.default_rng(M + N + K)
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    b = rng.standard_normal((N, K)).astype(np.float32)
+    qa, sa, _ = orc.quantize_e4m3_tensor(a)
+    qb, sb, _ = orc.quantize_e4m3_tensor(b)
+    Bdev = qb if layout == "nk" else np.ascontiguousarray(qb.T)
+    lay = rb.B_NK if layout == "nk" else rb.B_KN
+    sad = torch.tensor([sa], dtype=torch.float32, device=cuda)
+    sbd = torch.tensor([sb], dtype=torch.float32, device=cuda)
+    c = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    rb.gemm_e4m3(dev_tensor(qa, cuda), dev_tensor(Bdev, cuda), lay, c, rb.OUT_F32)
+    cb = torch.empty((M, N), dtype=torch.int16, device=cuda)
+    rb.gemm_e4m3(dev_tensor(qa, cuda), dev_tensor(Bdev, cuda), lay, cb, rb.OUT_BF16, sad, sbd)
+    rb.sync_status()
+    want = orc.gemm_f32(orc.e4m3_decode(qa), orc.e4m3_decode(qb), True)
+    err = rel_l2(c.cpu().numpy(), want)
+    assert err < TOL_CONTRACT and err < TOL_KERNEL, err
+    wantb = want * np.float32(np.float32(sa) * np.float32(sb))
+    errb = rel_l2(orc.bf16_decode(cb.cpu().numpy().view(np.uint16)), wantb)
+    assert errb < TOL_CONTRACT, errb
+
+
+def test_gemm_e4m3_integer_data_exact(rb, orc, cuda, golden):
+    # tests/test_gemm_fp8.cpp:73-99: integers 1..8, the f32 result is exact
+    qa, qb_kn, want = golden["ge_A"], golden["ge_B"], golden["ge_C"]
+    c = torch.empty(want.shape, dtype=torch.float32, device=cuda)
+    rb.gemm_e4m3(dev_tensor(qa, cuda), dev_tensor(qb_kn, cuda), rb.B_KN, c, rb.OUT_F32)
+    rb.sync_status()
+    assert (c.cpu().numpy() == want).all()
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 64), (40, 56, 72), (512, 512, 512), (777, 640, 320)])
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+def test_gemm_f16(rb, orc, cuda, shape, bf16, layout):
+    M, N, K = shape
+    if layout == "kn" and N % 8:
+        pytest.skip("B[K][N] needs N % 8 == 0")
+    rng = np.random.default_rng(M * 3 + N + K)
+    enc = orc.bf16_encode if bf16 else orc.f16_encode
+    dec = orc.bf16_decode if bf16 else orc.f16_decode
+    a = enc(rng.uniform(-1, 1, (M, K)).astype(np.float32))
+    b = enc(rng.uniform(-1, 1, (N, K)).astype(np.float32))
+    Bdev = b if layout == "nk" else np.ascontiguousarray(b.T)
+    lay = rb.B_NK if layout == "nk" else rb.B_KN
+    c = torch.empty((M, N), dtype=torch.float32, device=cuda)
+    rb.gemm_f16(dev_tensor(a.view(np.int16), cuda), dev_tensor(Bdev.view(np.int16), cuda), lay, c,
+                rb.OUT_F32, is_bf16=bf16)
+    rb.sync_status()
+    want = orc.gemm_f32(dec(a), dec(b), True)
+    err = rel_l2(c.cpu().numpy(), want)
+    assert err < TOL_CONTRACT and err < TOL_KERNEL, err
+
+
+def test_unsupported_layouts_are_refused(rb, cuda):
+    A = torch.zeros((64, 24), dtype=torch.int8, device=cuda)   # K = 24: rows not 16-byte
+    B = torch.zeros((64, 24), dtype=torch.int8, device=cuda)
+    C = torch.zeros((64, 64), dtype=torch.int32, device=cuda)
+    with pytest.raises(rb.RougeB200Error) as e:
+        rb.gemm_i8(A, B, rb.B_NK, C, rb.OUT_I32)
+    assert e.value.status == rb.EUNSUPPORTED
