@@ -22,6 +22,7 @@
 #include <cstdint>
 
 #include "formats.cuh"
+#include "x86fp.cuh"
 #include "ptx.cuh"
 #include "runtime.cuh"
 
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int local = 0;
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
-      if (args.scale_a && args.scale_b) sab = __fmul_rn(__ldg(args.scale_a), __ldg(args.scale_b));
+      if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
     }
     for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
@@ -266,9 +267,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               const int col = col0 + j < args.N ? col0 + j : args.N - 1;
               const float sb = __ldg(args.scales_b + (args.b_cols ? col : 0));
               // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies
-              f[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
+              f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
             } else {
-              f[j] = __fmul_rn(__uint_as_float(v[j]), sab);
+              f[j] = x86_mul(__uint_as_float(v[j]), sab);
             }
           }
           if constexpr (OUT == ROUGE_B200_OUT_F32) {

@@ -12,6 +12,7 @@
 #include <cstdint>
 
 #include "formats.cuh"
+#include "x86fp.cuh"
 #include "runtime.cuh"
 
 namespace rb200 {
@@ -141,10 +142,10 @@ __global__ void __launch_bounds__(kThreads) dequant_i8_kernel(const int8_t *__re
     const uint32_t w = __ldcs(q4 + i);
     const float s = scales ? __ldg(scales + (i * 4) / cols) : scale;
     float4 o;
-    o.x = __fmul_rn(static_cast<float>(static_cast<int8_t>(w & 0xFFu)), s);
-    o.y = __fmul_rn(static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFFu)), s);
-    o.z = __fmul_rn(static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFFu)), s);
-    o.w = __fmul_rn(static_cast<float>(static_cast<int8_t>(w >> 24)), s);
+    o.x = x86_mul(static_cast<float>(static_cast<int8_t>(w & 0xFFu)), s);
+    o.y = x86_mul(static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFFu)), s);
+    o.z = x86_mul(static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFFu)), s);
+    o.w = x86_mul(static_cast<float>(static_cast<int8_t>(w >> 24)), s);
     __stcs(o4 + i, o);
   }
 }
@@ -175,10 +176,10 @@ __global__ void __launch_bounds__(kThreads) absmax_kernel(const float *__restric
 }
 
 __device__ __forceinline__ uint32_t enc4(float4 v, float s) {
-  return static_cast<uint32_t>(encode_e4m3(__fdiv_rn(v.x, s))) |
-         (static_cast<uint32_t>(encode_e4m3(__fdiv_rn(v.y, s))) << 8) |
-         (static_cast<uint32_t>(encode_e4m3(__fdiv_rn(v.z, s))) << 16) |
-         (static_cast<uint32_t>(encode_e4m3(__fdiv_rn(v.w, s))) << 24);
+  return static_cast<uint32_t>(encode_e4m3(x86_div(v.x, s))) |
+         (static_cast<uint32_t>(encode_e4m3(x86_div(v.y, s))) << 8) |
+         (static_cast<uint32_t>(encode_e4m3(x86_div(v.z, s))) << 16) |
+         (static_cast<uint32_t>(encode_e4m3(x86_div(v.w, s))) << 24);
 }
 
 // out[i] = e4m3(x[i] / s), s = amax / 448 (1 when amax == 0). 16 elements
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kThreads) e4m3_scaled_kernel(const float *__re
     o.w = enc4(a3, s);
     o16[i] = o;
   }
-  for (size_t t = n16 * 16 + tid; t < n; t += stride) out[t] = encode_e4m3(__fdiv_rn(x[t], s));
+  for (size_t t = n16 * 16 + tid; t < n; t += stride) out[t] = encode_e4m3(x86_div(x[t], s));
 }
 
 // ---------------------------------------------------------------- converts

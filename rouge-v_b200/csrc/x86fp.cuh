@@ -1,0 +1,34 @@
+// f32 multiply / divide with the NaN results of x86-64 SSE arithmetic.
+//
+// The reference computes on x86-64, where an operation with a NaN operand
+// returns that operand (quieted), and an invalid operation (0/0, inf/inf,
+// 0*inf) returns the "default NaN" 0xFFC00000, whose sign bit is set. The
+// GPU returns the canonical NaN 0x7FFFFFFF in all these cases. The sign of
+// a NaN decides its E4M3 code (sign|0x7F) and its f32 bits, so kernels whose
+// outputs must equal the reference bit for bit use these helpers. Results
+// for non-NaN outcomes are the plain IEEE round-to-nearest ones.
+#pragma once
+
+#include <cstdint>
+
+namespace rb200 {
+
+__device__ __forceinline__ float x86_quiet(float a) {
+  return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+}
+
+__device__ __forceinline__ float x86_div(float x, float s) {
+  if (isnan(x)) return x86_quiet(x);
+  if (isnan(s)) return x86_quiet(s);
+  const float q = __fdiv_rn(x, s);
+  return isnan(q) ? __uint_as_float(0xFFC00000u) : q;
+}
+
+__device__ __forceinline__ float x86_mul(float a, float b) {
+  if (isnan(a)) return x86_quiet(a);
+  if (isnan(b)) return x86_quiet(b);
+  const float p = __fmul_rn(a, b);
+  return isnan(p) ? __uint_as_float(0xFFC00000u) : p;
+}
+
+}  // namespace rb200

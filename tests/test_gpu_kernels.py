@@ -140,6 +140,25 @@ def test_e4m3_per_tensor(rb, orc, cuda, n):
     assert (out.cpu().numpy() == oc).all()
 
 
+def test_e4m3_per_tensor_special_values(rb, orc, cuda):
+    # x86-64 results the reference produces: a NaN operand keeps its sign,
+    # inf/inf is the negative default NaN, x/inf is +-0.
+    nan_neg = np.array([0xFFC00001], np.uint32).view(np.float32)[0]
+    cases = [
+        np.array([np.inf, -np.inf, 1.0, 0.0, -2.0, nan_neg, np.nan, -0.0] * 2, np.float32),
+        np.array([1e-44, -1e-44, 0.0, 3e-45] * 4, np.float32),    # amax/448 underflows to 0
+        np.array([0.0] * 16, np.float32),                          # amax 0 -> s = 1
+    ]
+    for x in cases:
+        am = torch.empty(2, dtype=torch.float32, device=cuda)
+        out = torch.empty(x.size, dtype=torch.uint8, device=cuda)
+        rb.quantize_e4m3_tensor(dev_tensor(x, cuda), am[0:1], am[1:2], out)
+        rb.sync_status()
+        oc, os_, _ = orc.quantize_e4m3_tensor(x)
+        assert np.float32(am[1].item()).view(np.uint32) == np.float32(os_).view(np.uint32)
+        assert (out.cpu().numpy() == oc).all(), (x, out.cpu().numpy(), oc)
+
+
 def test_absmax_all_zero(rb, cuda):
     x = torch.zeros(1000, dtype=torch.float32, device=cuda)
     am = torch.full((1,), 5.0, dtype=torch.float32, device=cuda)
