@@ -115,7 +115,17 @@ def make_inputs(rb):
 
 
 def l2_flush(buf):
-    buf.zero_()  # 256 MiB write: evicts the 126 MB L2
+    """Evict the 126 MB L2 before a timed step: write the first 256 MiB half
+    of `buf`, then read the second half, so the write-backs of the dirty lines
+    happen here and not inside the next timed kernel."""
+    half = buf.numel() // 2
+    buf[:half].zero_()
+    buf[half:].view(torch_int32()).sum()
+
+
+def torch_int32():
+    import torch
+    return torch.int32
 
 
 def run_ours(args, rank, world, local_rank):
@@ -136,19 +146,39 @@ def run_ours(args, rank, world, local_rank):
     sw = torch.empty(N, dtype=torch.float32, device=dev)
     C = torch.empty((M, N), dtype=torch.float32, device=dev)
     rb.quantize_i8_rows(wd, sw, qw)          # weights: quantized once per output channel
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.zeros(512 << 20, dtype=torch.uint8, device=dev)
+
+    def quant():
+        rb.quantize_i8_rows(xd, sx, qx)
+
+    def gemm():
+        rb.gemm_i8(qx, qw, rb.B_NK, C, rb.OUT_F32, sx, 1, sw, 1)
+
+    for _ in range(args.warmup):
+        l2_flush(flush)
+        quant()
+        gemm()
+    rb.sync_status()
+    # Each kernel is replayed from a CUDA graph: the host-side launch path
+    # (ctypes, tensor-map encoding) stays out of the device-timed step.
+    g_quant, g_gemm = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_quant):
+        quant()
+    with torch.cuda.graph(g_gemm):
+        gemm()
+    torch.cuda.synchronize()
 
     def step(evs=None):
         if evs:
             evs[0].record()
-        rb.quantize_i8_rows(xd, sx, qx)
+        g_quant.replay()
         if evs:
             evs[1].record()
-        rb.gemm_i8(qx, qw, rb.B_NK, C, rb.OUT_F32, sx, 1, sw, 1)
+        g_gemm.replay()
         if evs:
             evs[2].record()
 
-    for _ in range(args.warmup):
+    for _ in range(2):
         l2_flush(flush)
         step()
     rb.sync_status()
@@ -212,7 +242,8 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded splitmix64/Box-Muller, BASELINE config 2 distributions)",
         "config": {"workload": "w8a8_linear_4096 (BASELINE config 2)", "M": M, "N": N, "K": K,
                    "out": "f32", "weights": "pre-quantized per output channel (setup)",
-                   "l2": "flushed: 256 MiB write before every step",
+                   "l2": "flushed before every step: 256 MiB write, then 256 MiB read "
+                         "(dirty lines retired outside the timed region)",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<I8>",
                      "achieved": round(gemm_tops, 2), "peak": round(int8_peak, 1), "unit": "TOP/s",

@@ -20,6 +20,7 @@
 
 #include <atomic>
 #include <cstdint>
+#include <cstring>
 
 #include "formats.cuh"
 #include "x86fp.cuh"
@@ -32,7 +33,7 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBKBytes = 128;   // one swizzle atom row: 128 B of K per stage row
 constexpr int kGroupM = 16;
-constexpr int kGemmThreads = 256;
+constexpr int kGemmThreads = 384;  // warps 0-3: producer, MMA, TMEM allocator, idle; 4-11: epilogue
 
 struct GemmArgs {
   int M, N, K;
@@ -45,9 +46,11 @@ struct GemmArgs {
   const float *scale_a;   // e4m3 / f16: per-tensor scale scalars (or null)
   const float *scale_b;
   int bf16;               // kind::f16 inputs are bf16
-  int vec_ok;             // C and ldc allow 16-byte vector stores
+  int use_tma_store;      // C and ldc are 16-byte aligned: epilogue stores through TMA
   int *err;
 };
+
+constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
 
 template <MmaKind KIND, int BN, bool B_MN>
 struct Cfg {
@@ -62,7 +65,9 @@ struct Cfg {
   static constexpr int B_CHUNKS = (BN * ESIZE) / kBKBytes;  // 128-byte N chunks (MN-major B)
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int EPI_BYTES = 8 * kStageBytes;  // one staging buffer per epilogue warp
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(TMEM_COLS == 64 || TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512,
                 "TMEM allocation must be a power of two >= 32");
@@ -82,17 +87,128 @@ __device__ __forceinline__ void report(int *err, volatile int *abort, int code) 
   if (err) atomicCAS(err, 0, code);
 }
 
+// Converts one 32-column chunk of one warp's 32 accumulator rows (thread =
+// row, v[j] = column col0 + j) and writes it to C.
+//   TMA path: the chunk goes to a 128-byte (f32/i32) or 64-byte (bf16)
+//   swizzled staging buffer in shared memory and one lane issues a tiled
+//   TMA store of the 32 x 32 box; out-of-range rows and columns are
+//   clipped by the tensor map. Two buffers alternate per warp.
+//   Direct path (C not 16-byte aligned): predicated per-thread stores.
+template <MmaKind KIND, int OUT>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint32_t (&v)[32],
+                                               int col0, int row0, int row, bool row_ok, float sa,
+                                               bool sa_ok, float sab, uint8_t *buf,
+                                               const CUtensorMap *tmC, int lane) {
+  uint32_t o[32];  // f32 / i32 bits, or bf16 pairs in o[0..15]
+  if constexpr (OUT == ROUGE_B200_OUT_I32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) o[j] = v[j];
+  } else {
+    float f[32];
+    bool may_nan = true;
+    if constexpr (KIND == MmaKind::I8) {
+      float sbl;  // scale of column col0 + lane
+      if (args.b_cols) {
+        const int col = col0 + lane;
+        sbl = col < args.N ? __ldg(args.scales_b + col) : 0.0f;
+      } else {
+        sbl = __ldg(args.scales_b);
+      }
+      // With sa and every column scale of the chunk finite and below 2^96,
+      // (float)acc * sa is finite (|acc| < 2^31) and the second product can
+      // only overflow to +-inf, which x86 and the GPU both produce: no NaN,
+      // so the plain multiplies are exact here.
+      const bool fast = __all_sync(0xffffffffu, sa_ok && fabsf(sbl) < 7.9e28f);
+      may_nan = !fast;
+      // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies
+      if (fast) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sb = args.b_cols ? __shfl_sync(0xffffffffu, sbl, j) : sbl;
+          f[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float sb = args.b_cols ? __shfl_sync(0xffffffffu, sbl, j) : sbl;
+          f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__uint_as_float(v[j]), sab);
+    }
+    if constexpr (OUT == ROUGE_B200_OUT_F32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(f[j]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = bf16x2_rn(f[2 * j], f[2 * j + 1]);
+      if (may_nan) {  // the reference writes every NaN as 0x7fc0 (fp16.cpp:106)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          if (isnan(f[2 * j])) o[j] = (o[j] & 0xFFFF0000u) | 0x7FC0u;
+          if (isnan(f[2 * j + 1])) o[j] = (o[j] & 0x0000FFFFu) | 0x7FC00000u;
+        }
+      }
+    }
+  }
+
+  if (args.use_tma_store) {
+    if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
+    __syncwarp();
+    const uint32_t base = smem_u32(buf);
+    if constexpr (OUT == ROUGE_B200_OUT_BF16) {
+      const uint32_t r = base + static_cast<uint32_t>(lane) * 64u;  // 64-byte swizzle atoms
+      const uint32_t x = (static_cast<uint32_t>(lane) >> 1) & 3u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        st_shared_v4(r + ((static_cast<uint32_t>(k) ^ x) << 4), o[4 * k], o[4 * k + 1],
+                     o[4 * k + 2], o[4 * k + 3]);
+    } else {
+      const uint32_t r = base + static_cast<uint32_t>(lane) * 128u;  // 128-byte swizzle atoms
+      const uint32_t x = static_cast<uint32_t>(lane) & 7u;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        st_shared_v4(r + ((static_cast<uint32_t>(k) ^ x) << 4), o[4 * k], o[4 * k + 1],
+                     o[4 * k + 2], o[4 * k + 3]);
+    }
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (row0 < args.M) tma_store_2d(tmC, buf, col0, row0);
+      bulk_commit();
+    }
+    return;
+  }
+
+  if (!row_ok) return;
+  const bool full_chunk = col0 + 32 <= args.N;
+  if constexpr (OUT == ROUGE_B200_OUT_BF16) {
+    uint16_t *crow = static_cast<uint16_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full_chunk || col0 + j < args.N)
+        crow[j] = static_cast<uint16_t>(o[j >> 1] >> ((j & 1) * 16));
+  } else {
+    uint32_t *crow = static_cast<uint32_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full_chunk || col0 + j < args.N) crow[j] = o[j];
+  }
+}
+
 template <MmaKind KIND, int BN, bool B_MN, int OUT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
   using C = Cfg<KIND, BN, B_MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
   uint64_t *empty = full + C::STAGES;
   uint64_t *tfull = empty + C::STAGES;  // [2]
   uint64_t *tempty = tfull + 2;         // [2]
@@ -110,7 +226,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);  // one arrival per epilogue warp
+      mbar_init(&tempty[i], 8);  // one arrival per epilogue warp
     }
     mbar_init(mdone, 1);
     *abort = 0;
@@ -214,7 +330,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    // Eight warps: warp w reads TMEM lanes [32*(w%4), +32) (the lane quarter
+    // its position in the warpgroup allows) and half h = (w-4)/4 of the
+    // tile's columns. One 4 KB staging buffer per warp for its TMA stores.
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;
+    uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * kStageBytes;
     int local = 0;
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
@@ -230,77 +351,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int row0 = mb * kBM + quarter * 32;
+      const int row = row0 + lane;
       const bool row_ok = row < args.M;
       float sa = 1.0f;
       if constexpr (KIND == MmaKind::I8) {
-        if (OUT != ROUGE_B200_OUT_I32 && row_ok)
-          sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
+        if (OUT != ROUGE_B200_OUT_I32 && row_ok) sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
       }
+      const bool sa_ok = fabsf(sa) < 7.9e28f;  // finite and below 2^96
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        const int col0 = nb * BN + c;
-        if (col0 >= args.N) break;  // warp-uniform
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c), v);
-        tmem_ld_wait_regs(v);
-        if (!row_ok) continue;
-        const bool full_chunk = col0 + 32 <= args.N;
-        if constexpr (OUT == ROUGE_B200_OUT_I32) {
-          int32_t *crow = static_cast<int32_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
-          if (full_chunk && args.vec_ok) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<int4 *>(crow + j) = make_int4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-            #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) crow[j] = static_cast<int32_t>(v[j]);
-          }
-        } else {
-          float f[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if constexpr (KIND == MmaKind::I8) {
-              const int col = col0 + j < args.N ? col0 + j : args.N - 1;
-              const float sb = __ldg(args.scales_b + (args.b_cols ? col : 0));
-              // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies
-              f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
-            } else {
-              f[j] = x86_mul(__uint_as_float(v[j]), sab);
-            }
-          }
-          if constexpr (OUT == ROUGE_B200_OUT_F32) {
-            float *crow = static_cast<float *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
-            if (full_chunk && args.vec_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4 *>(crow + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < args.N) crow[j] = f[j];
-            }
-          } else {  // BF16
-            uint16_t *crow =
-                static_cast<uint16_t *>(args.C) + static_cast<long long>(row) * args.ldc + col0;
-            if (full_chunk && args.vec_ok) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 w;
-                w.x = encode_bf16(f[j]) | (static_cast<uint32_t>(encode_bf16(f[j + 1])) << 16);
-                w.y = encode_bf16(f[j + 2]) | (static_cast<uint32_t>(encode_bf16(f[j + 3])) << 16);
-                w.z = encode_bf16(f[j + 4]) | (static_cast<uint32_t>(encode_bf16(f[j + 5])) << 16);
-                w.w = encode_bf16(f[j + 6]) | (static_cast<uint32_t>(encode_bf16(f[j + 7])) << 16);
-                *reinterpret_cast<uint4 *>(crow + j) = w;
-              }
-            } else {
-              #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < args.N) crow[j] = encode_bf16(f[j]);
-            }
+      const int cols_left = args.N - nb * BN;
+      const int nchunks = cols_left >= BN ? BN / 32 : (cols_left + 31) / 32;  // warp-uniform
+      const int c_end = min(nchunks, (half + 1) * (BN / 64));
+      const int c_beg = half * (BN / 64);
+      if (c_beg < c_end) {
+        uint32_t va[32], vb[32];
+        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
+        tmem_ld_wait_regs(va);
+        for (int c = c_beg; c < c_end; c += 2) {
+          // The load of chunk c+1 is in flight while chunk c is converted and stored.
+          if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
+          epilogue_chunk<KIND, OUT>(args, va, nb * BN + c * 32, row0, row, row_ok, sa, sa_ok, sab,
+                                    stage, &tmC, lane);
+          if (c + 1 < c_end) {
+            tmem_ld_wait_regs(vb);
+            if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
+            epilogue_chunk<KIND, OUT>(args, vb, nb * BN + (c + 1) * 32, row0, row, row_ok, sa,
+                                      sa_ok, sab, stage, &tmC, lane);
+            if (c + 2 < c_end) tmem_ld_wait_regs(va);
           }
         }
       }
@@ -308,6 +387,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[slot]);
     }
+    if (args.use_tma_store && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before_sync();
@@ -334,6 +414,18 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
     s = make_tmap_2d(&tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
                      kBKBytes / C::ESIZE, C::BK);
   if (s != ROUGE_B200_OK) return s;
+  // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
+  // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  if (args.use_tma_store) {
+    const bool b16 = OUT == ROUGE_B200_OUT_BF16;
+    s = make_tmap_2d(&tc, args.C,
+                     b16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, args.N,
+                     args.M, static_cast<uint64_t>(args.ldc) * (b16 ? 2 : 4), 32, 32,
+                     b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != ROUGE_B200_OK) return s;
+  }
 
   auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT>;
   // The shared-memory opt-in is a per-device function attribute.
@@ -348,7 +440,7 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
   }
   const int sms = current_sm_count();
   const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, args);
+  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
   return cuda_status(cudaGetLastError());
 }
 
@@ -374,7 +466,13 @@ int launch_kind(const void *A, long long lda, const void *B, long long ldb, int 
   const int sms = current_sm_count();
   const long long tiles256 =
       static_cast<long long>((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
+#ifdef RB200_FORCE_BN  // compile-time tile override for tuning builds
+  const int bn = RB200_FORCE_BN;
+  (void)tiles256;
+  (void)sms;
+#else
   const int bn = tiles256 >= sms ? 256 : 128;
+#endif
   args.num_m = (args.M + kBM - 1) / kBM;
   args.num_n = (args.N + bn - 1) / bn;
   const int esize = KIND == MmaKind::F16 ? 2 : 1;
@@ -421,7 +519,7 @@ int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const in
   g.M = M; g.N = N; g.K = K;
   g.C = Cp; g.ldc = ldc;
   g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
-  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
   g.err = device_error_word();
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
@@ -433,7 +531,7 @@ int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const
   g.M = M; g.N = N; g.K = K;
   g.C = Cp; g.ldc = ldc;
   g.scale_a = scale_a; g.scale_b = scale_b;
-  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
   g.err = device_error_word();
   return launch_kind<MmaKind::F8F6F4>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
@@ -445,7 +543,7 @@ int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const
   g.M = M; g.N = N; g.K = K;
   g.C = Cp; g.ldc = ldc;
   g.bf16 = is_bf16 ? 1 : 0;
-  g.vec_ok = vec_ok(Cp, ldc, out_type);
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
   g.err = device_error_word();
   return launch_kind<MmaKind::F16>(A, lda, B, ldb, b_layout, g, out_type, st);
 }

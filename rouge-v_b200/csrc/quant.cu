@@ -9,10 +9,13 @@
 // multiple of the SM count, and warp-shuffle reductions.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <cstdint>
 
 #include "formats.cuh"
 #include "x86fp.cuh"
+#include "ptx.cuh"
 #include "runtime.cuh"
 
 namespace rb200 {
@@ -26,10 +29,26 @@ constexpr int kThreads = 256;
 // as quant_int8.cpp:38-46,87 computes it on x86-64: nearbyint of the
 // double product, then a conversion whose out-of-range / NaN result is
 // INT32_MIN, then the clamp to [-127, 127].
-__device__ __forceinline__ int code_i8(float x, double inv) {
+__device__ __forceinline__ int code_i8_exact(float x, double inv) {
   const double p = __dmul_rn(static_cast<double>(x), inv);
   if (!(p >= -2147483648.5 && p < 2147483647.5)) return -127;  // NaN, +-Inf, overflow
   const int q = __double2int_rn(p);
+  return q < -127 ? -127 : (q > 127 ? 127 : q);
+}
+
+// Same result as code_i8_exact, mostly in single precision. With
+// inv_f = (float)inv the f32 product differs from the double product by
+// less than 2^-15 whenever |p| < 2^8, so its round-to-nearest-even integer
+// agrees unless p lies within 2^-12 of a half-integer; those elements (and
+// large or non-finite products) take the double path. The integer is read
+// from the bits of p + 1.5 * 2^23, which rounds to nearest even.
+__device__ __forceinline__ int code_i8(float x, double inv, float inv_f) {
+  const float p = __fmul_rn(x, inv_f);
+  const float big = __fadd_rn(p, 12582912.0f);
+  const float r = __fsub_rn(big, 12582912.0f);
+  const float dist_to_tie = fabsf(fabsf(__fsub_rn(p, r)) - 0.5f);
+  if (!(fabsf(p) < 256.0f) || dist_to_tie < 0.000244140625f) return code_i8_exact(x, inv);
+  const int q = static_cast<int>(__float_as_uint(big)) - 0x4B400000;
   return q < -127 ? -127 : (q > 127 ? 127 : q);
 }
 
@@ -54,54 +73,164 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   return m;
 }
 
-// One CTA per row (grid-stride over rows). The first VPT*256 float4 of the
-// row stay in registers between the max pass and the encode pass; longer
-// rows re-read the remainder (an L2 hit: the row was just streamed).
+template <int VPT>
+__device__ __forceinline__ void load_row(float4 (&v)[VPT], const float4 *xr, int nvec) {
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * kThreads;
+    v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// Persistent CTAs (grid = resident CTAs), grid-stride over rows. The first
+// VPT*256 float4 of a row stay in registers between its max pass and its
+// encode pass, and the next row's loads are issued before the current row
+// is reduced, so HBM reads stay in flight across the block reduction.
+// Longer rows re-read their remainder (an L2 hit). One __syncthreads per
+// row: the reduction slots are double-buffered by row parity.
 template <int VPT>
 __global__ void __launch_bounds__(kThreads) quant_i8_rows_kernel(const float *__restrict__ x,
                                                                  int rows, int cols,
                                                                  float *__restrict__ scales,
                                                                  int8_t *__restrict__ out) {
-  __shared__ float red[kThreads / 32];
-  __shared__ double s_inv;
+  __shared__ float red[2][kThreads / 32];
   const int nvec = cols >> 2;
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int r = blockIdx.x;
+  float4 cur[VPT];
+  if (r < rows) load_row(cur, reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols), nvec);
+  for (int parity = 0; r < rows; r += gridDim.x, parity ^= 1) {
     const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols);
     uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
-    float4 v[VPT];
+    const int rn = r + gridDim.x;
+    float4 nxt[VPT];
+    if (rn < rows)
+      load_row(nxt, reinterpret_cast<const float4 *>(x + static_cast<size_t>(rn) * cols), nvec);
     float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int i = threadIdx.x + j * kThreads;
-      if (i < nvec) {
-        v[j] = __ldcs(xr + i);
-        amax = fmaxf(amax, absmax4(v[j]));
-      }
-    }
+    for (int j = 0; j < VPT; ++j) amax = fmaxf(amax, absmax4(cur[j]));
     for (int i = threadIdx.x + VPT * kThreads; i < nvec; i += kThreads)
       amax = fmaxf(amax, absmax4(__ldg(xr + i)));
-    amax = block_max(amax, red);
-    if (threadIdx.x == 0) {
-      // quant_int8.cpp:82-84: scale and its reciprocal in double.
-      const double a = static_cast<double>(amax);
-      const float s = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
-      scales[r] = s;
-      s_inv = __ddiv_rn(1.0, static_cast<double>(s));
-    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[parity][warp] = amax;
     __syncthreads();
-    const double inv = s_inv;
+    float m = red[parity][0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, red[parity][w]);
+    // quant_int8.cpp:82-84: scale and its reciprocal in double, one lane per warp.
+    float s = 0.0f;
+    double inv = 0.0;
+    if (lane == 0) {
+      const double a = static_cast<double>(m);
+      s = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
+      inv = __ddiv_rn(1.0, static_cast<double>(s));
+    }
+    s = __shfl_sync(0xffffffffu, s, 0);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    if (threadIdx.x == 0) scales[r] = s;
+    const float inv_f = __double2float_rn(inv);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int i = threadIdx.x + j * kThreads;
       if (i < nvec)
-        orow[i] = pack4(code_i8(v[j].x, inv), code_i8(v[j].y, inv), code_i8(v[j].z, inv),
-                        code_i8(v[j].w, inv));
+        orow[i] = pack4(code_i8(cur[j].x, inv, inv_f), code_i8(cur[j].y, inv, inv_f),
+                        code_i8(cur[j].z, inv, inv_f), code_i8(cur[j].w, inv, inv_f));
     }
     for (int i = threadIdx.x + VPT * kThreads; i < nvec; i += kThreads) {
       const float4 t = __ldcs(xr + i);
-      orow[i] = pack4(code_i8(t.x, inv), code_i8(t.y, inv), code_i8(t.z, inv), code_i8(t.w, inv));
+      orow[i] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f),
+                      code_i8(t.w, inv, inv_f));
     }
-    __syncthreads();  // red[] and s_inv are reused by the next row
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
+// Row pipeline through shared memory: thread 0 keeps `stages` rows in
+// flight with cp.async.bulk copies (one mbarrier per slot); all 256
+// threads reduce and encode the oldest row from shared memory, then free
+// its slot for the row `stages` ahead. Persistent CTAs, grid-stride over
+// rows; row bytes (cols * 4) up to the slot size. The time-bounded waits
+// report ROUGE_B200_ETIMEOUT through *err instead of hanging.
+__global__ void __launch_bounds__(kThreads) quant_i8_rows_bulk_kernel(
+    const float *__restrict__ x, int rows, int cols, float *__restrict__ scales,
+    int8_t *__restrict__ out, int stages, int *err) {
+  extern __shared__ __align__(128) uint8_t qsm[];
+  __shared__ float red[2][kThreads / 32];
+  __shared__ __align__(8) uint64_t full[8];
+  const int nvec = cols >> 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const volatile int never = 0;
+  bool aborted = false;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    mbar_init_fence();
+    int r = blockIdx.x;
+    for (int s = 0; s < stages && r < rows; ++s, r += gridDim.x) {
+      mbar_arrive_expect_tx(&full[s], row_bytes);
+      bulk_load(qsm + static_cast<size_t>(s) * row_bytes, x + static_cast<size_t>(r) * cols,
+                row_bytes, &full[s]);
+    }
+  }
+  __syncthreads();
+  int i = 0;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x, ++i) {
+    const int s = i % stages;
+    const uint32_t phase = static_cast<uint32_t>(i / stages) & 1u;
+    const bool ok = mbar_wait(&full[s], phase, &never);
+    const float4 *row = reinterpret_cast<const float4 *>(qsm + static_cast<size_t>(s) * row_bytes);
+    float amax = 0.0f;
+    for (int v = threadIdx.x; v < nvec; v += kThreads) amax = fmaxf(amax, absmax4(row[v]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (lane == 0) red[i & 1][warp] = amax;
+    // One barrier both publishes the partial maxima and makes the timeout
+    // decision collective, so no thread is left waiting at a later barrier.
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0 && err) atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
+      aborted = true;
+      break;
+    }
+    float m = red[i & 1][0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) m = fmaxf(m, red[i & 1][w]);
+    // quant_int8.cpp:82-84: scale and its reciprocal in double, one lane per warp.
+    float sc = 0.0f;
+    double inv = 0.0;
+    if (lane == 0) {
+      const double a = static_cast<double>(m);
+      sc = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
+      inv = __ddiv_rn(1.0, static_cast<double>(sc));
+    }
+    sc = __shfl_sync(0xffffffffu, sc, 0);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    if (threadIdx.x == 0) scales[r] = sc;
+    const float inv_f = __double2float_rn(inv);
+    uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
+    for (int v = threadIdx.x; v < nvec; v += kThreads) {
+      const float4 t = row[v];
+      orow[v] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f),
+                      code_i8(t.w, inv, inv_f));
+    }
+    __syncthreads();  // slot s fully read: refill it with the row `stages` ahead
+    if (threadIdx.x == 0) {
+      const int rn = r + stages * gridDim.x;
+      if (rn < rows) {
+        mbar_arrive_expect_tx(&full[s], row_bytes);
+        bulk_load(qsm + static_cast<size_t>(s) * row_bytes, x + static_cast<size_t>(rn) * cols,
+                  row_bytes, &full[s]);
+      }
+    }
+  }
+  if (aborted && threadIdx.x == 0) {
+    // Let the copies already issued (rows i .. i+stages-1 of this CTA, as
+    // far as they exist) land before the shared memory is released.
+    const int n_cta = (rows - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                      static_cast<int>(gridDim.x);
+    for (int j = i; j < i + stages && j < n_cta; ++j)
+      mbar_wait(&full[j % stages], static_cast<uint32_t>(j / stages) & 1u, &never);
   }
 }
 
@@ -115,6 +244,7 @@ __global__ void __launch_bounds__(kThreads) quant_i8_tensor_kernel(const float *
   const double a = static_cast<double>(__ldg(amax));
   const float s = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
   const double inv = __ddiv_rn(1.0, static_cast<double>(s));
+  const float inv_f = __double2float_rn(inv);
   const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   if (tid == 0 && scale_out) *scale_out = s;
@@ -123,9 +253,9 @@ __global__ void __launch_bounds__(kThreads) quant_i8_tensor_kernel(const float *
   uint32_t *o4 = reinterpret_cast<uint32_t *>(out);
   for (size_t i = tid; i < n4; i += stride) {
     const float4 t = __ldcs(x4 + i);
-    o4[i] = pack4(code_i8(t.x, inv), code_i8(t.y, inv), code_i8(t.z, inv), code_i8(t.w, inv));
+    o4[i] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f), code_i8(t.w, inv, inv_f));
   }
-  for (size_t t = n4 * 4 + tid; t < n; t += stride) out[t] = static_cast<int8_t>(code_i8(x[t], inv));
+  for (size_t t = n4 * 4 + tid; t < n; t += stride) out[t] = static_cast<int8_t>(code_i8(x[t], inv, inv_f));
 }
 
 // out = (float)q * s per element; s = scales[row] or the single `scale`.
@@ -268,15 +398,57 @@ int stream_grid(size_t work_items) {
 
 // Launchers used by the host drop-in layer (no validation beyond what the
 // callers already did).
+// Resident CTAs per SM of a kernel, from the occupancy calculator (cached
+// per kernel; the value is the same on every B200).
+template <class K>
+int resident_ctas(K kernel, int &cache) {
+  if (cache == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, 0) != cudaSuccess) {
+      cudaGetLastError();
+      n = 4;
+    }
+    cache = n > 0 ? n : 1;
+  }
+  return cache * current_sm_count();
+}
+
 int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8_t *out,
                          cudaStream_t st) {
-  const int sms = current_sm_count();
-  const int grid = rows < sms * 8 ? rows : sms * 8;
+  static int occ4 = 0, occ8 = 0;
   const int nvec = cols / 4;
-  if (nvec <= 4 * kThreads)
-    quant_i8_rows_kernel<4><<<grid, kThreads, 0, st>>>(x, rows, cols, scales, out);
-  else
-    quant_i8_rows_kernel<8><<<grid, kThreads, 0, st>>>(x, rows, cols, scales, out);
+  const size_t row_bytes = static_cast<size_t>(cols) * 4;
+  if (row_bytes <= 32768) {
+    // Shared-memory row pipeline: 64 KB of rows in flight per CTA (96 KB
+    // for 32 KB rows), 2-3 CTAs per SM.
+    const int stages =
+        row_bytes <= 16384 ? static_cast<int>(std::min<size_t>(8, 65536 / row_bytes)) : 3;
+    const int smem = static_cast<int>(stages * row_bytes);
+    static std::atomic<unsigned long long> attr_done{0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done.load() & (1ull << (dev & 63)))) {
+      int s = cuda_status(cudaFuncSetAttribute(quant_i8_rows_bulk_kernel,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, 98304));
+      if (s != ROUGE_B200_OK) return s;
+      attr_done.fetch_or(1ull << (dev & 63));
+    }
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, quant_i8_rows_bulk_kernel, kThreads,
+                                                      smem) != cudaSuccess || occ < 1) {
+      cudaGetLastError();
+      occ = 1;
+    }
+    const int cap = occ * current_sm_count();
+    quant_i8_rows_bulk_kernel<<<rows < cap ? rows : cap, kThreads, smem, st>>>(
+        x, rows, cols, scales, out, stages, device_error_word());
+  } else if (nvec <= 4 * kThreads) {
+    const int cap = resident_ctas(quant_i8_rows_kernel<4>, occ4);
+    quant_i8_rows_kernel<4><<<rows < cap ? rows : cap, kThreads, 0, st>>>(x, rows, cols, scales, out);
+  } else {
+    const int cap = resident_ctas(quant_i8_rows_kernel<8>, occ8);
+    quant_i8_rows_kernel<8><<<rows < cap ? rows : cap, kThreads, 0, st>>>(x, rows, cols, scales, out);
+  }
   return cuda_status(cudaGetLastError());
 }
 

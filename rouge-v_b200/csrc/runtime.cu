@@ -128,7 +128,8 @@ int take_device_error(cudaStream_t stream) {
 }
 
 int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, uint64_t inner,
-                 uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer) {
+                 uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle) {
   auto fn = encode_tiled_fn();
   if (!fn) return set_status(ROUGE_B200_ENODEV);
   if ((reinterpret_cast<uintptr_t>(base) & 15u) || (pitch_bytes & 15u))
@@ -138,7 +139,7 @@ int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, uint
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(tm, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? ROUGE_B200_OK : set_status(ROUGE_B200_EUNSUPPORTED);
 }

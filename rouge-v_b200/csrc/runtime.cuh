@@ -33,11 +33,13 @@ int take_device_error(cudaStream_t stream);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
-// 2-D tiled tensor map with 128-byte swizzle, zero fill out of bounds.
+// 2-D tiled tensor map, zero fill out of bounds (128-byte swizzle unless
+// another is given).
 //   inner/outer: tensor extent in elements; pitch_bytes: row pitch;
 //   box_inner/box_outer: box extent in elements.
 int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, uint64_t inner,
-                 uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+                 uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Library-owned resources for the synchronous host-pointer entries: one
 // non-blocking stream and a growable device workspace per device. Callers

@@ -31,4 +31,21 @@ __device__ __forceinline__ float x86_mul(float a, float b) {
   return isnan(p) ? __uint_as_float(0xFFC00000u) : p;
 }
 
+// Two f32 values to packed bf16 (lo in bits 0-15) with the hardware RNE
+// conversion. For every non-NaN input this equals the reference's
+// (bits + 0x7fff + lsb) >> 16 (fp16.cpp:101-112), including subnormals and
+// overflow to infinity; NaN inputs must be mapped to 0x7fc0 by the caller.
+__device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// x86_mul with the NaN handling moved off the common path: one multiply
+// and one NaN test, the full rule only when the product is NaN.
+__device__ __forceinline__ float x86_mul_fast(float a, float b) {
+  const float p = __fmul_rn(a, b);
+  return isnan(p) ? x86_mul(a, b) : p;
+}
+
 }  // namespace rb200

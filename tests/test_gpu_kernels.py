@@ -64,6 +64,28 @@ def test_quantize_i8_rows_special_values(rb, orc, cuda):
     assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
 
 
+def test_quantize_i8_rows_near_ties(rb, orc, cuda):
+    # Values a few ulps around k + 1/2 under several scales: the products the
+    # single-precision fast path must hand to the exact double path.
+    rows = []
+    base = np.arange(-126, 127, dtype=np.float32) + np.float32(0.5)
+    for amax in (127.0, 100.0, 3.0, 1e-3, 12345.678):
+        s = np.float32(np.float64(amax) / 127.0)
+        for d in range(-3, 4):
+            v = (base.astype(np.float64) * float(s)).astype(np.float32)
+            v = (v.view(np.int32) + d).view(np.float32)
+            row = np.concatenate([[np.float32(amax)], v, np.zeros(256 - 1 - v.size, np.float32)])
+            rows.append(row[:256])
+    x = np.stack(rows).astype(np.float32)
+    q = torch.empty(x.shape, dtype=torch.int8, device=cuda)
+    s = torch.empty(x.shape[0], dtype=torch.float32, device=cuda)
+    rb.quantize_i8_rows(dev_tensor(x, cuda), s, q)
+    rb.sync_status()
+    oq, os_ = orc.quantize_i8_rows(x)
+    assert (s.cpu().numpy() == os_).all()
+    assert (q.cpu().numpy() == oq).all()
+
+
 def test_dequantize_i8_rows(rb, orc, cuda):
     rng = np.random.default_rng(1)
     q = rng.integers(-127, 128, (33, 64), dtype=np.int8)
