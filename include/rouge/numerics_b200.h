@@ -36,6 +36,13 @@ extern "C" {
 /* Types shared with the reference                                          */
 /* ------------------------------------------------------------------------ */
 
+/* A translation unit that also includes the reference header
+ * rouge/numerics.h (which defines RougeGemmConfig and declares the drop-in
+ * names) defines ROUGE_B200_WITH_REFERENCE_HEADER before including this
+ * header; the shared type and the drop-in declarations are then taken from
+ * the reference header. */
+#ifndef ROUGE_B200_WITH_REFERENCE_HEADER
+
 /* Replaces RougeGemmConfig, numerics.h:35-41. Accepted and ignored by the
  * GPU entries except as a hint; garbage values never cause out-of-bounds
  * work (the reference normalises them at gemm.cpp:254-275). */
@@ -46,6 +53,8 @@ typedef struct RougeGemmConfig {
   int unroll;
   int split_k;
 } RougeGemmConfig;
+
+#endif /* ROUGE_B200_WITH_REFERENCE_HEADER */
 
 /* ------------------------------------------------------------------------ */
 /* Status codes and library state                                           */
@@ -124,6 +133,16 @@ void rouge_dequantize_i8_tensor(const int8_t *q, int n, float scale, float *out)
 void rouge_dequantize_i8_channel(const int8_t *q, int rows, int cols,
                                  const float *scales, float *out);
 
+/* Replace rouge_quantize_i8_group / rouge_dequantize_i8_group,
+ * numerics.h:148-149,154-156 (quant_int8.cpp:94-142, 162-179): asymmetric
+ * 0..255 codes per group of cols/groups consecutive elements, scale and
+ * zero point per group (scales/zeros[rows*groups]). cols % groups != 0 is
+ * refused as in the reference. */
+int rouge_quantize_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                            uint8_t *zeros, uint8_t *out);
+void rouge_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
+                               const float *scales, const uint8_t *zeros, float *out);
+
 /* Replaces rouge_gemm_i8, numerics.h:160-162 (quant_int8.cpp:189-211).
  * A[M][K] s8, B[K][N] s8 row-major; exact int32 accumulation, then
  * C[m][n] = ((float)acc * sa) * sb. */
@@ -162,6 +181,14 @@ int rouge_b200_quantize_i8_rows(const float *x, int rows, int cols, float *scale
 int rouge_b200_dequantize_i8_rows(const int8_t *q, int rows, int cols,
                                   const float *scales, float scale, float *out,
                                   void *stream);
+
+/* Device-pointer per-group quantization / dequantization (same semantics
+ * as rouge_quantize_i8_group / rouge_dequantize_i8_group). */
+int rouge_b200_quantize_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                                 uint8_t *zeros, uint8_t *out, void *stream);
+int rouge_b200_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
+                                   const float *scales, const uint8_t *zeros, float *out,
+                                   void *stream);
 
 /* Per-tensor absolute maximum of x[n] (f32, device) into *amax (device f32).
  * NaNs are ignored, as std::fabs/operator> ignore them on the host. */

@@ -56,6 +56,8 @@ class Oracle:
             ("or_quantize_i8_rows", _I, [_P, _I, _I, _P, _P]),
             ("or_quantize_i8_tensor", _I, [_P, _I, _P, _P]),
             ("or_dequantize_i8_rows", None, [_P, _I, _I, _P, _P]),
+            ("or_quantize_i8_group", _I, [_P, _I, _I, _I, _P, _P, _P]),
+            ("or_dequantize_i8_group", None, [_P, _I, _I, _I, _P, _P, _P]),
             ("or_gemm_i8_rows", None, [_I, _I, _P, _P, _I, _P, _I, _P, _I, _P, _I, _P, _P]),
             ("or_gemm_f32_rows", None, [_I, _I, _P, _P, _I, _P, _I, _P]),
             ("or_absmax", _F, [_P, _SZ]),
@@ -116,6 +118,23 @@ class Oracle:
         out = np.empty(x.size, np.int8)
         assert self.lib.or_quantize_i8_tensor(_ptr(x), x.size, _ptr(s), _ptr(out)) == 1
         return out, float(s[0])
+
+    def quantize_i8_group(self, x, groups):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = x.shape
+        s = np.empty(rows * groups, np.float32)
+        z = np.empty(rows * groups, np.uint8)
+        q = np.empty((rows, cols), np.uint8)
+        assert self.lib.or_quantize_i8_group(_ptr(x), rows, cols, groups, _ptr(s), _ptr(z), _ptr(q)) == 1
+        return q, s, z
+
+    def dequantize_i8_group(self, q, groups, s, z):
+        q = np.ascontiguousarray(q, dtype=np.uint8)
+        out = np.empty(q.shape, np.float32)
+        self.lib.or_dequantize_i8_group(_ptr(q), q.shape[0], q.shape[1], groups,
+                                        _ptr(np.ascontiguousarray(s, np.float32)),
+                                        _ptr(np.ascontiguousarray(z, np.uint8)), _ptr(out))
+        return out
 
     def dequantize_i8_rows(self, q, scales):
         q = np.ascontiguousarray(q, dtype=np.int8)
@@ -204,6 +223,8 @@ class Reference:
             ("rouge_quantize_i8_tensor", _I, [_P, _I, _P, _P]),
             ("rouge_quantize_i8_channel", _I, [_P, _I, _I, _P, _P]),
             ("rouge_dequantize_i8_channel", None, [_P, _I, _I, _P, _P]),
+            ("rouge_quantize_i8_group", _I, [_P, _I, _I, _I, _P, _P, _P]),
+            ("rouge_dequantize_i8_group", None, [_P, _I, _I, _I, _P, _P, _P]),
             ("rouge_gemm_i8", None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
             ("rouge_gemm_f32", None, [_I, _I, _I, _P, _P, _P, _P]),
             ("rouge_gemm_f16", None, [_I, _I, _I, _P, _P, _P, _P]),
@@ -241,6 +262,24 @@ class Reference:
         q = np.empty(x.size, np.int8)
         assert self.lib.rouge_quantize_i8_tensor(_ptr(x), x.size, _ptr(s), _ptr(q)) == 1
         return q, float(s[0])
+
+    def quantize_i8_group(self, x, groups):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        rows, cols = x.shape
+        s = np.empty(rows * groups, np.float32)
+        z = np.empty(rows * groups, np.uint8)
+        q = np.empty((rows, cols), np.uint8)
+        assert self.lib.rouge_quantize_i8_group(_ptr(x), rows, cols, groups, _ptr(s), _ptr(z),
+                                                _ptr(q)) == 1
+        return q, s, z
+
+    def dequantize_i8_group(self, q, groups, s, z):
+        q = np.ascontiguousarray(q, dtype=np.uint8)
+        out = np.empty(q.shape, np.float32)
+        self.lib.rouge_dequantize_i8_group(_ptr(q), q.shape[0], q.shape[1], groups,
+                                           _ptr(np.ascontiguousarray(s, np.float32)),
+                                           _ptr(np.ascontiguousarray(z, np.uint8)), _ptr(out))
+        return out
 
     def gemm_i8(self, A, B_kn, sa, a_rows, sb, b_cols, threads=1):
         A = np.ascontiguousarray(A, dtype=np.int8)

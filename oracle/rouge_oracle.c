@@ -160,6 +160,65 @@ int or_quantize_i8_tensor(const float *x, int n, float *scale_out, int8_t *out) 
   return 1;
 }
 
+/* Asymmetric per-group: quant_int8.cpp:94-142. */
+static uint8_t clamp_u8(double v) {
+  double r = nearbyint(v);
+  int32_t i = (r != r || r >= 2147483648.0 || r < -2147483648.0) ? INT32_MIN : (int32_t)r;
+  return (uint8_t)(i < 0 ? 0 : (i > 255 ? 255 : i));
+}
+
+int or_quantize_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                         uint8_t *zeros, uint8_t *out) {
+  if (!x || !scales || !zeros || !out || rows <= 0 || cols <= 0 || groups <= 0) return 0;
+  if (cols % groups) return 0;
+  int gsz = cols / groups;
+  for (int r = 0; r < rows; ++r)
+    for (int g = 0; g < groups; ++g) {
+      const float *v = x + (size_t)r * cols + (size_t)g * gsz;
+      double lo = v[0], hi = v[0]; /* :107-113 */
+      for (int i = 1; i < gsz; ++i) {
+        if ((double)v[i] < lo) lo = v[i];
+        if ((double)v[i] > hi) hi = v[i];
+      }
+      float s;
+      uint8_t z;
+      if (lo >= 0.0) { /* :122-131 */
+        z = 0;
+        s = hi > 0.0 ? (float)(hi / 255.0) : 1.0f;
+      } else if (hi <= 0.0) {
+        z = 255;
+        s = lo < 0.0 ? (float)(-lo / 255.0) : 1.0f;
+      } else {
+        s = (float)((hi - lo) / 255.0);
+        z = clamp_u8(-lo / (double)s);
+      }
+      scales[r * groups + g] = s;
+      zeros[r * groups + g] = z;
+      double inv = 1.0 / (double)s; /* :134-138 */
+      for (int i = 0; i < gsz; ++i) {
+        double q = (double)v[i] * inv;
+        q = q + (double)z;
+        out[(size_t)r * cols + (size_t)g * gsz + i] = clamp_u8(q);
+      }
+    }
+  return 1;
+}
+
+/* quant_int8.cpp:162-179 */
+void or_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
+                            const float *scales, const uint8_t *zeros, float *out) {
+  int gsz = cols / groups;
+  for (int r = 0; r < rows; ++r)
+    for (int g = 0; g < groups; ++g) {
+      float s = scales[r * groups + g];
+      double z = zeros[r * groups + g];
+      for (int i = 0; i < gsz; ++i) {
+        size_t k = (size_t)r * cols + (size_t)g * gsz + i;
+        out[k] = (float)(((double)q[k] - z) * (double)s);
+      }
+    }
+}
+
 void or_dequantize_i8_rows(const int8_t *q, int rows, int cols, const float *scales, float *out) {
   for (int r = 0; r < rows; ++r) /* quant_int8.cpp:151-160 */
     for (int c = 0; c < cols; ++c)

@@ -23,6 +23,10 @@ int launch_quant_i8_tensor(const float *x, size_t n, float *amax, float *scale_o
                            cudaStream_t st);
 int launch_dequant_i8(const int8_t *q, int rows, int cols, const float *scales, float scale,
                       float *out, cudaStream_t st);
+int launch_quant_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                          uint8_t *zeros, uint8_t *out, cudaStream_t st);
+int launch_dequant_i8_group(const uint8_t *q, int rows, int cols, int groups, const float *scales,
+                            const uint8_t *zeros, float *out, cudaStream_t st);
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
                    long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
                    int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st);
@@ -176,6 +180,58 @@ int rouge_quantize_i8_tensor(const float *x, int n, float *scale_out, int8_t *ou
       ROUGE_B200_OK)
     return 0;
   return finish(st) == ROUGE_B200_OK ? 1 : 0;
+}
+
+int rouge_quantize_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                            uint8_t *zeros, uint8_t *out) {
+  if (!x || !scales || !zeros || !out || rows <= 0 || cols <= 0 || groups <= 0) return 0;
+  if (cols % groups != 0) return 0;  // quant_int8.cpp:96-98
+  HostCallContext *ctx = host_context();
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t n = static_cast<size_t>(rows) * cols, ng = static_cast<size_t>(rows) * groups;
+  const size_t need = Carve::need(n * 4) + Carve::need(n) + Carve::need(ng * 4) + Carve::need(ng);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return 0;
+  Carve cv(ctx->ws);
+  float *dx = cv.take<float>(n);
+  uint8_t *dq = cv.take<uint8_t>(n);
+  float *ds = cv.take<float>(ng);
+  uint8_t *dz = cv.take<uint8_t>(ng);
+  cudaStream_t st = ctx->stream;
+  if (cuda_status(cudaMemcpyAsync(dx, x, n * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK) return 0;
+  if (launch_quant_i8_group(dx, rows, cols, groups, ds, dz, dq, st) != ROUGE_B200_OK) return 0;
+  if (cuda_status(cudaMemcpyAsync(out, dq, n, cudaMemcpyDeviceToHost, st)) != ROUGE_B200_OK) return 0;
+  if (cuda_status(cudaMemcpyAsync(scales, ds, ng * 4, cudaMemcpyDeviceToHost, st)) != ROUGE_B200_OK)
+    return 0;
+  if (cuda_status(cudaMemcpyAsync(zeros, dz, ng, cudaMemcpyDeviceToHost, st)) != ROUGE_B200_OK)
+    return 0;
+  return finish(st) == ROUGE_B200_OK ? 1 : 0;
+}
+
+void rouge_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
+                               const float *scales, const uint8_t *zeros, float *out) {
+  if (!q || !scales || !zeros || !out || rows <= 0 || cols <= 0 || groups <= 0) return;
+  if (cols % groups != 0) return;  // quant_int8.cpp:165-167
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t n = static_cast<size_t>(rows) * cols, ng = static_cast<size_t>(rows) * groups;
+  const size_t need = Carve::need(n) + Carve::need(n * 4) + Carve::need(ng * 4) + Carve::need(ng);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  Carve cv(ctx->ws);
+  uint8_t *dq = cv.take<uint8_t>(n);
+  float *dout = cv.take<float>(n);
+  float *ds = cv.take<float>(ng);
+  uint8_t *dz = cv.take<uint8_t>(ng);
+  cudaStream_t st = ctx->stream;
+  if (cuda_status(cudaMemcpyAsync(dq, q, n, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK) return;
+  if (cuda_status(cudaMemcpyAsync(ds, scales, ng * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+    return;
+  if (cuda_status(cudaMemcpyAsync(dz, zeros, ng, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK) return;
+  if (launch_dequant_i8_group(dq, rows, cols, groups, ds, dz, dout, st) != ROUGE_B200_OK) return;
+  if (cuda_status(cudaMemcpyAsync(out, dout, n * 4, cudaMemcpyDeviceToHost, st)) != ROUGE_B200_OK)
+    return;
+  finish(st);
 }
 
 void rouge_dequantize_i8_channel(const int8_t *q, int rows, int cols, const float *scales,

@@ -57,6 +57,36 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
 }
 
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+// Single-precision code of one element in the low byte of the returned
+// word. p + 1.5*2^23 rounds p to the nearest even integer q and, for
+// |q| <= 127, has the bit pattern 0x4B400000 + q, whose low byte is q in
+// two's complement; clamping that sum to [magic - 127, magic + 127] is the
+// clamp of quant_int8.cpp:45 and maps a NaN product to -127 as x86 does.
+// `tie` is set when p lies within 2^-12 of a half-integer (see code_i8).
+__device__ __forceinline__ uint32_t code_word(float x, float inv_f, bool &tie) {
+  const float p = __fmul_rn(x, inv_f);
+  const float big = __fadd_rn(p, kRoundMagic);
+  const float r = __fsub_rn(big, kRoundMagic);
+  tie |= fabsf(fabsf(__fsub_rn(p, r)) - 0.5f) < 0.000244140625f;
+  return __float_as_uint(fminf(fmaxf(big, kRoundMagic - 127.0f), kRoundMagic + 127.0f));
+}
+
+// Four codes packed into one word (element 0 in the low byte). Rows whose
+// reciprocal scale is not a finite float (scale below 2^-128 or zero: the
+// products may overflow to +inf, which x86 maps to -127) and elements near
+// a rounding tie take the double-precision path of code_i8_exact.
+__device__ __forceinline__ uint32_t encode4_i8(float4 t, double inv, float inv_f, bool exact_row) {
+  bool tie = exact_row;
+  const uint32_t a = code_word(t.x, inv_f, tie), b = code_word(t.y, inv_f, tie);
+  const uint32_t c = code_word(t.z, inv_f, tie), d = code_word(t.w, inv_f, tie);
+  if (tie)
+    return pack4(code_i8_exact(t.x, inv), code_i8_exact(t.y, inv), code_i8_exact(t.z, inv),
+                 code_i8_exact(t.w, inv));
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 __device__ __forceinline__ float absmax4(float4 v) {
   return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
@@ -130,18 +160,14 @@ __global__ void __launch_bounds__(kThreads) quant_i8_rows_kernel(const float *__
     inv = __shfl_sync(0xffffffffu, inv, 0);
     if (threadIdx.x == 0) scales[r] = s;
     const float inv_f = __double2float_rn(inv);
+    const bool exact_row = isinf(inv_f);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int i = threadIdx.x + j * kThreads;
-      if (i < nvec)
-        orow[i] = pack4(code_i8(cur[j].x, inv, inv_f), code_i8(cur[j].y, inv, inv_f),
-                        code_i8(cur[j].z, inv, inv_f), code_i8(cur[j].w, inv, inv_f));
+      if (i < nvec) orow[i] = encode4_i8(cur[j], inv, inv_f, exact_row);
     }
-    for (int i = threadIdx.x + VPT * kThreads; i < nvec; i += kThreads) {
-      const float4 t = __ldcs(xr + i);
-      orow[i] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f),
-                      code_i8(t.w, inv, inv_f));
-    }
+    for (int i = threadIdx.x + VPT * kThreads; i < nvec; i += kThreads)
+      orow[i] = encode4_i8(__ldcs(xr + i), inv, inv_f, exact_row);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
   }
@@ -208,12 +234,11 @@ __global__ void __launch_bounds__(kThreads) quant_i8_rows_bulk_kernel(
     inv = __shfl_sync(0xffffffffu, inv, 0);
     if (threadIdx.x == 0) scales[r] = sc;
     const float inv_f = __double2float_rn(inv);
+    const bool exact_row = isinf(inv_f);
     uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
-    for (int v = threadIdx.x; v < nvec; v += kThreads) {
-      const float4 t = row[v];
-      orow[v] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f),
-                      code_i8(t.w, inv, inv_f));
-    }
+#pragma unroll 4
+    for (int v = threadIdx.x; v < nvec; v += kThreads)
+      orow[v] = encode4_i8(row[v], inv, inv_f, exact_row);
     __syncthreads();  // slot s fully read: refill it with the row `stages` ahead
     if (threadIdx.x == 0) {
       const int rn = r + stages * gridDim.x;
@@ -251,11 +276,86 @@ __global__ void __launch_bounds__(kThreads) quant_i8_tensor_kernel(const float *
   const size_t n4 = n / 4;
   const float4 *x4 = reinterpret_cast<const float4 *>(x);
   uint32_t *o4 = reinterpret_cast<uint32_t *>(out);
-  for (size_t i = tid; i < n4; i += stride) {
-    const float4 t = __ldcs(x4 + i);
-    o4[i] = pack4(code_i8(t.x, inv, inv_f), code_i8(t.y, inv, inv_f), code_i8(t.z, inv, inv_f), code_i8(t.w, inv, inv_f));
+  const bool exact_row = isinf(inv_f);
+  for (size_t i = tid; i < n4; i += stride) o4[i] = encode4_i8(__ldcs(x4 + i), inv, inv_f, exact_row);
+  for (size_t t = n4 * 4 + tid; t < n; t += stride)
+    out[t] = static_cast<int8_t>(code_i8(x[t], inv, inv_f));
+}
+
+// Asymmetric per-group quantization (quant_int8.cpp:94-142), one warp per
+// group of gsz = cols / groups consecutive elements of a row. In double, as
+// the reference: lo/hi of the group; scale and zero by the three cases of
+// :122-131; code = clamp(rne(x * (1.0/scale) + zero), 0, 255) with the
+// multiply and the add rounded separately (the reference's translation unit
+// is built without FMA instructions).
+__global__ void __launch_bounds__(kThreads) quant_i8_group_kernel(
+    const float *__restrict__ x, int rows, int cols, int groups, float *__restrict__ scales,
+    uint8_t *__restrict__ zeros, uint8_t *__restrict__ out) {
+  const int gsz = cols / groups;
+  const long long total = static_cast<long long>(rows) * groups;
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long g = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5; g < total;
+       g += warps) {
+    const float *src = x + (g / groups) * static_cast<long long>(cols) + (g % groups) * gsz;
+    uint8_t *dst = out + (g / groups) * static_cast<long long>(cols) + (g % groups) * gsz;
+    float lo = src[0], hi = src[0];
+    for (int i = lane; i < gsz; i += 32) {
+      const float v = src[i];
+      lo = v < lo ? v : lo;  // comparisons ignore NaN, as the reference's do
+      hi = v > hi ? v : hi;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float l2 = __shfl_xor_sync(0xffffffffu, lo, o), h2 = __shfl_xor_sync(0xffffffffu, hi, o);
+      lo = l2 < lo ? l2 : lo;
+      hi = h2 > hi ? h2 : hi;
+    }
+    float scale = 1.0f;
+    int zero = 0;
+    double inv = 1.0;
+    if (lane == 0) {
+      const double dlo = lo, dhi = hi;
+      if (dlo >= 0.0) {
+        zero = 0;
+        scale = dhi > 0.0 ? __double2float_rn(__ddiv_rn(dhi, 255.0)) : 1.0f;
+      } else if (dhi <= 0.0) {
+        zero = 255;
+        scale = dlo < 0.0 ? __double2float_rn(__ddiv_rn(-dlo, 255.0)) : 1.0f;
+      } else {
+        scale = __double2float_rn(__ddiv_rn(__dsub_rn(dhi, dlo), 255.0));
+        const double z = __ddiv_rn(-dlo, static_cast<double>(scale));
+        int zi = (z >= -2147483648.5 && z < 2147483647.5) ? __double2int_rn(z) : INT_MIN;
+        zero = zi < 0 ? 0 : (zi > 255 ? 255 : zi);
+      }
+      inv = __ddiv_rn(1.0, static_cast<double>(scale));
+      scales[g] = scale;
+      zeros[g] = static_cast<uint8_t>(zero);
+    }
+    zero = __shfl_sync(0xffffffffu, zero, 0);
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    const double dz = static_cast<double>(zero);
+    for (int i = lane; i < gsz; i += 32) {
+      const double q = __dadd_rn(__dmul_rn(static_cast<double>(src[i]), inv), dz);
+      int qi = (q >= -2147483648.5 && q < 2147483647.5) ? __double2int_rn(q) : INT_MIN;
+      dst[i] = static_cast<uint8_t>(qi < 0 ? 0 : (qi > 255 ? 255 : qi));
+    }
   }
-  for (size_t t = n4 * 4 + tid; t < n; t += stride) out[t] = static_cast<int8_t>(code_i8(x[t], inv, inv_f));
+}
+
+// out = (float)(((double)q - zero) * (double)scale)  (quant_int8.cpp:162-179)
+__global__ void __launch_bounds__(kThreads) dequant_i8_group_kernel(
+    const uint8_t *__restrict__ q, int rows, int cols, int groups, const float *__restrict__ scales,
+    const uint8_t *__restrict__ zeros, float *__restrict__ out) {
+  const int gsz = cols / groups;
+  const long long n = static_cast<long long>(rows) * cols;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const long long g = (i / cols) * groups + (i % cols) / gsz;
+    const double v = __dmul_rn(__dsub_rn(static_cast<double>(q[i]), static_cast<double>(zeros[g])),
+                               static_cast<double>(scales[g]));
+    out[i] = __double2float_rn(v);
+  }
 }
 
 // out = (float)q * s per element; s = scales[row] or the single `scale`.
@@ -462,6 +562,21 @@ int launch_quant_i8_tensor(const float *x, size_t n, float *amax, float *scale_o
   return cuda_status(cudaGetLastError());
 }
 
+int launch_quant_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                          uint8_t *zeros, uint8_t *out, cudaStream_t st) {
+  const long long total = static_cast<long long>(rows) * groups;
+  quant_i8_group_kernel<<<stream_grid(static_cast<size_t>(total) * 32), kThreads, 0, st>>>(
+      x, rows, cols, groups, scales, zeros, out);
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_dequant_i8_group(const uint8_t *q, int rows, int cols, int groups, const float *scales,
+                            const uint8_t *zeros, float *out, cudaStream_t st) {
+  dequant_i8_group_kernel<<<stream_grid(static_cast<size_t>(rows) * cols), kThreads, 0, st>>>(
+      q, rows, cols, groups, scales, zeros, out);
+  return cuda_status(cudaGetLastError());
+}
+
 int launch_dequant_i8(const int8_t *q, int rows, int cols, const float *scales, float scale,
                       float *out, cudaStream_t st) {
   const size_t n4 = static_cast<size_t>(rows) * cols / 4;
@@ -509,6 +624,27 @@ int rouge_b200_quantize_i8_rows(const float *x, int rows, int cols, float *scale
   int s = device_ready();
   if (s != ROUGE_B200_OK) return s;
   return launch_quant_i8_rows(x, rows, cols, scales, out, as_stream(stream));
+}
+
+int rouge_b200_quantize_i8_group(const float *x, int rows, int cols, int groups, float *scales,
+                                 uint8_t *zeros, uint8_t *out, void *stream) {
+  if (!x || !scales || !zeros || !out || rows <= 0 || cols <= 0 || groups <= 0 ||
+      cols % groups != 0)
+    return set_status(ROUGE_B200_EINVAL);
+  int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_quant_i8_group(x, rows, cols, groups, scales, zeros, out, as_stream(stream));
+}
+
+int rouge_b200_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
+                                   const float *scales, const uint8_t *zeros, float *out,
+                                   void *stream) {
+  if (!q || !scales || !zeros || !out || rows <= 0 || cols <= 0 || groups <= 0 ||
+      cols % groups != 0)
+    return set_status(ROUGE_B200_EINVAL);
+  int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_dequant_i8_group(q, rows, cols, groups, scales, zeros, out, as_stream(stream));
 }
 
 int rouge_b200_dequantize_i8_rows(const int8_t *q, int rows, int cols, const float *scales,

@@ -71,6 +71,10 @@ _SIGS = {
     "rouge_quantize_i8_channel": (_I, [_P, _I, _I, _P, _P]),
     "rouge_dequantize_i8_tensor": (None, [_P, _I, _F, _P]),
     "rouge_dequantize_i8_channel": (None, [_P, _I, _I, _P, _P]),
+    "rouge_quantize_i8_group": (_I, [_P, _I, _I, _I, _P, _P, _P]),
+    "rouge_dequantize_i8_group": (None, [_P, _I, _I, _I, _P, _P, _P]),
+    "rouge_b200_quantize_i8_group": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
+    "rouge_b200_dequantize_i8_group": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_i8": (None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
     "rouge_gemm_e4m3": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_f16": (None, [_I, _I, _I, _P, _P, _P, _P]),
@@ -146,6 +150,16 @@ def quantize_i8_rows(x, scales, out):
 def dequantize_i8_rows(q, scales, out, scale=0.0):
     _check("rouge_b200_dequantize_i8_rows", lib().rouge_b200_dequantize_i8_rows(
         _dp(q), q.shape[0], q.shape[1], _dp(scales), scale, _dp(out), _stream()))
+
+
+def quantize_i8_group(x, groups, scales, zeros, out):
+    _check("rouge_b200_quantize_i8_group", lib().rouge_b200_quantize_i8_group(
+        _dp(x), x.shape[0], x.shape[1], groups, _dp(scales), _dp(zeros), _dp(out), _stream()))
+
+
+def dequantize_i8_group(q, groups, scales, zeros, out):
+    _check("rouge_b200_dequantize_i8_group", lib().rouge_b200_dequantize_i8_group(
+        _dp(q), q.shape[0], q.shape[1], groups, _dp(scales), _dp(zeros), _dp(out), _stream()))
 
 
 def absmax(x, amax):
@@ -235,6 +249,30 @@ def host_quantize_i8_tensor(x: np.ndarray):
         _last_error("rouge_quantize_i8_tensor")
         raise RougeB200Error("rouge_quantize_i8_tensor", EINVAL, "returned 0")
     return q, float(s[0])
+
+
+def host_quantize_i8_group(x: np.ndarray, groups: int):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    s = np.empty(rows * groups, np.float32)
+    z = np.empty(rows * groups, np.uint8)
+    q = np.empty((rows, cols), np.uint8)
+    lib().rouge_b200_clear_error()
+    if lib().rouge_quantize_i8_group(_hp(x), rows, cols, groups, _hp(s), _hp(z), _hp(q)) != 1:
+        _last_error("rouge_quantize_i8_group")
+        raise RougeB200Error("rouge_quantize_i8_group", EINVAL, "returned 0")
+    return q, s, z
+
+
+def host_dequantize_i8_group(q: np.ndarray, groups: int, s: np.ndarray, z: np.ndarray):
+    q = np.ascontiguousarray(q, np.uint8)
+    s = np.ascontiguousarray(s, np.float32)
+    z = np.ascontiguousarray(z, np.uint8)
+    out = np.empty(q.shape, np.float32)
+    lib().rouge_b200_clear_error()
+    lib().rouge_dequantize_i8_group(_hp(q), q.shape[0], q.shape[1], groups, _hp(s), _hp(z), _hp(out))
+    _last_error("rouge_dequantize_i8_group")
+    return out
 
 
 def host_dequantize_i8_channel(q: np.ndarray, scales: np.ndarray):

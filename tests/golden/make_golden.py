@@ -84,6 +84,18 @@ def main() -> None:
     qt, st = R.quantize_i8_tensor(X[:20])
     out["q8t_codes"], out["q8t_scale"] = qt, np.float32(st)
 
+    # --- asymmetric per-group (quant_int8.cpp:94-142, 162-179) ---
+    G = rng.standard_normal((12, 64)).astype(np.float32)
+    G[0] = np.abs(G[0])            # all >= 0: zero point 0
+    G[1] = -np.abs(G[1])           # all <= 0: zero point 255
+    G[2] = 0.0                     # constant zero group: scale 1
+    G[3, :16] = 2.0                # constant positive group
+    G[4, 5] = np.nan
+    out["qg_x"] = G
+    qg, sg, zg = R.quantize_i8_group(G, 4)
+    out["qg_codes"], out["qg_scales"], out["qg_zeros"] = qg, sg, zg
+    out["qg_back"] = R.dequantize_i8_group(qg, 4, sg, zg)
+
     # --- exact int8 GEMM (quant_int8.cpp:189-211) ---
     for tag, (M, N, K) in {"a": (7, 5, 11), "b": (33, 48, 40), "c": (130, 96, 64)}.items():
         A = rng.integers(-127, 128, (M, K), dtype=np.int8)

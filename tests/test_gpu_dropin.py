@@ -22,6 +22,18 @@ def test_quantize_i8_tensor_golden(rb, cuda, golden):
     assert np.float32(s) == golden["q8t_scale"]
 
 
+def test_quantize_i8_group_golden(rb, cuda, golden):
+    q, s, z = rb.host_quantize_i8_group(golden["qg_x"], 4)
+    assert (q == golden["qg_codes"]).all()
+    assert (s.view(np.uint32) == golden["qg_scales"].view(np.uint32)).all()
+    assert (z == golden["qg_zeros"]).all()
+    back = rb.host_dequantize_i8_group(q, 4, s, z)
+    assert (back.view(np.uint32) == golden["qg_back"].view(np.uint32)).all()
+    # cols % groups != 0 is refused (quant_int8.cpp:98)
+    with pytest.raises(rb.RougeB200Error):
+        rb.host_quantize_i8_group(golden["qg_x"][:, :63], 4)
+
+
 def test_quantize_i8_odd_columns(rb, orc, cuda):
     rng = np.random.default_rng(4)
     for shape in ((5, 3), (9, 41), (2, 1)):

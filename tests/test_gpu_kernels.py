@@ -86,6 +86,39 @@ def test_quantize_i8_rows_near_ties(rb, orc, cuda):
     assert (q.cpu().numpy() == oq).all()
 
 
+@pytest.mark.parametrize("shape,groups", [((1, 4), 1), ((33, 96), 8), ((5, 7), 7), ((512, 4096), 32)])
+def test_quantize_i8_group(rb, orc, cuda, shape, groups):
+    rng = np.random.default_rng(shape[0] + groups)
+    x = (rng.standard_normal(shape) * 3).astype(np.float32)
+    x[0] = np.abs(x[0])
+    rows, cols = shape
+    q = torch.empty(shape, dtype=torch.uint8, device=cuda)
+    s = torch.empty(rows * groups, dtype=torch.float32, device=cuda)
+    z = torch.empty(rows * groups, dtype=torch.uint8, device=cuda)
+    rb.quantize_i8_group(dev_tensor(x, cuda), groups, s, z, q)
+    back = torch.empty(shape, dtype=torch.float32, device=cuda)
+    rb.dequantize_i8_group(q, groups, s, z, back)
+    rb.sync_status()
+    oq, os_, oz = orc.quantize_i8_group(x, groups)
+    assert (q.cpu().numpy() == oq).all()
+    assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
+    assert (z.cpu().numpy() == oz).all()
+    ob = orc.dequantize_i8_group(oq, groups, os_, oz)
+    assert (back.cpu().numpy().view(np.uint32) == ob.view(np.uint32)).all()
+
+
+def test_quantize_i8_group_golden(rb, cuda, golden):
+    x = golden["qg_x"]
+    q = torch.empty(x.shape, dtype=torch.uint8, device=cuda)
+    s = torch.empty(x.shape[0] * 4, dtype=torch.float32, device=cuda)
+    z = torch.empty(x.shape[0] * 4, dtype=torch.uint8, device=cuda)
+    rb.quantize_i8_group(dev_tensor(x, cuda), 4, s, z, q)
+    rb.sync_status()
+    assert (q.cpu().numpy() == golden["qg_codes"]).all()
+    assert (s.cpu().numpy().view(np.uint32) == golden["qg_scales"].view(np.uint32)).all()
+    assert (z.cpu().numpy() == golden["qg_zeros"]).all()
+
+
 def test_dequantize_i8_rows(rb, orc, cuda):
     rng = np.random.default_rng(1)
     q = rng.integers(-127, 128, (33, 64), dtype=np.int8)

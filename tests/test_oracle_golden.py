@@ -96,6 +96,25 @@ def test_int8_rows_match_golden(orc, golden):
     assert np.float32(st) == golden["q8t_scale"]
 
 
+def test_int8_group_matches_golden(orc, golden):
+    q, s, z = orc.quantize_i8_group(golden["qg_x"], 4)
+    assert (q == golden["qg_codes"]).all()
+    assert (s.view(np.uint32) == golden["qg_scales"].view(np.uint32)).all()
+    assert (z == golden["qg_zeros"]).all()
+    back = orc.dequantize_i8_group(q, 4, s, z)
+    assert (back.view(np.uint32) == golden["qg_back"].view(np.uint32)).all()
+
+
+def test_int8_group_one_step_bound(orc):
+    # tests/test_ai.cpp:130-160: error within one step of the stored scale
+    rng = np.random.default_rng(0xA1)
+    x = rng.uniform(-2, 2, (4, 64)).astype(np.float32)
+    q, s, z = orc.quantize_i8_group(x, 8)
+    back = orc.dequantize_i8_group(q, 8, s, z)
+    step = np.repeat(s.reshape(4, 8), 8, axis=1).astype(np.float64)
+    assert (np.abs(x - back) <= step * (1.0 + 1e-5) + 1e-6).all()
+
+
 def test_int8_rows_half_step_bound(orc):
     # tests/test_ai.cpp:100-123
     rng = np.random.default_rng(0xA1)

@@ -34,6 +34,19 @@ def test_quantize_rows_vs_reference(orc, ref, shape):
     assert (q3 == q2).all() and (s3 == s2).all()
 
 
+@pytest.mark.parametrize("shape,groups", [((1, 4), 1), ((33, 96), 8), ((5, 7), 7), ((128, 4096), 32)])
+def test_quantize_group_vs_reference(orc, ref, shape, groups):
+    rng = np.random.default_rng(shape[1] + groups)
+    x = (rng.standard_normal(shape) * 3).astype(np.float32)
+    x[0, 0] = abs(x[0, 0]) + 5.0
+    mine = orc.quantize_i8_group(x, groups)
+    theirs = ref.quantize_i8_group(x, groups)
+    for a, b in zip(mine, theirs):
+        assert (a.view(np.uint8) == b.view(np.uint8)).all()
+    assert (orc.dequantize_i8_group(*mine[:1], groups, mine[1], mine[2]).view(np.uint32)
+            == ref.dequantize_i8_group(theirs[0], groups, theirs[1], theirs[2]).view(np.uint32)).all()
+
+
 def test_gemm_i8_vs_reference(orc, ref):
     rng = np.random.default_rng(3)
     M, N, K = 97, 80, 300
