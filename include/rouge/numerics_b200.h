@@ -242,6 +242,19 @@ int rouge_b200_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *
                         int b_layout, int is_bf16, void *C, int ldc, int out_type,
                         void *stream);
 
+/* Implicit-GEMM 2-D convolution on tcgen05 (kind::f16), the B200 form of
+ * rouge_conv2d_f32 / rouge_conv_implicit_f32 (numerics.h:76-79,106-109;
+ * conv.cpp:26-66): cross-correlation with symmetric stride and zero
+ * padding, OH = (H + 2*pad - KH)/stride + 1, then + bias[co].
+ *   X  [N][H][W][Cin]      f16 (is_bf16 = 0) or bf16 codes, NHWC
+ *   Wt [Cout][KH][KW][Cin] same type
+ *   bias [Cout] f32 or NULL; Y [N][OH][OW][Cout] f32, f32 accumulation.
+ * Requires Cin % 64 == 0, Cout % 4 == 0, 16-byte aligned X / Wt, an input
+ * of at least 128 KB, KH, KW <= 256, pad <= 128, stride <= 8. */
+int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW,
+                               int stride, int pad, const uint16_t *X, const uint16_t *Wt,
+                               const float *bias, float *Y, int is_bf16, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Seeded synthetic inputs (host, multi-threaded)                           */
 /* ------------------------------------------------------------------------ */

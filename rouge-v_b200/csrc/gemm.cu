@@ -48,6 +48,12 @@ struct GemmArgs {
   int bf16;               // kind::f16 inputs are bf16
   int use_tma_store;      // C and ldc are 16-byte aligned: epilogue stores through TMA
   int *err;
+  // Implicit-GEMM convolution (A gathered by im2col TMA): M = N*OH*OW
+  // output pixels, K = KH*KW*Cin ordered (kr, kc, c), k-block = one filter
+  // tap x 64 channels.
+  const float *bias;      // per output channel (column) bias added in the epilogue, or null
+  int conv_cblocks;       // Cin / 64
+  int conv_kw, conv_oh, conv_ow, conv_stride, conv_pad, conv_cin;
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
@@ -134,6 +140,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
           f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
         }
       }
+    } else if (args.bias) {
+      // conv.cpp:61-64: bias added to the finished f32 sum of each channel
+      const int col = col0 + lane;
+      const float bl = col < args.N ? __ldg(args.bias + col) : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        f[j] = __fadd_rn(__uint_as_float(v[j]), __shfl_sync(0xffffffffu, bl, j));
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__uint_as_float(v[j]), sab);
@@ -198,7 +211,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 }
 
-template <MmaKind KIND, int BN, bool B_MN, int OUT>
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
@@ -250,6 +263,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, args.num_m, args.num_n, mb, nb);
+      // Convolution: box position of the tile's first output pixel.
+      int cw = 0, ch = 0, cn = 0;
+      if constexpr (CONV) {
+        const int p0 = mb * kBM, ohw = args.conv_oh * args.conv_ow;
+        cn = p0 / ohw;
+        const int rem = p0 - cn * ohw;
+        ch = (rem / args.conv_ow) * args.conv_stride - args.conv_pad;
+        cw = (rem % args.conv_ow) * args.conv_stride - args.conv_pad;
+      }
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % C::STAGES;
         const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
@@ -259,9 +281,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
-        tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kb * C::BK, mb * kBM);
+        int kx = kb * C::BK;  // K coordinate of the B tile
+        if constexpr (CONV) {
+          const int tap = kb / args.conv_cblocks;
+          const int c0 = (kb - tap * args.conv_cblocks) * C::BK;
+          const int kr = tap / args.conv_kw, kc = tap - kr * args.conv_kw;
+          tma_load_im2col_4d(sA + s * C::A_BYTES, &tmA, &full[s], c0, cw, ch, cn,
+                             static_cast<uint16_t>(kc), static_cast<uint16_t>(kr));
+          kx = tap * args.conv_cin + c0;
+        } else {
+          tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kx, mb * kBM);
+        }
         if constexpr (!B_MN) {
-          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kb * C::BK, nb * BN);
+          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kx, nb * BN);
         } else {
 #pragma unroll
           for (int j = 0; j < C::B_CHUNKS; ++j)
@@ -398,6 +430,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// Builds the output map and launches one GEMM / convolution.
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV>
+int launch_tiles(const CUtensorMap &ta, const CUtensorMap &tb, GemmArgs args, cudaStream_t st) {
+  using C = Cfg<KIND, BN, B_MN>;
+  int s = ROUGE_B200_OK;
+  // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
+  // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  if (args.use_tma_store) {
+    const bool b16 = OUT == ROUGE_B200_OUT_BF16;
+    s = make_tmap_2d(&tc, args.C,
+                     b16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, args.N,
+                     args.M, static_cast<uint64_t>(args.ldc) * (b16 ? 2 : 4), 32, 32,
+                     b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (s != ROUGE_B200_OK) return s;
+  }
+
+  auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT, CONV>;
+  // The shared-memory opt-in is a per-device function attribute.
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load() & bit)) {
+    s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    if (s != ROUGE_B200_OK) return s;
+    attr_done.fetch_or(bit);
+  }
+  const int sms = current_sm_count();
+  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
+  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
+  return cuda_status(cudaGetLastError());
+}
+
 template <MmaKind KIND, int BN, bool B_MN, int OUT>
 int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
                      cudaStream_t st) {
@@ -414,34 +481,7 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
     s = make_tmap_2d(&tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
                      kBKBytes / C::ESIZE, C::BK);
   if (s != ROUGE_B200_OK) return s;
-  // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
-  // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
-  CUtensorMap tc;
-  std::memset(&tc, 0, sizeof(tc));
-  if (args.use_tma_store) {
-    const bool b16 = OUT == ROUGE_B200_OUT_BF16;
-    s = make_tmap_2d(&tc, args.C,
-                     b16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, args.N,
-                     args.M, static_cast<uint64_t>(args.ldc) * (b16 ? 2 : 4), 32, 32,
-                     b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
-    if (s != ROUGE_B200_OK) return s;
-  }
-
-  auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT>;
-  // The shared-memory opt-in is a per-device function attribute.
-  static std::atomic<unsigned long long> attr_done{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(attr_done.load() & bit)) {
-    s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    if (s != ROUGE_B200_OK) return s;
-    attr_done.fetch_or(bit);
-  }
-  const int sms = current_sm_count();
-  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
-  return cuda_status(cudaGetLastError());
+  return launch_tiles<KIND, BN, B_MN, OUT, false>(ta, tb, args, st);
 }
 
 template <MmaKind KIND, int BN, bool B_MN>
@@ -510,7 +550,57 @@ int vec_ok(const void *Cp, long long ldc, int out_type) {
              : 0;
 }
 
+template <int BN>
+int launch_conv_bn(const CUtensorMap &ta, const uint16_t *Wt, GemmArgs g, cudaStream_t st) {
+  CUtensorMap tb;
+  int s = make_tmap_2d(&tb, Wt, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.K, g.N,
+                       static_cast<uint64_t>(g.K) * 2, 64, BN);
+  if (s != ROUGE_B200_OK) return s;
+  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true>(ta, tb, g, st);
+}
+
 }  // namespace
+
+// Implicit-GEMM convolution, NHWC f16/bf16 in, f32 NHWC out (+ bias).
+// GEMM view: M = N*OH*OW output pixels, N = Cout, K = KH*KW*Cin in
+// (kr, kc, c) order, so the weights [Cout][KH][KW][Cin] are the K-major B
+// operand as stored. The A tile of k-block (tap, c0) is one im2col TMA load:
+// 128 consecutive output pixels (crossing rows and images) x 64 channels of
+// filter tap (kr, kc), zeros in the padding.
+int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
+                    const uint16_t *X, const uint16_t *Wt, const float *bias, float *Y,
+                    int is_bf16, cudaStream_t st) {
+  const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
+  GemmArgs g{};
+  g.M = N * OH * OW;
+  g.N = Cout;
+  g.K = KH * KW * Cin;
+  g.C = Y;
+  g.ldc = Cout;
+  g.bf16 = is_bf16 ? 1 : 0;
+  g.bias = bias;
+  g.use_tma_store = vec_ok(Y, Cout, ROUGE_B200_OUT_F32);
+  g.err = device_error_word();
+  g.conv_cblocks = Cin / 64;
+  g.conv_kw = KW;
+  g.conv_oh = OH;
+  g.conv_ow = OW;
+  g.conv_stride = stride;
+  g.conv_pad = pad;
+  g.conv_cin = Cin;
+  CUtensorMap ta;
+  int s = make_tmap_im2col_nhwc(&ta, X, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, N, H, W, Cin, -pad, -pad,
+                                pad - (KW - 1), pad - (KH - 1), 64, kBM, stride, stride);
+  if (s != ROUGE_B200_OK) return s;
+  const int sms = current_sm_count();
+  const long long tiles256 = static_cast<long long>((g.M + kBM - 1) / kBM) * ((Cout + 255) / 256);
+  const int bn = (Cout > 128 && tiles256 >= sms) ? 256 : 128;
+  g.num_m = (g.M + kBM - 1) / kBM;
+  g.num_n = (Cout + bn - 1) / bn;
+  g.num_k = KH * KW * g.conv_cblocks;
+  g.num_tiles = g.num_m * g.num_n;
+  return bn == 256 ? launch_conv_bn<256>(ta, Wt, g, st) : launch_conv_bn<128>(ta, Wt, g, st);
+}
 
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
                    long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
@@ -578,6 +668,29 @@ int rouge_b200_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B
   const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
   return launch_gemm_e4m3(M, N, K, A, K, B, ldb, b_layout, scale_a, scale_b, C, ldc, out_type,
                           as_stream(stream));
+}
+
+int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride,
+                               int pad, const uint16_t *X, const uint16_t *Wt, const float *bias,
+                               float *Y, int is_bf16, void *stream) {
+  if (!X || !Wt || !Y || N <= 0 || H <= 0 || W <= 0 || Cin <= 0 || Cout <= 0 || KH <= 0 ||
+      KW <= 0 || stride <= 0 || pad < 0)
+    return set_status(ROUGE_B200_EINVAL);
+  const long long OH = (static_cast<long long>(H) + 2 * pad - KH) / stride + 1;
+  const long long OW = (static_cast<long long>(W) + 2 * pad - KW) / stride + 1;
+  if (OH <= 0 || OW <= 0) return set_status(ROUGE_B200_EINVAL);  // conv.cpp:249
+  // im2col TMA limits: 64-channel boxes, corners in [-128, 127], filter
+  // offsets below 256, traversal stride up to 8; inputs of at least 128 KB.
+  const long long xbytes = static_cast<long long>(N) * H * W * Cin * 2;
+  if (Cin % 64 || Cout % 4 || pad > 128 || pad - (KW - 1) < -128 || pad - (KH - 1) < -128 ||
+      KH > 256 || KW > 256 || stride > 8 || xbytes < 131072 ||
+      static_cast<long long>(N) * OH * OW > 0x7fffffffLL ||
+      (reinterpret_cast<uintptr_t>(X) & 15u) || (reinterpret_cast<uintptr_t>(Wt) & 15u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_conv_f16(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, bias, Y, is_bf16,
+                         as_stream(stream));
 }
 
 int rouge_b200_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B, int b_layout,

@@ -92,6 +92,20 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *tm, ui
       : "memory");
 }
 
+// 4-D im2col-mode load (NHWC activations): `pixelsPerColumn` output pixels
+// starting at box position (w, h, n), channels [c, c + channelsPerPixel),
+// each pixel displaced by the filter tap (off_w, off_h). Padding reads as 0.
+__device__ __forceinline__ void tma_load_im2col_4d(void *dst, const CUtensorMap *tm,
+                                                   uint64_t *bar, int32_t c, int32_t w, int32_t h,
+                                                   int32_t n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n),
+      "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 // Contiguous bulk copy global -> shared (both 16-byte aligned, bytes a
 // multiple of 16), completing `bytes` of transaction count on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,

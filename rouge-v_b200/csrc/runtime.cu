@@ -52,7 +52,42 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_tiled_fn() {
   return fn;
 }
 
+PFN_cuTensorMapEncodeIm2col_v12000 encode_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      p = nullptr;
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  }();
+  return fn;
+}
+
 }  // namespace
+
+int make_tmap_im2col_nhwc(CUtensorMap *tm, const void *x, CUtensorMapDataType dt, int esize, int n,
+                          int h, int w, int c, int lower_w, int lower_h, int upper_w, int upper_h,
+                          int channels, int pixels, int stride_w, int stride_h) {
+  auto fn = encode_im2col_fn();
+  if (!fn) return set_status(ROUGE_B200_ENODEV);
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return set_status(ROUGE_B200_EUNSUPPORTED);
+  const cuuint64_t cb = static_cast<cuuint64_t>(c) * esize;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(c), static_cast<cuuint64_t>(w),
+                        static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(n)};
+  cuuint64_t strides[3] = {cb, cb * w, cb * w * h};
+  int lower[2] = {lower_w, lower_h};
+  int upper[2] = {upper_w, upper_h};
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(stride_w), static_cast<cuuint32_t>(stride_h), 1};
+  CUresult r = fn(tm, dt, 4, const_cast<void *>(x), dims, strides, lower, upper,
+                  static_cast<cuuint32_t>(channels), static_cast<cuuint32_t>(pixels), estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? ROUGE_B200_OK : set_status(ROUGE_B200_EUNSUPPORTED);
+}
 
 int set_status(int status) {
   if (status != ROUGE_B200_OK) g_last_error = status;

@@ -41,6 +41,14 @@ int make_tmap_2d(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, uint
                  uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
 
+// 4-D im2col tensor map over NHWC activations x[n][h][w][c] (128-byte
+// swizzle, zero fill): boxes of `pixels` output pixels x `channels`
+// channels; lower/upper corners and traversal strides as for
+// cuTensorMapEncodeIm2col.
+int make_tmap_im2col_nhwc(CUtensorMap *tm, const void *x, CUtensorMapDataType dt, int esize, int n,
+                          int h, int w, int c, int lower_w, int lower_h, int upper_w, int upper_h,
+                          int channels, int pixels, int stride_w, int stride_h);
+
 // Library-owned resources for the synchronous host-pointer entries: one
 // non-blocking stream and a growable device workspace per device. Callers
 // hold `lock` for the whole call.

@@ -90,6 +90,7 @@ _SIGS = {
     "rouge_b200_gemm_i8": (_I, [_I, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P]),
     "rouge_b200_gemm_e4m3": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P, _I, _I, _P]),
     "rouge_b200_gemm_f16": (_I, [_I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P]),
+    "rouge_b200_conv2d_nhwc_f16": (_I, [_I] * 9 + [_P, _P, _P, _P, _I, _P]),
     "rouge_b200_synth_uniform": (_I, [_U64, _SZ, _F, _F, _P]),
     "rouge_b200_synth_normal": (_I, [_U64, _SZ, _F, _F, _P]),
     "rouge_b200_synth_outliers": (C.c_longlong, [_U64, _SZ, _F, _F, _P]),
@@ -213,6 +214,15 @@ def gemm_f16(A, B, b_layout, C_, out_type, is_bf16=False):
     _check("rouge_b200_gemm_f16", lib().rouge_b200_gemm_f16(
         M, N, K, _dp(A), _dp(B), b_layout, int(is_bf16), _dp(C_), C_.stride(0), out_type,
         _stream()))
+
+
+def conv2d_nhwc_f16(X, Wt, bias, Y, stride, pad, is_bf16=False):
+    """X[N][H][W][Cin], Wt[Cout][KH][KW][Cin] (16-bit codes), Y[N][OH][OW][Cout] f32."""
+    N, H, W, Cin = X.shape
+    Cout, KH, KW, _ = Wt.shape
+    _check("rouge_b200_conv2d_nhwc_f16", lib().rouge_b200_conv2d_nhwc_f16(
+        N, H, W, Cin, Cout, KH, KW, stride, pad, _dp(X), _dp(Wt), _dp(bias), _dp(Y),
+        int(is_bf16), _stream()))
 
 
 def sync_status():
