@@ -86,6 +86,11 @@ RougeGemmConfig rouge_gemm_default_config(void);
  * present, else 0. */
 int rouge_b200_device_ok(void);
 
+/* Caps the SMs the persistent kernels size their grids for (0 = all).
+ * Leaving SMs free lets communication kernels on another stream overlap
+ * (used by the sharded GEMM). Process-wide; returns the previous value. */
+int rouge_b200_set_sm_budget(int sms);
+
 /* Synchronises `stream`, then reads and clears the current device's error
  * word, which kernels set when a bounded device-side wait runs out.
  * Returns ROUGE_B200_OK or the failure (e.g. ROUGE_B200_ETIMEOUT). */
@@ -255,6 +260,15 @@ int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, i
                                int stride, int pad, const uint16_t *X, const uint16_t *Wt,
                                const float *bias, float *Y, int is_bf16, void *stream);
 
+/* N-sharded GEMM, layout step after the all-gather:
+ * rank r of g owns output columns [r*ns, (r+1)*ns); shards gathered in
+ * bands of R rows arrive as src[M/R][g][R][ns]; this writes them to
+ * dst[M][ldd] row-major (columns >= N dropped). esize = 1, 2 or 4 bytes;
+ * ns, N, ldd multiples of 16/esize; M % R == 0; 16-byte aligned buffers.
+ * No reference counterpart: the reference has no multi-GPU code. */
+int rouge_b200_unshard_columns(const void *src, void *dst, int M, int N, int g, int ns, int R,
+                               int ldd, int esize, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Seeded synthetic inputs (host, multi-threaded)                           */
 /* ------------------------------------------------------------------------ */
@@ -264,6 +278,12 @@ int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, i
 int rouge_b200_synth_uniform(uint64_t seed, size_t n, float lo, float hi, float *out);
 int rouge_b200_synth_normal(uint64_t seed, size_t n, float mean, float stddev, float *out);
 long long rouge_b200_synth_outliers(uint64_t seed, size_t n, float frac, float mult, float *x);
+/* The same streams from element `offset` on (offset even for _normal), so
+ * a rank can generate only its own shard of a tensor. */
+int rouge_b200_synth_normal_at(uint64_t seed, size_t offset, size_t n, float mean, float stddev,
+                               float *out);
+long long rouge_b200_synth_outliers_at(uint64_t seed, size_t offset, size_t n, float frac,
+                                       float mult, float *x);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -120,10 +120,16 @@ int device_ready() {
   return d.status == ROUGE_B200_OK ? ROUGE_B200_OK : set_status(d.status);
 }
 
+namespace {
+std::atomic<int> g_sm_budget{0};  // 0 = all SMs
+}
+
 int current_sm_count() {
   int dev = 0;
   if (current_device_index(&dev) != ROUGE_B200_OK) return 0;
-  return devices()[dev].sm_count;
+  const int n = devices()[dev].sm_count;
+  const int cap = g_sm_budget.load();
+  return (cap > 0 && cap < n) ? cap : n;
 }
 
 int *device_error_word() {
@@ -249,6 +255,14 @@ RougeGemmConfig rouge_gemm_default_config(void) {
 
 int rouge_b200_device_ok(void) {
   return rb200::device_ready() == ROUGE_B200_OK ? 1 : 0;
+}
+
+/* Caps the number of SMs the persistent kernels size their grids for (0 =
+ * all SMs). Leaving a few SMs free lets communication kernels that run on
+ * another stream (e.g. the all-gather of the sharded GEMM) overlap. Returns
+ * the previous value. */
+int rouge_b200_set_sm_budget(int sms) {
+  return rb200::g_sm_budget.exchange(sms > 0 ? sms : 0);
 }
 
 /* Reads and clears the device error word of the current device after

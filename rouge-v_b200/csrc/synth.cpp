@@ -58,15 +58,18 @@ int rouge_b200_synth_uniform(uint64_t seed, size_t n, float lo, float hi, float 
   return 0;
 }
 
-/* out[i] ~ N(mean, std^2): Box-Muller on draws (2j, 2j+1) gives elements
- * 2j (cosine branch) and 2j+1 (sine branch). */
-int rouge_b200_synth_normal(uint64_t seed, size_t n, float mean, float stddev, float *out) {
-  if (!out) return -1;
-  const size_t pairs = (n + 1) / 2;
+/* Elements [offset, offset + n) of the N(mean, std^2) stream for `seed`
+ * into out[0..n): Box-Muller on draws (2j, 2j+1) gives elements 2j (cosine
+ * branch) and 2j+1 (sine branch). offset must be even. */
+int rouge_b200_synth_normal_at(uint64_t seed, size_t offset, size_t n, float mean, float stddev,
+                               float *out) {
+  if (!out || (offset & 1)) return -1;
+  const size_t pairs = (n + 1) / 2, p0 = offset / 2;
   parallel_ranges(pairs, [=](size_t a, size_t b) {
     for (size_t j = a; j < b; ++j) {
-      const double u1 = (static_cast<double>(draw(seed, 2 * j) >> 40) + 1.0) * (1.0 / 16777216.0);
-      const double u2 = unit(draw(seed, 2 * j + 1));
+      const size_t g = p0 + j;
+      const double u1 = (static_cast<double>(draw(seed, 2 * g) >> 40) + 1.0) * (1.0 / 16777216.0);
+      const double u2 = unit(draw(seed, 2 * g + 1));
       const double r = std::sqrt(-2.0 * std::log(u1));
       const double t = kTwoPi * u2;
       out[2 * j] = static_cast<float>(mean + stddev * r * std::cos(t));
@@ -76,23 +79,33 @@ int rouge_b200_synth_normal(uint64_t seed, size_t n, float mean, float stddev, f
   return 0;
 }
 
-/* Multiplies x[i] by `mult` where an independent uniform draw (stream
- * seed ^ 0xD1B54A32D192ED03) is below `frac`: the "1% of entries x20
- * outliers" of the W8A8 activation workload. Returns the count. */
-long long rouge_b200_synth_outliers(uint64_t seed, size_t n, float frac, float mult, float *x) {
+int rouge_b200_synth_normal(uint64_t seed, size_t n, float mean, float stddev, float *out) {
+  return rouge_b200_synth_normal_at(seed, 0, n, mean, stddev, out);
+}
+
+/* Multiplies x[i] (element offset + i of the stream) by `mult` where an
+ * independent uniform draw (stream seed ^ 0xD1B54A32D192ED03) is below
+ * `frac`: the "1% of entries x20 outliers" of the W8A8 activation
+ * workload. Returns the count. */
+long long rouge_b200_synth_outliers_at(uint64_t seed, size_t offset, size_t n, float frac,
+                                       float mult, float *x) {
   if (!x) return -1;
   const uint64_t s2 = seed ^ 0xD1B54A32D192ED03ull;
   std::atomic<long long> total{0};
   parallel_ranges(n, [&](size_t a, size_t b) {
     long long c = 0;
     for (size_t i = a; i < b; ++i)
-      if (unit(draw(s2, i)) < static_cast<double>(frac)) {
+      if (unit(draw(s2, offset + i)) < static_cast<double>(frac)) {
         x[i] *= mult;
         ++c;
       }
     total += c;
   });
   return total.load();
+}
+
+long long rouge_b200_synth_outliers(uint64_t seed, size_t n, float frac, float mult, float *x) {
+  return rouge_b200_synth_outliers_at(seed, 0, n, frac, mult, x);
 }
 
 }  // extern "C"

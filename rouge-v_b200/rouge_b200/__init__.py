@@ -94,6 +94,9 @@ _SIGS = {
     "rouge_b200_synth_uniform": (_I, [_U64, _SZ, _F, _F, _P]),
     "rouge_b200_synth_normal": (_I, [_U64, _SZ, _F, _F, _P]),
     "rouge_b200_synth_outliers": (C.c_longlong, [_U64, _SZ, _F, _F, _P]),
+    "rouge_b200_synth_normal_at": (_I, [_U64, _SZ, _SZ, _F, _F, _P]),
+    "rouge_b200_synth_outliers_at": (C.c_longlong, [_U64, _SZ, _SZ, _F, _F, _P]),
+    "rouge_b200_unshard_columns": (_I, [_P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
 }
 
 _lib = None
@@ -356,5 +359,17 @@ def synth_normal(seed: int, shape, mean: float, std: float, out=None) -> np.ndar
     return out
 
 
-def synth_outliers(seed: int, x: np.ndarray, frac: float, mult: float) -> int:
-    return int(lib().rouge_b200_synth_outliers(seed, x.size, frac, mult, _hp(x)))
+def synth_outliers(seed: int, x: np.ndarray, frac: float, mult: float, offset: int = 0) -> int:
+    return int(lib().rouge_b200_synth_outliers_at(seed, offset, x.size, frac, mult, _hp(x)))
+
+
+def synth_normal_at(seed: int, offset: int, shape, mean: float, std: float) -> np.ndarray:
+    out = np.empty(shape, np.float32)
+    assert lib().rouge_b200_synth_normal_at(seed, offset, out.size, mean, std, _hp(out)) == 0
+    return out
+
+
+def unshard_columns(src, dst, M, N, g, ns, R):
+    """src[M/R][g][R][ns] (all-gathered bands) -> dst[M][ldd] row-major."""
+    _check("rouge_b200_unshard_columns", lib().rouge_b200_unshard_columns(
+        _dp(src), _dp(dst), M, N, g, ns, R, dst.stride(0), src.element_size(), _stream()))
