@@ -67,6 +67,7 @@ typedef struct RougeGemmConfig {
 #define ROUGE_B200_EUNSUPPORTED (-4) /* shape or alignment outside the kernel's contract */
 #define ROUGE_B200_ETIMEOUT (-5)     /* a bounded device-side wait ran out; results invalid */
 #define ROUGE_B200_ENOMEM (-6)       /* device or pinned allocation failed */
+#define ROUGE_B200_ETOOBIG (-7)      /* problem does not fit a fixed scratch area */
 
 /* Status of the last failing call on this host thread (0 if none since the
  * last rouge_b200_clear_error). */
@@ -154,6 +155,23 @@ void rouge_dequantize_i8_group(const uint8_t *q, int rows, int cols, int groups,
 void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
                    const float *scales_a, int a_rows, const float *scales_b,
                    int b_cols, float *C);
+
+/* No counterpart in the reference. rouge_gemm_i8 (same arguments, same
+ * results) for callers that cannot let the library allocate device memory,
+ * such as a process that reserves the GPU's memory for its own allocator at
+ * start-up or a loop that must not allocate once it runs. Host pointers,
+ * synchronous. Stages operands, scales and output in a fixed 64 MiB device
+ * array (one per GPU, held until exit) instead of an allocated workspace:
+ * M*Kp + Kp*Np + 4*(M+N) + 4*M*N bytes (Kp, Np = K, N rounded up to 16, plus
+ * alignment) must fit, otherwise ROUGE_B200_ETOOBIG and C is not written.
+ * The first call on a device does a one-time set-up (the device address of
+ * the array); make it before any stream capture. Calls share the array:
+ * they are serialised by a lock and synchronise before returning; GPU work
+ * that overlapped a call's use of the array would race with it. Returns a
+ * status (ROUGE_B200_OK on success). */
+int rouge_gemm_i8_noalloc(int M, int N, int K, const int8_t *A, const int8_t *B,
+                          const float *scales_a, int a_rows, const float *scales_b,
+                          int b_cols, float *C);
 
 /* Replaces rouge_gemm_e4m3, numerics.h:68-69 (fp8.cpp:116-124).
  * A[M][K], B[K][N] OCP E4M3 codes; C f32 = dec(A) * dec(B), f32 accumulate. */

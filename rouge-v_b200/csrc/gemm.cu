@@ -614,6 +614,21 @@ int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const in
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
 
+// As launch_gemm_i8, with the device word that receives a timeout status
+// supplied by the caller.
+int launch_gemm_i8_with_err(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
+                            long long ldb, int b_layout, const float *sa, int a_rows,
+                            const float *sb, int b_cols, void *Cp, long long ldc, int out_type,
+                            int *err, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.err = err;
+  return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
 int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const uint8_t *B,
                      long long ldb, int b_layout, const float *scale_a, const float *scale_b,
                      void *Cp, long long ldc, int out_type, cudaStream_t st) {

@@ -237,6 +237,7 @@ const char *rouge_b200_status_string(int status) {
     case ROUGE_B200_EUNSUPPORTED: return "shape or alignment not supported";
     case ROUGE_B200_ETIMEOUT: return "device-side wait timed out";
     case ROUGE_B200_ENOMEM: return "out of memory";
+    case ROUGE_B200_ETOOBIG: return "problem larger than the fixed scratch area of this entry point";
     default: return "unknown status";
   }
 }

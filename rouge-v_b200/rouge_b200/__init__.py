@@ -29,6 +29,7 @@ ECUDA = -3
 EUNSUPPORTED = -4
 ETIMEOUT = -5
 ENOMEM = -6
+ETOOBIG = -7
 
 B_KN = 0
 B_NK = 1
@@ -76,6 +77,7 @@ _SIGS = {
     "rouge_b200_quantize_i8_group": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "rouge_b200_dequantize_i8_group": (_I, [_P, _I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_i8": (None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
+    "rouge_gemm_i8_noalloc": (_I, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
     "rouge_gemm_e4m3": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_f16": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_bf16": (None, [_I, _I, _I, _P, _P, _P, _P]),
