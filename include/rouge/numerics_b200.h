@@ -92,6 +92,20 @@ int rouge_b200_device_ok(void);
  * (used by the sharded GEMM). Process-wide; returns the previous value. */
 int rouge_b200_set_sm_budget(int sms);
 
+/* GEMM / convolution tile shapes (no reference counterpart: the reference's
+ * RougeGemmConfig blocking is a CPU cache blocking and is ignored).
+ *   AUTO   256 x 256 tiles computed by 2-SM CTA pairs when 128 x 256 tiles
+ *          would fill every SM, else 128 x 128 tiles on single CTAs
+ *   SINGLE single-CTA tiles only (128 x 256 or 128 x 128)
+ *   PAIR   CTA-pair tiles only (256 x 256)
+ * int8 results are identical in every mode (exact int32 accumulation).
+ * Process-wide; returns the previous
+ * mode, or ROUGE_B200_EINVAL for an unknown mode (nothing changed). */
+#define ROUGE_B200_TILES_AUTO 0
+#define ROUGE_B200_TILES_SINGLE 1
+#define ROUGE_B200_TILES_PAIR 2
+int rouge_b200_set_tile_mode(int mode);
+
 /* Synchronises `stream`, then reads and clears the current device's error
  * word, which kernels set when a bounded device-side wait runs out.
  * Returns ROUGE_B200_OK or the failure (e.g. ROUGE_B200_ETIMEOUT). */

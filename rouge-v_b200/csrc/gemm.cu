@@ -211,6 +211,67 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 }
 
+// One epilogue warp's share of one accumulator tile: TMEM lanes
+// [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`
+// of the BN columns in TMEM slot `slot`. Two 32-column tcgen05.ld loads are
+// kept in flight: chunk c+1 loads while chunk c is converted and stored.
+template <MmaKind KIND, int BN, int OUT>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tmem_base, int slot,
+                                              int m0, int nb, int quarter, int half, float sab,
+                                              uint8_t *stage, const CUtensorMap *tmC, int lane) {
+  const int row0 = m0 + quarter * 32;
+  const int row = row0 + lane;
+  const bool row_ok = row < args.M;
+  float sa = 1.0f;
+  if constexpr (KIND == MmaKind::I8) {
+    if (OUT != ROUGE_B200_OUT_I32 && row_ok) sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
+  }
+  const bool sa_ok = fabsf(sa) < 7.9e28f;  // finite and below 2^96
+  const uint32_t tbase =
+      tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * BN);
+  const int cols_left = args.N - nb * BN;
+  const int nchunks = cols_left >= BN ? BN / 32 : (cols_left + 31) / 32;  // warp-uniform
+  const int c_end = min(nchunks, (half + 1) * (BN / 64));
+  const int c_beg = half * (BN / 64);
+  if (c_beg >= c_end) return;
+  uint32_t va[32], vb[32];
+  tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
+  tmem_ld_wait_regs(va);
+  for (int c = c_beg; c < c_end; c += 2) {
+    if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
+    epilogue_chunk<KIND, OUT>(args, va, nb * BN + c * 32, row0, row, row_ok, sa, sa_ok, sab, stage,
+                              tmC, lane);
+    if (c + 1 < c_end) {
+      tmem_ld_wait_regs(vb);
+      if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
+      epilogue_chunk<KIND, OUT>(args, vb, nb * BN + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
+                                sab, stage, tmC, lane);
+      if (c + 2 < c_end) tmem_ld_wait_regs(va);
+    }
+  }
+}
+
+// Convolution: im2col box position (w, h, image) of output pixel p0, the
+// first pixel of a 128-row A block.
+__device__ __forceinline__ void conv_box(const GemmArgs &args, int p0, int &cw, int &ch, int &cn) {
+  const int ohw = args.conv_oh * args.conv_ow;
+  cn = p0 / ohw;
+  const int rem = p0 - cn * ohw;
+  ch = (rem / args.conv_ow) * args.conv_stride - args.conv_pad;
+  cw = (rem % args.conv_ow) * args.conv_stride - args.conv_pad;
+}
+
+// K-block kb of a convolution: filter tap (kr, kc), first channel c0, and
+// the K coordinate of the matching weight columns.
+__device__ __forceinline__ void conv_kblock(const GemmArgs &args, int kb, int bk, int &c0, int &kr,
+                                            int &kc, int &kx) {
+  const int tap = kb / args.conv_cblocks;
+  c0 = (kb - tap * args.conv_cblocks) * bk;
+  kr = tap / args.conv_kw;
+  kc = tap - kr * args.conv_kw;
+  kx = tap * args.conv_cin + c0;
+}
+
 template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -263,15 +324,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
       int mb, nb;
       tile_coords(t, args.num_m, args.num_n, mb, nb);
-      // Convolution: box position of the tile's first output pixel.
       int cw = 0, ch = 0, cn = 0;
-      if constexpr (CONV) {
-        const int p0 = mb * kBM, ohw = args.conv_oh * args.conv_ow;
-        cn = p0 / ohw;
-        const int rem = p0 - cn * ohw;
-        ch = (rem / args.conv_ow) * args.conv_stride - args.conv_pad;
-        cw = (rem % args.conv_ow) * args.conv_stride - args.conv_pad;
-      }
+      if constexpr (CONV) conv_box(args, mb * kBM, cw, ch, cn);
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % C::STAGES;
         const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
@@ -283,12 +337,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mbar_arrive_expect_tx(&full[s], C::STAGE_BYTES);
         int kx = kb * C::BK;  // K coordinate of the B tile
         if constexpr (CONV) {
-          const int tap = kb / args.conv_cblocks;
-          const int c0 = (kb - tap * args.conv_cblocks) * C::BK;
-          const int kr = tap / args.conv_kw, kc = tap - kr * args.conv_kw;
+          int c0, kr, kc;
+          conv_kblock(args, kb, C::BK, c0, kr, kc, kx);
           tma_load_im2col_4d(sA + s * C::A_BYTES, &tmA, &full[s], c0, cw, ch, cn,
                              static_cast<uint16_t>(kc), static_cast<uint16_t>(kr));
-          kx = tap * args.conv_cin + c0;
         } else {
           tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kx, mb * kBM);
         }
@@ -383,38 +435,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      const int row0 = mb * kBM + quarter * 32;
-      const int row = row0 + lane;
-      const bool row_ok = row < args.M;
-      float sa = 1.0f;
-      if constexpr (KIND == MmaKind::I8) {
-        if (OUT != ROUGE_B200_OUT_I32 && row_ok) sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
-      }
-      const bool sa_ok = fabsf(sa) < 7.9e28f;  // finite and below 2^96
-      const uint32_t tbase =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * BN);
-      const int cols_left = args.N - nb * BN;
-      const int nchunks = cols_left >= BN ? BN / 32 : (cols_left + 31) / 32;  // warp-uniform
-      const int c_end = min(nchunks, (half + 1) * (BN / 64));
-      const int c_beg = half * (BN / 64);
-      if (c_beg < c_end) {
-        uint32_t va[32], vb[32];
-        tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
-        tmem_ld_wait_regs(va);
-        for (int c = c_beg; c < c_end; c += 2) {
-          // The load of chunk c+1 is in flight while chunk c is converted and stored.
-          if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
-          epilogue_chunk<KIND, OUT>(args, va, nb * BN + c * 32, row0, row, row_ok, sa, sa_ok, sab,
-                                    stage, &tmC, lane);
-          if (c + 1 < c_end) {
-            tmem_ld_wait_regs(vb);
-            if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
-            epilogue_chunk<KIND, OUT>(args, vb, nb * BN + (c + 1) * 32, row0, row, row_ok, sa,
-                                      sa_ok, sab, stage, &tmC, lane);
-            if (c + 2 < c_end) tmem_ld_wait_regs(va);
-          }
-        }
-      }
+      epilogue_tile<KIND, BN, OUT>(args, tmem_base, slot, mb * kBM, nb, quarter, half, sab, stage,
+                                   &tmC, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[slot]);
@@ -430,10 +452,250 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ----------------------------------------------------------- CTA-pair tiles
+//
+// A 2-CTA cluster computes a 256 x BN tile with tcgen05.mma.cta_group::2
+// (M = 256): CTA rank r loads rows [128r, +128) of the A block and half r
+// of B's BN rows/columns into its own stage ring, the leader (rank 0) issues
+// the MMAs for both, and each CTA's TMEM receives its own 128 accumulator
+// rows, which its own epilogue warps drain. Per 128 x BN of output each SM
+// thus reads 128 + BN/2 operand rows from shared memory instead of 128 + BN:
+// the operand feed, not the tensor pipe, limits the single-CTA tile.
+//
+// Synchronisation (all barriers live in the CTA that waits on them):
+//   full[s]   leader only: armed by the leader's producer with both CTAs'
+//             bytes; both producers' loads complete_tx on it (cta_group::2
+//             TMA form, barrier addressed in the leader)
+//   empty[s]  each CTA: the leader's MMA commit arrives on both
+//   tfull[2]  each CTA: the leader's commit after a tile's last k-block
+//   tempty[2] leader only: 16 arrivals, one per epilogue warp of each CTA
+template <MmaKind KIND, int BN, bool B_MN>
+struct Cfg2 {
+  static constexpr int ESIZE = KIND == MmaKind::F16 ? 2 : 1;
+  static constexpr int BK = kBKBytes / ESIZE;
+  static constexpr int UMMA_K = 32 / ESIZE;
+  static constexpr int HALF_N = BN / 2;  // B rows (K-major) / columns (MN-major) per CTA
+  static constexpr int A_BYTES = kBM * kBKBytes;
+  static constexpr int B_BYTES = HALF_N * kBKBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
+  static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int EPI_BYTES = 8 * kStageBytes;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
+  static_assert(!B_MN || B_CHUNKS >= 1, "MN-major B needs whole 128-byte chunks per CTA");
+  static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
+};
+
+__device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint32_t peer_abort) {
+  *abort = 1;
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
+  if (err) atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
+}
+
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+  using C = Cfg2<KIND, BN, B_MN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + C::STAGES * C::A_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
+  uint64_t *empty = full + C::STAGES;
+  uint64_t *tfull = empty + C::STAGES;  // [2]
+  uint64_t *tempty = tfull + 2;         // [2]
+  uint64_t *mdone = tempty + 2;         // [1]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+  volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: leader
+  const int cluster = static_cast<int>(blockIdx.x >> 1);
+  const int nclusters = static_cast<int>(gridDim.x >> 1);
+  const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int *>(abort)), rank ^ 1u);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 16);
+    }
+    mbar_init(mdone, 1);
+    *abort = 0;
+    mbar_init_fence();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before_sync();
+  cluster_sync();  // barriers of both CTAs initialised, both TMEM allocations done
+  tc_fence_after_sync();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
+    int it = 0;
+    bool ok = true;
+    for (int t = cluster; ok && t < args.num_tiles; t += nclusters) {
+      int mb, nb;
+      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;  // this CTA's A rows
+      const int n0 = nb * BN + static_cast<int>(rank) * C::HALF_N;  // this CTA's B half
+      int cw = 0, ch = 0, cn = 0;
+      if constexpr (CONV) conv_box(args, m0, cw, ch, cn);
+      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
+        if (!mbar_wait(&empty[s], (round & 1u) ^ 1u, abort)) {
+          report_pair(args.err, abort, peer_abort);
+          ok = false;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+        const uint32_t bar = full0 + static_cast<uint32_t>(s * 8);
+        int kx = kb * C::BK;
+        if constexpr (CONV) {
+          int c0, kr, kc;
+          conv_kblock(args, kb, C::BK, c0, kr, kc, kx);
+          tma_load_im2col_4d_pair(sA + s * C::A_BYTES, &tmA, bar, c0, cw, ch, cn,
+                                  static_cast<uint16_t>(kc), static_cast<uint16_t>(kr));
+        } else {
+          tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, bar, kx, m0);
+        }
+        if constexpr (!B_MN) {
+          tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, bar, kx, n0);
+        } else {
+#pragma unroll
+          for (int j = 0; j < C::B_CHUNKS; ++j)
+            tma_load_2d_pair(sB + s * C::B_BYTES + j * C::B_CHUNK_BYTES, &tmB, bar,
+                             n0 + j * (kBKBytes / C::ESIZE), kb * C::BK);
+        }
+      }
+    }
+    // Wait for the leader's releases of the last stages, so that no commit
+    // from the leader's MMA is still to arrive on this CTA's barriers when
+    // the cluster exits (on the abort path, so that the leader's full
+    // barriers have seen the last loads land: best effort, bounded).
+    const volatile int never = 0;
+    for (int j = (it > C::STAGES ? it - C::STAGES : 0); j < it; ++j) {
+      if (ok) {
+        if (!mbar_wait(&empty[j % C::STAGES], static_cast<uint32_t>(j / C::STAGES) & 1u, abort)) {
+          report_pair(args.err, abort, peer_abort);
+          ok = false;
+        }
+      } else if (rank == 0) {
+        mbar_wait(&full[j % C::STAGES], static_cast<uint32_t>(j / C::STAGES) & 1u, &never);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;
+    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : 0u;
+    const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
+    const uint32_t idesc = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
+    const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
+    const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
+    int it = 0, local = 0;
+    bool ok = true;
+    bool issued = false;
+    for (int t = cluster; ok && t < args.num_tiles; t += nclusters, ++local) {
+      const int slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tempty[slot], (use & 1u) ^ 1u, abort)) {
+        report_pair(args.err, abort, peer_abort);
+        ok = false;
+        break;
+      }
+      tc_fence_after_sync();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+      for (int kb = 0; kb < args.num_k; ++kb, ++it) {
+        const int s = it % C::STAGES;
+        const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
+        if (!mbar_wait(&full[s], round & 1u, abort)) {
+          report_pair(args.err, abort, peer_abort);
+          ok = false;
+          break;
+        }
+        tc_fence_after_sync();
+        const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
+        const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < C::BK / C::UMMA_K; ++k) {
+          const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
+          const uint64_t bdesc =
+              B_MN ? smem_desc_sw128(b0 + k * C::UMMA_K * kBKBytes, C::B_CHUNK_BYTES, 1024)
+                   : smem_desc_sw128(b0 + k * 32, 16, 1024);
+          umma_pair<KIND>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+        }
+        issued = true;
+        tc_commit_pair(smem_u32(&empty[s]));
+        tc_commit_pair(empty_peer + static_cast<uint32_t>(s * 8));
+      }
+      if (!ok) break;
+      tc_commit_pair(smem_u32(&tfull[slot]));
+      tc_commit_pair(tfull_peer + static_cast<uint32_t>(slot * 8));
+    }
+    if (!ok && issued) {
+      const volatile int never = 0;
+      tc_commit_pair(smem_u32(mdone));
+      mbar_wait(mdone, 0u, &never);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 4) >> 2;
+    uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * kStageBytes;
+    const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);  // leader's tempty[0]
+    int local = 0;
+    float sab = 1.0f;
+    if constexpr (KIND != MmaKind::I8) {
+      if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
+    }
+    for (int t = cluster; t < args.num_tiles; t += nclusters, ++local) {
+      int mb, nb;
+      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      const int slot = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&tfull[slot], use & 1u, abort)) {
+        report_pair(args.err, abort, peer_abort);
+        break;
+      }
+      tc_fence_after_sync();
+      epilogue_tile<KIND, BN, OUT>(args, tmem_base, slot, mb * 2 * kBM + static_cast<int>(rank) * kBM,
+                                   nb, quarter, half, sab, stage, &tmC, lane);
+      tc_fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
+    }
+    if (args.use_tma_store && lane == 0) bulk_wait_all();
+  }
+
+  tc_fence_before_sync();
+  cluster_sync();  // all MMAs into both TMEMs done, no remote arrivals pending
+  if (warp == 2) {
+    tc_fence_after_sync();
+    tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
+  }
+}
+
 // Builds the output map and launches one GEMM / convolution.
-template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV>
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR>
 int launch_tiles(const CUtensorMap &ta, const CUtensorMap &tb, GemmArgs args, cudaStream_t st) {
-  using C = Cfg<KIND, BN, B_MN>;
   int s = ROUGE_B200_OK;
   // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
   // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
@@ -448,24 +710,62 @@ int launch_tiles(const CUtensorMap &ta, const CUtensorMap &tb, GemmArgs args, cu
     if (s != ROUGE_B200_OK) return s;
   }
 
-  auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT, CONV>;
-  // The shared-memory opt-in is a per-device function attribute.
-  static std::atomic<unsigned long long> attr_done{0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const unsigned long long bit = 1ull << (dev & 63);
-  if (!(attr_done.load() & bit)) {
-    s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
-    if (s != ROUGE_B200_OK) return s;
-    attr_done.fetch_or(bit);
-  }
+  const unsigned long long bit = 1ull << (current_device() & 63);
   const int sms = current_sm_count();
-  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
-  return cuda_status(cudaGetLastError());
+  if constexpr (!PAIR) {
+    using C = Cfg<KIND, BN, B_MN>;
+    auto kern = gemm_tc_kernel<KIND, BN, B_MN, OUT, CONV>;
+    // The shared-memory opt-in is a per-device function attribute.
+    static std::atomic<unsigned long long> attr_done{0};
+    if (!(attr_done.load() & bit)) {
+      s = cuda_status(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      if (s != ROUGE_B200_OK) return s;
+      attr_done.fetch_or(bit);
+    }
+    const int grid = args.num_tiles < sms ? args.num_tiles : sms;
+    kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
+    return cuda_status(cudaGetLastError());
+  } else {
+    using C = Cfg2<KIND, BN, B_MN>;
+    auto kern = gemm_tc2_kernel<KIND, BN, B_MN, OUT, CONV>;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Per device: the shared-memory opt-in, then how many 2-CTA clusters of
+    // this kernel fit on the GPU at once (SM pairs of one TPC).
+    static std::atomic<unsigned long long> attr_done{0};
+    static std::atomic<int> max_clusters[64];
+    const int dev = current_device() & 63;
+    if (!(attr_done.load() & bit)) {
+      s = cuda_status(
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      if (s != ROUGE_B200_OK) return s;
+      cfg.gridDim = dim3(2, 1, 1);
+      int n = 0;
+      s = cuda_status(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      if (s != ROUGE_B200_OK) return s;
+      if (n < 1) return set_status(ROUGE_B200_EUNSUPPORTED);
+      max_clusters[dev].store(n);
+      attr_done.fetch_or(bit);
+    }
+    int clusters = max_clusters[dev].load();
+    if (clusters > sms / 2) clusters = sms / 2 > 0 ? sms / 2 : 1;
+    if (clusters > args.num_tiles) clusters = args.num_tiles;
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
+  }
 }
 
-template <MmaKind KIND, int BN, bool B_MN, int OUT>
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool PAIR>
 int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
                      cudaStream_t st) {
   using C = Cfg<KIND, BN, B_MN>;
@@ -475,56 +775,74 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
   int s = make_tmap_2d(&ta, A, dt, args.K, args.M, static_cast<uint64_t>(lda) * C::ESIZE, C::BK,
                        kBM);
   if (s != ROUGE_B200_OK) return s;
-  if (!B_MN)
-    s = make_tmap_2d(&tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK, BN);
+  if (!B_MN)  // a CTA of a pair loads half of the tile's BN rows of B
+    s = make_tmap_2d(&tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK,
+                     PAIR ? BN / 2 : BN);
   else
     s = make_tmap_2d(&tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
                      kBKBytes / C::ESIZE, C::BK);
   if (s != ROUGE_B200_OK) return s;
-  return launch_tiles<KIND, BN, B_MN, OUT, false>(ta, tb, args, st);
+  return launch_tiles<KIND, BN, B_MN, OUT, false, PAIR>(ta, tb, args, st);
 }
 
-template <MmaKind KIND, int BN, bool B_MN>
+template <MmaKind KIND, int BN, bool B_MN, bool PAIR>
 int launch_out(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
                int out_type, cudaStream_t st) {
   switch (out_type) {
     case ROUGE_B200_OUT_F32:
-      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_F32>(A, lda, B, ldb, args, st);
+      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_F32, PAIR>(A, lda, B, ldb, args, st);
     case ROUGE_B200_OUT_BF16:
-      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_BF16>(A, lda, B, ldb, args, st);
+      return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_BF16, PAIR>(A, lda, B, ldb, args, st);
     default:
       if constexpr (KIND == MmaKind::I8)
-        return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_I32>(A, lda, B, ldb, args, st);
+        return launch_gemm_impl<KIND, BN, B_MN, ROUGE_B200_OUT_I32, PAIR>(A, lda, B, ldb, args,
+                                                                          st);
       return set_status(ROUGE_B200_EINVAL);
   }
+}
+
+// Tile shape chooser. A wave of 256 x 256 CTA-pair tiles whenever the
+// 128 x 256 tiles fill every SM at least once (same tile count per SM, half
+// the operand reads per output); otherwise 128 x 128 single-CTA tiles, which
+// spread a small problem over more SMs. rouge_b200_set_tile_mode overrides.
+std::atomic<int> g_tile_mode{ROUGE_B200_TILES_AUTO};
+
+bool use_pair_tiles(int M, int N) {
+  const int mode = g_tile_mode.load();
+  if (mode != ROUGE_B200_TILES_AUTO) return mode == ROUGE_B200_TILES_PAIR;
+  const long long tiles256 = static_cast<long long>((M + kBM - 1) / kBM) * ((N + 255) / 256);
+  return tiles256 >= current_sm_count();
 }
 
 template <MmaKind KIND>
 int launch_kind(const void *A, long long lda, const void *B, long long ldb, int b_layout,
                 GemmArgs args, int out_type, cudaStream_t st) {
-  // BN = 256 unless that leaves most SMs idle; then 128.
-  const int sms = current_sm_count();
+  const bool pair = use_pair_tiles(args.M, args.N);
+  // Single-CTA tiles: BN = 256 unless that leaves most SMs idle; then 128.
   const long long tiles256 =
       static_cast<long long>((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
 #ifdef RB200_FORCE_BN  // compile-time tile override for tuning builds
-  const int bn = RB200_FORCE_BN;
+  const int bn = pair ? 256 : RB200_FORCE_BN;
   (void)tiles256;
-  (void)sms;
 #else
-  const int bn = tiles256 >= sms ? 256 : 128;
+  const int bn = (pair || tiles256 >= current_sm_count()) ? 256 : 128;
 #endif
-  args.num_m = (args.M + kBM - 1) / kBM;
+  const int bm = pair ? 2 * kBM : kBM;
+  args.num_m = (args.M + bm - 1) / bm;
   args.num_n = (args.N + bn - 1) / bn;
   const int esize = KIND == MmaKind::F16 ? 2 : 1;
   const int bk = kBKBytes / esize;
   args.num_k = (args.K + bk - 1) / bk;
   args.num_tiles = args.num_m * args.num_n;
   const bool mn = b_layout == ROUGE_B200_B_KN;
+  if (pair)
+    return mn ? launch_out<KIND, 256, true, true>(A, lda, B, ldb, args, out_type, st)
+              : launch_out<KIND, 256, false, true>(A, lda, B, ldb, args, out_type, st);
   if (bn == 256)
-    return mn ? launch_out<KIND, 256, true>(A, lda, B, ldb, args, out_type, st)
-              : launch_out<KIND, 256, false>(A, lda, B, ldb, args, out_type, st);
-  return mn ? launch_out<KIND, 128, true>(A, lda, B, ldb, args, out_type, st)
-            : launch_out<KIND, 128, false>(A, lda, B, ldb, args, out_type, st);
+    return mn ? launch_out<KIND, 256, true, false>(A, lda, B, ldb, args, out_type, st)
+              : launch_out<KIND, 256, false, false>(A, lda, B, ldb, args, out_type, st);
+  return mn ? launch_out<KIND, 128, true, false>(A, lda, B, ldb, args, out_type, st)
+            : launch_out<KIND, 128, false, false>(A, lda, B, ldb, args, out_type, st);
 }
 
 int check_common(int M, int N, int K, const void *A, const void *B, const void *Cp, int ldc,
@@ -550,13 +868,13 @@ int vec_ok(const void *Cp, long long ldc, int out_type) {
              : 0;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 int launch_conv_bn(const CUtensorMap &ta, const uint16_t *Wt, GemmArgs g, cudaStream_t st) {
   CUtensorMap tb;
   int s = make_tmap_2d(&tb, Wt, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.K, g.N,
-                       static_cast<uint64_t>(g.K) * 2, 64, BN);
+                       static_cast<uint64_t>(g.K) * 2, 64, PAIR ? BN / 2 : BN);
   if (s != ROUGE_B200_OK) return s;
-  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true>(ta, tb, g, st);
+  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, tb, g, st);
 }
 
 }  // namespace
@@ -594,12 +912,18 @@ int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int 
   if (s != ROUGE_B200_OK) return s;
   const int sms = current_sm_count();
   const long long tiles256 = static_cast<long long>((g.M + kBM - 1) / kBM) * ((Cout + 255) / 256);
-  const int bn = (Cout > 128 && tiles256 >= sms) ? 256 : 128;
-  g.num_m = (g.M + kBM - 1) / kBM;
+  const bool pair = g_tile_mode.load() == ROUGE_B200_TILES_AUTO
+                        ? (Cout > 128 && tiles256 >= sms)
+                        : g_tile_mode.load() == ROUGE_B200_TILES_PAIR;
+  const int bn = (pair || (Cout > 128 && tiles256 >= sms)) ? 256 : 128;
+  const int bm = pair ? 2 * kBM : kBM;
+  g.num_m = (g.M + bm - 1) / bm;
   g.num_n = (Cout + bn - 1) / bn;
   g.num_k = KH * KW * g.conv_cblocks;
   g.num_tiles = g.num_m * g.num_n;
-  return bn == 256 ? launch_conv_bn<256>(ta, Wt, g, st) : launch_conv_bn<128>(ta, Wt, g, st);
+  if (pair) return launch_conv_bn<256, true>(ta, Wt, g, st);
+  return bn == 256 ? launch_conv_bn<256, false>(ta, Wt, g, st)
+                   : launch_conv_bn<128, false>(ta, Wt, g, st);
 }
 
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
@@ -658,6 +982,13 @@ int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const
 using namespace rb200;
 
 extern "C" {
+
+int rouge_b200_set_tile_mode(int mode) {
+  if (mode != ROUGE_B200_TILES_AUTO && mode != ROUGE_B200_TILES_SINGLE &&
+      mode != ROUGE_B200_TILES_PAIR)
+    return set_status(ROUGE_B200_EINVAL);
+  return g_tile_mode.exchange(mode);
+}
 
 int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, int b_layout,
                        const float *scales_a, int a_rows, const float *scales_b, int b_cols,

@@ -124,6 +124,11 @@ namespace {
 std::atomic<int> g_sm_budget{0};  // 0 = all SMs
 }
 
+int current_device() {
+  int dev = 0;
+  return current_device_index(&dev) == ROUGE_B200_OK ? dev : 0;
+}
+
 int current_sm_count() {
   int dev = 0;
   if (current_device_index(&dev) != ROUGE_B200_OK) return 0;

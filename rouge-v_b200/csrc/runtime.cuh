@@ -23,6 +23,8 @@ int cuda_status(cudaError_t e);
 
 // ROUGE_B200_OK when the current device is a compute-capability 10.x part.
 int device_ready();
+// Index (below 64) of the current device; 0 if it cannot be read.
+int current_device();
 int current_sm_count();
 
 // Device word (int) that kernels set to a non-zero status when a bounded

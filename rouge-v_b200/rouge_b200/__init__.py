@@ -36,6 +36,9 @@ B_NK = 1
 OUT_F32 = 0
 OUT_BF16 = 1
 OUT_I32 = 2
+TILES_AUTO = 0
+TILES_SINGLE = 1
+TILES_PAIR = 2
 
 
 class RougeB200Error(RuntimeError):
@@ -62,6 +65,8 @@ _SIGS = {
     "rouge_gemm_isa_variant": (C.c_char_p, []),
     "rouge_b200_device_ok": (_I, []),
     "rouge_b200_sync_status": (_I, [_P]),
+    "rouge_b200_set_sm_budget": (_I, [_I]),
+    "rouge_b200_set_tile_mode": (_I, [_I]),
     "rouge_quantize_e4m3": (C.c_uint8, [_F]),
     "rouge_dequantize_e4m3": (_F, [C.c_uint8]),
     "rouge_quantize_f16": (C.c_uint16, [_F]),
@@ -232,6 +237,25 @@ def conv2d_nhwc_f16(X, Wt, bias, Y, stride, pad, is_bf16=False):
 
 def sync_status():
     _check("rouge_b200_sync_status", lib().rouge_b200_sync_status(_stream()))
+
+
+class tile_mode:
+    """Context manager selecting the GEMM / convolution tile shapes
+    (TILES_AUTO, TILES_SINGLE or TILES_PAIR) and restoring the previous mode."""
+
+    def __init__(self, mode: int):
+        self.mode = mode
+
+    def __enter__(self):
+        prev = lib().rouge_b200_set_tile_mode(self.mode)
+        if prev < 0:
+            raise RougeB200Error("rouge_b200_set_tile_mode", prev, "unknown mode")
+        self.prev = prev
+        return self
+
+    def __exit__(self, *exc):
+        lib().rouge_b200_set_tile_mode(self.prev)
+        return False
 
 
 # ------------------------------------------------------------- host drop-in API

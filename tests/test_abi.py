@@ -66,6 +66,17 @@ def test_invalid_arguments_are_refused(rb):
     assert (out == 7).all()
 
 
+def test_tile_mode_switch(rb):
+    L = rb.lib()
+    assert L.rouge_b200_set_tile_mode(7) == rb.EINVAL          # unknown: nothing changed
+    prev = L.rouge_b200_set_tile_mode(rb.TILES_PAIR)
+    assert prev == rb.TILES_AUTO
+    with rb.tile_mode(rb.TILES_SINGLE):
+        assert L.rouge_b200_set_tile_mode(rb.TILES_SINGLE) == rb.TILES_SINGLE
+    assert L.rouge_b200_set_tile_mode(prev) == rb.TILES_PAIR   # context manager restored it
+    L.rouge_b200_clear_error()
+
+
 def test_no_cpu_fallback_without_device(rb):
     import torch
     if torch.cuda.is_available():
