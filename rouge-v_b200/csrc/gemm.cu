@@ -478,7 +478,11 @@ struct Cfg2 {
   static constexpr int A_BYTES = kBM * kBKBytes;
   static constexpr int B_BYTES = HALF_N * kBKBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+#ifdef RB200_PAIR_STAGES  // stage-count override for tuning builds
+  static constexpr int STAGES = RB200_PAIR_STAGES;
+#else
   static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
+#endif
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;

@@ -87,6 +87,65 @@ __device__ __forceinline__ uint32_t encode4_i8(float4 t, double inv, float inv_f
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
+// ---- paired single-precision arithmetic (sm_100 f32x2: two lanes of work per instruction)
+
+__device__ __forceinline__ void mul2(float &d0, float &d1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ void sub2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "sub.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// encode4_i8 with paired arithmetic. Same codes: the product p = x * inv_f,
+// its nearest-even integer through the 1.5 * 2^23 constant, and the
+// distance d = p - rne(p) (exact: both subtractions are of nearby values)
+// are the f32 path of code_i8; |d| within 2^-12 of 0.5 sends the four
+// elements to the double path. On the f32 path (inv_f finite, so the scale
+// is above 2^-128 and carries a relative error below 2^-21, subnormal or
+// not) |p| = |x| * inv_f <= 127 * (1 + 2^-20) < 127.5 because |x| is at
+// most the row maximum; so only the lower clamp is needed, and it maps a
+// NaN product to -127.
+__device__ __forceinline__ uint32_t encode4_i8_x2(float4 t, double inv, float inv_f,
+                                                  bool exact_row) {
+  float p0, p1, p2, p3, b0, b1, b2, b3, r0, r1, r2, r3, d0, d1, d2, d3;
+  mul2(p0, p1, t.x, t.y, inv_f);
+  mul2(p2, p3, t.z, t.w, inv_f);
+  add2(b0, b1, p0, p1, kRoundMagic, kRoundMagic);
+  add2(b2, b3, p2, p3, kRoundMagic, kRoundMagic);
+  sub2(r0, r1, b0, b1, kRoundMagic, kRoundMagic);
+  sub2(r2, r3, b2, b3, kRoundMagic, kRoundMagic);
+  sub2(d0, d1, p0, p1, r0, r1);
+  sub2(d2, d3, p2, p3, r2, r3);
+  const float dm = fmaxf(max3(fabsf(d0), fabsf(d1), fabsf(d2)), fabsf(d3));
+  if (exact_row || dm >= 0.499755859375f)  // 0.5 - 2^-12
+    return pack4(code_i8_exact(t.x, inv), code_i8_exact(t.y, inv), code_i8_exact(t.z, inv),
+                 code_i8_exact(t.w, inv));
+  constexpr float lo = kRoundMagic - 127.0f;
+  const uint32_t a = __float_as_uint(fmaxf(b0, lo)), b = __float_as_uint(fmaxf(b1, lo));
+  const uint32_t c = __float_as_uint(fmaxf(b2, lo)), d = __float_as_uint(fmaxf(b3, lo));
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 __device__ __forceinline__ float absmax4(float4 v) {
   return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
@@ -170,6 +229,52 @@ __global__ void __launch_bounds__(kThreads) quant_i8_rows_kernel(const float *__
       orow[i] = encode4_i8(__ldcs(xr + i), inv, inv_f, exact_row);
 #pragma unroll
     for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
+// One warp per row with the whole row in registers (VPL float4 per lane,
+// rows up to VPL * 128 elements): one coalesced read of the row, the
+// maximum by warp shuffles, the scale computed redundantly by every lane,
+// then the encode from registers. No block-level synchronisation: a warp
+// waits only for its own loads, and the other warps of the SM (12 resident)
+// keep HBM busy meanwhile.
+constexpr int kWarpRowThreads = 128;
+
+template <int VPL>
+__global__ void __launch_bounds__(kWarpRowThreads, 3)
+    quant_i8_rows_warp_kernel(const float *__restrict__ x, int rows, int cols,
+                              float *__restrict__ scales, int8_t *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = cols >> 2;
+  const int nwarps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
+  for (int r = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < rows;
+       r += nwarps) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols);
+    float4 v[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int i = j * 32 + lane;
+      v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+      amax = max3(amax, max3(fabsf(v[j].x), fabsf(v[j].y), fabsf(v[j].z)), fabsf(v[j].w));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    // quant_int8.cpp:82-84: scale and its reciprocal in double.
+    const double a = static_cast<double>(amax);
+    const float s = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
+    const double inv = __ddiv_rn(1.0, static_cast<double>(s));
+    const float inv_f = __double2float_rn(inv);
+    const bool exact_row = isinf(inv_f);
+    if (lane == 0) scales[r] = s;
+    uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const int i = j * 32 + lane;
+      if (i < nvec) orow[i] = encode4_i8_x2(v[j], inv, inv_f, exact_row);
+    }
   }
 }
 
@@ -518,7 +623,18 @@ int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8
   static int occ4 = 0, occ8 = 0;
   const int nvec = cols / 4;
   const size_t row_bytes = static_cast<size_t>(cols) * 4;
-  if (row_bytes <= 32768) {
+  const int sms = current_sm_count();
+  if (nvec <= 1024 && rows >= 4 * sms) {
+    // Warp per row, row in registers: 3 CTAs of 4 warps per SM.
+    const int cap = 3 * sms;
+    const int blocks = std::min(cap, (rows + 3) / 4);
+    if (nvec <= 256)
+      quant_i8_rows_warp_kernel<8><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
+    else if (nvec <= 512)
+      quant_i8_rows_warp_kernel<16><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
+    else
+      quant_i8_rows_warp_kernel<32><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
+  } else if (row_bytes <= 32768) {
     // Shared-memory row pipeline: 64 KB of rows in flight per CTA (96 KB
     // for 32 KB rows), 2-3 CTAs per SM.
     const int stages =

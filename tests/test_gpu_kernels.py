@@ -23,7 +23,12 @@ def dev_tensor(a, device):
 
 # ---------------------------------------------------------------- int8 quant
 
-@pytest.mark.parametrize("shape", [(1, 4), (3, 8), (48, 40), (257, 1028), (64, 8192), (16, 12288)])
+# Row counts of 600 and more take the warp-per-row kernel (one per register
+# size: rows up to 1024, 2048 and 4096 elements), fewer rows and longer
+# rows the CTA-per-row kernels.
+@pytest.mark.parametrize("shape", [(1, 4), (3, 8), (48, 40), (257, 1028), (64, 8192), (16, 12288),
+                                   (1024, 1024), (700, 2044), (1200, 4096), (4096, 4096),
+                                   (640, 4100), (800, 12)])
 def test_quantize_i8_rows(rb, orc, cuda, shape):
     rng = np.random.default_rng(shape[0] * 7 + shape[1])
     x = rng.standard_normal(shape).astype(np.float32)
@@ -48,15 +53,19 @@ def test_quantize_i8_rows_golden(rb, cuda, golden):
     assert (s.cpu().numpy().view(np.uint32) == golden["q8_scales"].view(np.uint32)).all()
 
 
-def test_quantize_i8_rows_special_values(rb, orc, cuda):
-    x = np.zeros((6, 16), np.float32)
+@pytest.mark.parametrize("reps", [1, 200])
+def test_quantize_i8_rows_special_values(rb, orc, cuda, reps):
+    x = np.zeros((8, 16), np.float32)
     x[1] = np.inf                        # scale inf, codes from NaN products
     x[2, :4] = [np.inf, -np.inf, 1.0, -1.0]
     x[3] = 1e-44                         # subnormal row: scale underflows to 0
     x[4, :3] = [np.nan, 2.0, -3.0]
     x[5] = -0.0
+    x[6] = np.linspace(-1e-36, 1e-36, 16)  # subnormal scale, finite reciprocal
+    x[7] = np.linspace(-3e-37, 3e-37, 16)  # subnormal scale, reciprocal beyond f32
+    x = np.tile(x, (reps, 1))
     q = torch.empty(x.shape, dtype=torch.int8, device=cuda)
-    s = torch.empty(6, dtype=torch.float32, device=cuda)
+    s = torch.empty(x.shape[0], dtype=torch.float32, device=cuda)
     rb.quantize_i8_rows(dev_tensor(x, cuda), s, q)
     rb.sync_status()
     oq, os_ = orc.quantize_i8_rows(x)
@@ -64,7 +73,8 @@ def test_quantize_i8_rows_special_values(rb, orc, cuda):
     assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
 
 
-def test_quantize_i8_rows_near_ties(rb, orc, cuda):
+@pytest.mark.parametrize("reps", [1, 30])
+def test_quantize_i8_rows_near_ties(rb, orc, cuda, reps):
     # Values a few ulps around k + 1/2 under several scales: the products the
     # single-precision fast path must hand to the exact double path.
     rows = []
@@ -76,7 +86,7 @@ def test_quantize_i8_rows_near_ties(rb, orc, cuda):
             v = (v.view(np.int32) + d).view(np.float32)
             row = np.concatenate([[np.float32(amax)], v, np.zeros(256 - 1 - v.size, np.float32)])
             rows.append(row[:256])
-    x = np.stack(rows).astype(np.float32)
+    x = np.tile(np.stack(rows).astype(np.float32), (reps, 1))
     q = torch.empty(x.shape, dtype=torch.int8, device=cuda)
     s = torch.empty(x.shape[0], dtype=torch.float32, device=cuda)
     rb.quantize_i8_rows(dev_tensor(x, cuda), s, q)
