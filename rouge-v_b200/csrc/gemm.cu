@@ -2,19 +2,23 @@
 //   kind::i8     int8 x int8 -> exact int32 in TMEM   (rouge_gemm_i8, quant_int8.cpp:189-211)
 //   kind::f8f6f4 e4m3 x e4m3 -> f32 in TMEM          (rouge_gemm_e4m3, fp8.cpp:116-124)
 //   kind::f16    f16/bf16 -> f32 in TMEM              (rouge_gemm_f16/bf16, fp16.cpp:123-141)
+// and the implicit-GEMM convolution (conv.cpp:26-66, im2col TMA for A).
 //
-// One persistent CTA per SM (grid = min(tiles, SMs)), 256 threads:
+// Two persistent kernels with the same warp roles (384 threads):
 //   warp 0      TMA producer: A and B k-blocks into a STAGES-deep ring of
 //               128-byte-swizzled shared-memory stages (mbarrier full/empty)
-//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=BN,
-//               K=32 bytes per instruction) into a TMEM accumulator and
-//               releases each stage with tcgen05.commit
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (K = 32 bytes per
+//               instruction) into a TMEM accumulator and releases each
+//               stage with tcgen05.commit
 //   warp 2      TMEM allocator (2 x BN columns: double-buffered accumulator)
-//   warps 4-7   epilogue: tcgen05.ld of their 32 TMEM lanes, fused scale /
-//               dequant / bf16 conversion, predicated global stores; runs
-//               while the MMA warp fills the other accumulator
-// C tile = 128 x BN. Tiles are walked in groups of 16 M-blocks so that the
-// CTAs of one wave share A and B panels in L2.
+//   warps 4-11  epilogue: tcgen05.ld of TMEM lanes, fused scale / dequant /
+//               bias / bf16 conversion, TMA tile stores; runs while the MMA
+//               warp fills the other accumulator
+// gemm_tc_kernel: one CTA per SM, 128 x BN tiles (M = 128 MMAs).
+// gemm_tc2_kernel: 2-CTA clusters, 256 x 256 tiles (cta_group::2, M = 256
+// MMAs issued by the leader CTA over both CTAs' shared memory and TMEM).
+// Tiles are walked in groups of 16 M-blocks so that the CTAs of one wave
+// share A and B panels in L2.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -54,6 +58,10 @@ struct GemmArgs {
   const float *bias;      // per output channel (column) bias added in the epilogue, or null
   int conv_cblocks;       // Cin / 64
   int conv_kw, conv_oh, conv_ow, conv_stride, conv_pad, conv_cin;
+  // CTA-pair kernel, last partial round: units from split_from on are the
+  // remaining tiles cut N-wise into `split` parts of BN / split columns
+  // (one unit per part), so that the round's units fill more clusters.
+  int split_from, split;
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
@@ -86,6 +94,20 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int &mb
   const int r = t - group * kGroupM * num_n;
   mb = first_m + r % rows_in_group;
   nb = r / rows_in_group;
+}
+
+// Unit u of the CTA-pair kernel: tile (mb, nb), part `part` of `parts`.
+__device__ __forceinline__ void unit_coords(int u, const GemmArgs &args, int &mb, int &nb, int &part,
+                                            int &parts) {
+  int t = u;
+  part = 0;
+  parts = 1;
+  if (u >= args.split_from) {
+    parts = args.split;
+    t = args.split_from + (u - args.split_from) / parts;
+    part = (u - args.split_from) - (t - args.split_from) * parts;
+  }
+  tile_coords(t, args.num_m, args.num_n, mb, nb);
 }
 
 __device__ __forceinline__ void report(int *err, volatile int *abort, int code) {
@@ -211,13 +233,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 }
 
-// One epilogue warp's share of one accumulator tile: TMEM lanes
-// [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`
-// of the BN columns in TMEM slot `slot`. Two 32-column tcgen05.ld loads are
-// kept in flight: chunk c+1 loads while chunk c is converted and stored.
-template <MmaKind KIND, int BN, int OUT>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tmem_base, int slot,
-                                              int m0, int nb, int quarter, int half, float sab,
+// One epilogue warp's share of one accumulator tile of `width` columns
+// (C columns col0 ..) held from TMEM column tcol: TMEM lanes
+// [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`.
+// Two 32-column tcgen05.ld loads are kept in flight: chunk c+1 loads while
+// chunk c is converted and stored.
+template <MmaKind KIND, int OUT>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tcol, int m0, int col0,
+                                              int width, int quarter, int half, float sab,
                                               uint8_t *stage, const CUtensorMap *tmC, int lane) {
   const int row0 = m0 + quarter * 32;
   const int row = row0 + lane;
@@ -227,25 +250,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tme
     if (OUT != ROUGE_B200_OUT_I32 && row_ok) sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
   }
   const bool sa_ok = fabsf(sa) < 7.9e28f;  // finite and below 2^96
-  const uint32_t tbase =
-      tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * BN);
-  const int cols_left = args.N - nb * BN;
-  const int nchunks = cols_left >= BN ? BN / 32 : (cols_left + 31) / 32;  // warp-uniform
-  const int c_end = min(nchunks, (half + 1) * (BN / 64));
-  const int c_beg = half * (BN / 64);
+  const uint32_t tbase = tcol + (static_cast<uint32_t>(quarter * 32) << 16);
+  const int cols_left = args.N - col0;
+  const int nchunks = cols_left >= width ? width / 32 : (cols_left + 31) / 32;  // warp-uniform
+  const int per_half = width / 64;
+  const int c_end = min(nchunks, (half + 1) * per_half);
+  const int c_beg = half * per_half;
   if (c_beg >= c_end) return;
   uint32_t va[32], vb[32];
   tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
   tmem_ld_wait_regs(va);
   for (int c = c_beg; c < c_end; c += 2) {
     if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
-    epilogue_chunk<KIND, OUT>(args, va, nb * BN + c * 32, row0, row, row_ok, sa, sa_ok, sab, stage,
+    epilogue_chunk<KIND, OUT>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab, stage,
                               tmC, lane);
     if (c + 1 < c_end) {
       tmem_ld_wait_regs(vb);
       if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
-      epilogue_chunk<KIND, OUT>(args, vb, nb * BN + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
-                                sab, stage, tmC, lane);
+      epilogue_chunk<KIND, OUT>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok, sab,
+                                stage, tmC, lane);
       if (c + 2 < c_end) tmem_ld_wait_regs(va);
     }
   }
@@ -435,8 +458,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      epilogue_tile<KIND, BN, OUT>(args, tmem_base, slot, mb * kBM, nb, quarter, half, sab, stage,
-                                   &tmC, lane);
+      epilogue_tile<KIND, OUT>(args, tmem_base + static_cast<uint32_t>(slot * BN), mb * kBM,
+                               nb * BN, BN, quarter, half, sab, stage, &tmC, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[slot]);
@@ -504,7 +527,8 @@ __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint3
 template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC,
+                    const GemmArgs args) {
   using C = Cfg2<KIND, BN, B_MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -540,6 +564,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     mbar_init_fence();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (args.split > 1) tma_prefetch_desc(&tmB2);
   }
   if (warp == 2) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -556,10 +581,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int it = 0;
     bool ok = true;
     for (int t = cluster; ok && t < args.num_tiles; t += nclusters) {
-      int mb, nb;
-      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      int mb, nb, part, parts;
+      unit_coords(t, args, mb, nb, part, parts);
+      const int half_w = C::HALF_N / parts;                         // B rows per CTA
       const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;  // this CTA's A rows
-      const int n0 = nb * BN + static_cast<int>(rank) * C::HALF_N;  // this CTA's B half
+      const int n0 = nb * BN + part * (BN / parts) + static_cast<int>(rank) * half_w;
+      const CUtensorMap *tb = parts > 1 ? &tmB2 : &tmB;
+      const uint32_t tx = 2u * static_cast<uint32_t>(C::A_BYTES + half_w * kBKBytes);
       int cw = 0, ch = 0, cn = 0;
       if constexpr (CONV) conv_box(args, m0, cw, ch, cn);
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
@@ -570,7 +598,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ok = false;
           break;
         }
-        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+        if (rank == 0) mbar_arrive_expect_tx(&full[s], tx);
         const uint32_t bar = full0 + static_cast<uint32_t>(s * 8);
         int kx = kb * C::BK;
         if constexpr (CONV) {
@@ -582,8 +610,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, bar, kx, m0);
         }
         if constexpr (!B_MN) {
-          tma_load_2d_pair(sB + s * C::B_BYTES, &tmB, bar, kx, n0);
-        } else {
+          tma_load_2d_pair(sB + s * C::B_BYTES, tb, bar, kx, n0);
+        } else {  // (no split units with MN-major B)
 #pragma unroll
           for (int j = 0; j < C::B_CHUNKS; ++j)
             tma_load_2d_pair(sB + s * C::B_BYTES + j * C::B_CHUNK_BYTES, &tmB, bar,
@@ -611,7 +639,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;
     constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : 0u;
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
-    const uint32_t idesc = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
+    const uint32_t idesc_full = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
+    const uint32_t idesc_part =
+        make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN / (args.split > 1 ? args.split : 1));
     const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
     const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
     int it = 0, local = 0;
@@ -627,6 +657,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after_sync();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+      const uint32_t idesc = t >= args.split_from ? idesc_part : idesc_full;
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % C::STAGES;
         const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
@@ -671,8 +702,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
     }
     for (int t = cluster; t < args.num_tiles; t += nclusters, ++local) {
-      int mb, nb;
-      tile_coords(t, args.num_m, args.num_n, mb, nb);
+      int mb, nb, part, parts;
+      unit_coords(t, args, mb, nb, part, parts);
       const int slot = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       if (!mbar_wait(&tfull[slot], use & 1u, abort)) {
@@ -680,8 +711,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      epilogue_tile<KIND, BN, OUT>(args, tmem_base, slot, mb * 2 * kBM + static_cast<int>(rank) * kBM,
-                                   nb, quarter, half, sab, stage, &tmC, lane);
+      epilogue_tile<KIND, OUT>(args, tmem_base + static_cast<uint32_t>(slot * BN),
+                               mb * 2 * kBM + static_cast<int>(rank) * kBM,
+                               nb * BN + part * (BN / parts), BN / parts, quarter, half, sab, stage,
+                               &tmC, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
@@ -698,9 +731,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // Builds the output map and launches one GEMM / convolution.
-template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR>
-int launch_tiles(const CUtensorMap &ta, const CUtensorMap &tb, GemmArgs args, cudaStream_t st) {
+// make_b(box_rows, map) encodes the B operand's tensor map with boxes of
+// `box_rows` rows (K-major B) and returns a status.
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR, class MakeB>
+int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_t st) {
   int s = ROUGE_B200_OK;
+  CUtensorMap tb;
+  s = make_b(PAIR ? BN / 2 : BN, &tb);
+  if (s != ROUGE_B200_OK) return s;
   // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
   // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
   CUtensorMap tc;
@@ -763,9 +801,33 @@ int launch_tiles(const CUtensorMap &ta, const CUtensorMap &tb, GemmArgs args, cu
     }
     int clusters = max_clusters[dev].load();
     if (clusters > sms / 2) clusters = sms / 2 > 0 ? sms / 2 : 1;
+    // Last partial round: cut its tiles N-wise into 2 or 4 units when that
+    // many units still fit in one round (K-major B only).
+    const int tiles = args.num_tiles;
+    const int rem = tiles % clusters;
+    args.split_from = tiles;
+    args.split = 1;
+#ifndef RB200_MAX_SPLIT  // largest N-split of the last round (tuning builds)
+#define RB200_MAX_SPLIT 2
+#endif
+    if (!B_MN && rem) {
+      for (int f = RB200_MAX_SPLIT; f >= 2; f /= 2) {
+        if (rem * f <= clusters) {
+          args.split = f;
+          break;
+        }
+      }
+    }
+    CUtensorMap tb2 = tb;
+    if (args.split > 1) {
+      args.split_from = tiles - rem;
+      args.num_tiles = args.split_from + rem * args.split;
+      s = make_b(BN / 2 / args.split, &tb2);
+      if (s != ROUGE_B200_OK) return s;
+    }
     if (clusters > args.num_tiles) clusters = args.num_tiles;
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, tc, args));
   }
 }
 
@@ -775,18 +837,18 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
   using C = Cfg<KIND, BN, B_MN>;
   const CUtensorMapDataType dt =
       C::ESIZE == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUtensorMap ta, tb;
+  CUtensorMap ta;
   int s = make_tmap_2d(&ta, A, dt, args.K, args.M, static_cast<uint64_t>(lda) * C::ESIZE, C::BK,
                        kBM);
   if (s != ROUGE_B200_OK) return s;
-  if (!B_MN)  // a CTA of a pair loads half of the tile's BN rows of B
-    s = make_tmap_2d(&tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK,
-                     PAIR ? BN / 2 : BN);
-  else
-    s = make_tmap_2d(&tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
-                     kBKBytes / C::ESIZE, C::BK);
-  if (s != ROUGE_B200_OK) return s;
-  return launch_tiles<KIND, BN, B_MN, OUT, false, PAIR>(ta, tb, args, st);
+  auto make_b = [&](int box_rows, CUtensorMap *tb) {
+    if (!B_MN)  // K-major: boxes of box_rows rows of B
+      return make_tmap_2d(tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK,
+                          box_rows);
+    return make_tmap_2d(tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
+                        kBKBytes / C::ESIZE, C::BK);
+  };
+  return launch_tiles<KIND, BN, B_MN, OUT, false, PAIR>(ta, make_b, args, st);
 }
 
 template <MmaKind KIND, int BN, bool B_MN, bool PAIR>
@@ -874,11 +936,11 @@ int vec_ok(const void *Cp, long long ldc, int out_type) {
 
 template <int BN, bool PAIR>
 int launch_conv_bn(const CUtensorMap &ta, const uint16_t *Wt, GemmArgs g, cudaStream_t st) {
-  CUtensorMap tb;
-  int s = make_tmap_2d(&tb, Wt, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.K, g.N,
-                       static_cast<uint64_t>(g.K) * 2, 64, PAIR ? BN / 2 : BN);
-  if (s != ROUGE_B200_OK) return s;
-  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, tb, g, st);
+  auto make_b = [&](int box_rows, CUtensorMap *tb) {
+    return make_tmap_2d(tb, Wt, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.K, g.N,
+                        static_cast<uint64_t>(g.K) * 2, 64, box_rows);
+  };
+  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, make_b, g, st);
 }
 
 }  // namespace

@@ -117,6 +117,14 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
       : "memory");
 }
 
+// Asynchronous prefetch of a contiguous global range into L2 (address
+// 16-byte aligned, bytes a multiple of 16); no completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
+}
+
 // 2-D tiled store of a shared-memory box to global memory (bulk-group
 // completion). Coordinates must be non-negative.
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap *tm, const void *src, int32_t x,

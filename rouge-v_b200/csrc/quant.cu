@@ -125,8 +125,9 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 // not) |p| = |x| * inv_f <= 127 * (1 + 2^-20) < 127.5 because |x| is at
 // most the row maximum; so only the lower clamp is needed, and it maps a
 // NaN product to -127.
-__device__ __forceinline__ uint32_t encode4_i8_x2(float4 t, double inv, float inv_f,
-                                                  bool exact_row) {
+// Branch-free part: the four f32-path codes, and whether any element lies
+// near a tie (the caller re-encodes such words with code_i8_exact).
+__device__ __forceinline__ uint32_t encode4_i8_fast(float4 t, float inv_f, bool &tie) {
   float p0, p1, p2, p3, b0, b1, b2, b3, r0, r1, r2, r3, d0, d1, d2, d3;
   mul2(p0, p1, t.x, t.y, inv_f);
   mul2(p2, p3, t.z, t.w, inv_f);
@@ -136,14 +137,23 @@ __device__ __forceinline__ uint32_t encode4_i8_x2(float4 t, double inv, float in
   sub2(r2, r3, b2, b3, kRoundMagic, kRoundMagic);
   sub2(d0, d1, p0, p1, r0, r1);
   sub2(d2, d3, p2, p3, r2, r3);
-  const float dm = fmaxf(max3(fabsf(d0), fabsf(d1), fabsf(d2)), fabsf(d3));
-  if (exact_row || dm >= 0.499755859375f)  // 0.5 - 2^-12
-    return pack4(code_i8_exact(t.x, inv), code_i8_exact(t.y, inv), code_i8_exact(t.z, inv),
-                 code_i8_exact(t.w, inv));
+  tie = fmaxf(max3(fabsf(d0), fabsf(d1), fabsf(d2)), fabsf(d3)) >= 0.499755859375f;  // 0.5 - 2^-12
   constexpr float lo = kRoundMagic - 127.0f;
   const uint32_t a = __float_as_uint(fmaxf(b0, lo)), b = __float_as_uint(fmaxf(b1, lo));
   const uint32_t c = __float_as_uint(fmaxf(b2, lo)), d = __float_as_uint(fmaxf(b3, lo));
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+__device__ __forceinline__ uint32_t encode4_i8_exact(float4 t, double inv) {
+  return pack4(code_i8_exact(t.x, inv), code_i8_exact(t.y, inv), code_i8_exact(t.z, inv),
+               code_i8_exact(t.w, inv));
+}
+
+__device__ __forceinline__ uint32_t encode4_i8_x2(float4 t, double inv, float inv_f,
+                                                  bool exact_row) {
+  bool tie;
+  const uint32_t w = encode4_i8_fast(t, inv_f, tie);
+  return (exact_row || tie) ? encode4_i8_exact(t, inv) : w;
 }
 
 __device__ __forceinline__ float absmax4(float4 v) {
@@ -235,20 +245,38 @@ __global__ void __launch_bounds__(kThreads) quant_i8_rows_kernel(const float *__
 // One warp per row with the whole row in registers (VPL float4 per lane,
 // rows up to VPL * 128 elements): one coalesced read of the row, the
 // maximum by warp shuffles, the scale computed redundantly by every lane,
-// then the encode from registers. No block-level synchronisation: a warp
-// waits only for its own loads, and the other warps of the SM (12 resident)
-// keep HBM busy meanwhile.
-constexpr int kWarpRowThreads = 128;
-
+// then the encode from registers. One CTA per SM owns a contiguous range of
+// rows; its warps take the range's rows one at a time from a shared-memory
+// counter, so every SM finishes within about one row-time of the others
+// whatever the row count. A warp claims its next row before it reads the
+// current one and asks L2 to prefetch it (cp.async.bulk.prefetch), so HBM
+// reads stay in flight while the warp waits and computes, without holding
+// registers or shared memory for them. No block-level synchronisation
+// after the counter is set up.
 template <int VPL>
-__global__ void __launch_bounds__(kWarpRowThreads, 3)
+__global__ void __launch_bounds__(VPL > 16 ? 384 : 512, 1)
     quant_i8_rows_warp_kernel(const float *__restrict__ x, int rows, int cols,
-                              float *__restrict__ scales, int8_t *__restrict__ out) {
+                              float *__restrict__ scales, int8_t *__restrict__ out, int pf) {
+  static_assert(VPL >= 1 && VPL <= 32, "one bit per word of a lane in the fix-up mask");
+  __shared__ int next_row;
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int nvec = cols >> 2;
-  const int nwarps = static_cast<int>((gridDim.x * blockDim.x) >> 5);
-  for (int r = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < rows;
-       r += nwarps) {
+  const uint32_t row_bytes = static_cast<uint32_t>(cols) * 4u;
+  const int per = rows / static_cast<int>(gridDim.x);
+  const int extra = rows % static_cast<int>(gridDim.x);
+  const int b = static_cast<int>(blockIdx.x);
+  const int r_end = b * per + min(b, extra) + per + (b < extra ? 1 : 0);
+  int r = b * per + min(b, extra) + warp;  // first row: static
+  if (threadIdx.x == 0) next_row = r - warp + static_cast<int>(blockDim.x >> 5);
+  __syncthreads();
+  for (; r < r_end;) {
+    int rn = 0;
+    if (lane == 0) {
+      rn = atomicAdd(&next_row, 1);
+      if (pf && rn < r_end) bulk_prefetch_l2(x + static_cast<size_t>(rn) * cols, row_bytes);
+    }
+    rn = __shfl_sync(0xffffffffu, rn, 0);
     const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols);
     float4 v[VPL];
 #pragma unroll
@@ -270,11 +298,28 @@ __global__ void __launch_bounds__(kWarpRowThreads, 3)
     const bool exact_row = isinf(inv_f);
     if (lane == 0) scales[r] = s;
     uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
+    // Branch-free encode of every word (independent chains the scheduler
+    // can interleave); words near a tie are left out and marked, then
+    // re-encoded in double from a second read of their inputs (rare: about
+    // one word in 500, or every word of a row whose reciprocal scale
+    // overflows f32).
+    uint32_t redo = 0;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int i = j * 32 + lane;
-      if (i < nvec) orow[i] = encode4_i8_x2(v[j], inv, inv_f, exact_row);
+      bool tie;
+      const uint32_t w = encode4_i8_fast(v[j], inv_f, tie);
+      tie |= exact_row;
+      if (i < nvec && !tie) orow[i] = w;
+      redo |= (tie && i < nvec) ? (1u << j) : 0u;
     }
+    while (redo) {
+      const int j = __ffs(redo) - 1;
+      redo &= redo - 1;
+      const int i = j * 32 + lane;
+      orow[i] = encode4_i8_exact(__ldg(xr + i), inv);
+    }
+    r = rn;
   }
 }
 
@@ -624,17 +669,27 @@ int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8
   const int nvec = cols / 4;
   const size_t row_bytes = static_cast<size_t>(cols) * 4;
   const int sms = current_sm_count();
-  if (nvec <= 1024 && rows >= 4 * sms) {
-    // Warp per row, row in registers: 3 CTAs of 4 warps per SM.
-    const int cap = 3 * sms;
-    const int blocks = std::min(cap, (rows + 3) / 4);
+  if (nvec <= 1024 && rows >= 2 * sms) {
+    // Warp per row, row in registers: one CTA per SM, 12 warps (rows up to
+    // 4096 elements) or 16 warps.
+#ifndef RB200_QUANT_WARPS  // warps per CTA and L2 prefetch overrides for tuning builds
+#define RB200_QUANT_WARPS 0
+#endif
+#ifndef RB200_QUANT_PF
+#define RB200_QUANT_PF 1
+#endif
+    const int grid = std::min(sms, rows);
+    const int pf = RB200_QUANT_PF;
+    const int wq = RB200_QUANT_WARPS;
     if (nvec <= 256)
-      quant_i8_rows_warp_kernel<8><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
+      quant_i8_rows_warp_kernel<8><<<grid, wq ? 32 * wq : 512, 0, st>>>(x, rows, cols, scales, out, pf);
     else if (nvec <= 512)
-      quant_i8_rows_warp_kernel<16><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
+      quant_i8_rows_warp_kernel<16><<<grid, wq ? 32 * wq : 512, 0, st>>>(x, rows, cols, scales, out, pf);
     else
-      quant_i8_rows_warp_kernel<32><<<blocks, kWarpRowThreads, 0, st>>>(x, rows, cols, scales, out);
-  } else if (row_bytes <= 32768) {
+      quant_i8_rows_warp_kernel<32><<<grid, wq ? 32 * wq : 384, 0, st>>>(x, rows, cols, scales, out, pf);
+    return cuda_status(cudaGetLastError());
+  }
+  if (row_bytes <= 32768) {
     // Shared-memory row pipeline: 64 KB of rows in flight per CTA (96 KB
     // for 32 KB rows), 2-3 CTAs per SM.
     const int stages =

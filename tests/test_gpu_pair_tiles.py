@@ -28,8 +28,11 @@ def _dev(a, cuda):
     return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
 
 
+# Few tiles: the launcher also cuts the last round's tiles N-wise into two
+# units (K-major B), so these cover split units too, (256, 96, 128) one
+# whose second part lies wholly beyond N.
 I8_SHAPES = [(100, 256, 128), (256, 256, 256), (300, 200, 96), (520, 384, 640),
-             (1024, 1024, 1024), (4096, 512, 256), (256, 4096, 128)]
+             (1024, 1024, 1024), (4096, 512, 256), (256, 4096, 128), (256, 96, 128)]
 
 
 @pytest.mark.parametrize("mode", MODES)
