@@ -51,6 +51,7 @@ struct GemmArgs {
   const float *scale_b;
   int bf16;               // kind::f16 inputs are bf16
   int use_tma_store;      // C and ldc are 16-byte aligned: epilogue stores through TMA
+  int vec16;              // scales_b / bias are 16-byte aligned: vector loads of 4 columns
   int *err;
   // Implicit-GEMM convolution (A gathered by im2col TMA): M = N*OH*OW
   // output pixels, K = KH*KW*Cin ordered (kr, kc, c), k-block = one filter
@@ -115,14 +116,39 @@ __device__ __forceinline__ void report(int *err, volatile int *abort, int code) 
   if (err) atomicCAS(err, 0, code);
 }
 
+// 32 consecutive f32 values of a per-column vector (column scales, bias)
+// starting at column col0, identical in every lane: eight 16-byte loads of
+// one address per warp (broadcast) when the chunk is whole and the vector
+// 16-byte aligned, else one element per lane and shuffles.
+__device__ __forceinline__ void column_vector(const float *vec, bool vec16, int col0, int N,
+                                              int lane, float (&out)[32]) {
+  if (vec16 && col0 + 32 <= N) {
+    const float4 *p = reinterpret_cast<const float4 *>(vec + col0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 t = __ldg(p + q);
+      out[4 * q] = t.x;
+      out[4 * q + 1] = t.y;
+      out[4 * q + 2] = t.z;
+      out[4 * q + 3] = t.w;
+    }
+  } else {
+    const int col = col0 + lane;
+    const float mine = col < N ? __ldg(vec + col) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) out[j] = __shfl_sync(0xffffffffu, mine, j);
+  }
+}
+
 // Converts one 32-column chunk of one warp's 32 accumulator rows (thread =
 // row, v[j] = column col0 + j) and writes it to C.
 //   TMA path: the chunk goes to a 128-byte (f32/i32) or 64-byte (bf16)
-//   swizzled staging buffer in shared memory and one lane issues a tiled
-//   TMA store of the 32 x 32 box; out-of-range rows and columns are
-//   clipped by the tensor map. Two buffers alternate per warp.
+//   swizzled staging buffer `buf` in shared memory and one lane issues a
+//   tiled TMA store of the 32 x 32 box; out-of-range rows and columns are
+//   clipped by the tensor map. With NBUF staging buffers per warp used in
+//   turn, the store of the previous NBUF - 1 chunks may still be reading.
 //   Direct path (C not 16-byte aligned): predicated per-thread stores.
-template <MmaKind KIND, int OUT>
+template <MmaKind KIND, int OUT, int NBUF>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint32_t (&v)[32],
                                                int col0, int row0, int row, bool row_ok, float sa,
                                                bool sa_ok, float sab, uint8_t *buf,
@@ -135,43 +161,47 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
     float f[32];
     bool may_nan = true;
     if constexpr (KIND == MmaKind::I8) {
-      float sbl;  // scale of column col0 + lane
-      if (args.b_cols) {
-        const int col = col0 + lane;
-        sbl = col < args.N ? __ldg(args.scales_b + col) : 0.0f;
-      } else {
-        sbl = __ldg(args.scales_b);
-      }
+      // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies.
       // With sa and every column scale of the chunk finite and below 2^96,
       // (float)acc * sa is finite (|acc| < 2^31) and the second product can
       // only overflow to +-inf, which x86 and the GPU both produce: no NaN,
-      // so the plain multiplies are exact here.
+      // so plain (paired) multiplies are exact here.
+      const int col = col0 + lane;
+      const float sbl = args.b_cols ? (col < args.N ? __ldg(args.scales_b + col) : 0.0f)
+                                    : __ldg(args.scales_b);
       const bool fast = __all_sync(0xffffffffu, sa_ok && fabsf(sbl) < 7.9e28f);
       may_nan = !fast;
-      // quant_int8.cpp:208: ((float)acc * sa) * sb, two rounded multiplies
+      float sb[32];
+      if (args.b_cols) {
+        column_vector(args.scales_b, args.vec16, col0, args.N, lane, sb);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sb[j] = sbl;
+      }
       if (fast) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sb = args.b_cols ? __shfl_sync(0xffffffffu, sbl, j) : sbl;
-          f[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
+        for (int j = 0; j < 32; j += 2) {
+          float a0 = __int2float_rn(static_cast<int32_t>(v[j]));
+          float a1 = __int2float_rn(static_cast<int32_t>(v[j + 1]));
+          mul2(a0, a1, a0, a1, sa);
+          mul2(f[j], f[j + 1], a0, a1, sb[j], sb[j + 1]);
         }
       } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float sb = args.b_cols ? __shfl_sync(0xffffffffu, sbl, j) : sbl;
-          f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb);
-        }
+        for (int j = 0; j < 32; ++j)
+          f[j] = x86_mul(x86_mul(__int2float_rn(static_cast<int32_t>(v[j])), sa), sb[j]);
       }
     } else if (args.bias) {
       // conv.cpp:61-64: bias added to the finished f32 sum of each channel
-      const int col = col0 + lane;
-      const float bl = col < args.N ? __ldg(args.bias + col) : 0.0f;
+      float bv[32];
+      column_vector(args.bias, args.vec16, col0, args.N, lane, bv);
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        f[j] = __fadd_rn(__uint_as_float(v[j]), __shfl_sync(0xffffffffu, bl, j));
+      for (int j = 0; j < 32; j += 2)
+        add2(f[j], f[j + 1], __uint_as_float(v[j]), __uint_as_float(v[j + 1]), bv[j], bv[j + 1]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) f[j] = __fmul_rn(__uint_as_float(v[j]), sab);
+      for (int j = 0; j < 32; j += 2)
+        mul2(f[j], f[j + 1], __uint_as_float(v[j]), __uint_as_float(v[j + 1]), sab);
     }
     if constexpr (OUT == ROUGE_B200_OUT_F32) {
 #pragma unroll
@@ -190,7 +220,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 
   if (args.use_tma_store) {
-    if (lane == 0) bulk_wait_read<0>();  // this warp's previous store has read the buffer
+    if (lane == 0) bulk_wait_read<NBUF - 1>();  // this buffer's previous store has read it
     __syncwarp();
     const uint32_t base = smem_u32(buf);
     if constexpr (OUT == ROUGE_B200_OUT_BF16) {
@@ -238,10 +268,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
 // [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`.
 // Two 32-column tcgen05.ld loads are kept in flight: chunk c+1 loads while
 // chunk c is converted and stored.
-template <MmaKind KIND, int OUT>
+template <MmaKind KIND, int OUT, int NBUF>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tcol, int m0, int col0,
                                               int width, int quarter, int half, float sab,
-                                              uint8_t *stage, const CUtensorMap *tmC, int lane) {
+                                              uint8_t *stage, int &seq, const CUtensorMap *tmC,
+                                              int lane) {
   const int row0 = m0 + quarter * 32;
   const int row = row0 + lane;
   const bool row_ok = row < args.M;
@@ -260,15 +291,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   uint32_t va[32], vb[32];
   tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
   tmem_ld_wait_regs(va);
+  // staging buffer of this warp's seq-th chunk
+  auto buf = [&]() { return stage + (NBUF > 1 ? (seq++ & 1) * kStageBytes : 0); };
   for (int c = c_beg; c < c_end; c += 2) {
     if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
-    epilogue_chunk<KIND, OUT>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab, stage,
-                              tmC, lane);
+    epilogue_chunk<KIND, OUT, NBUF>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab,
+                                    buf(), tmC, lane);
     if (c + 1 < c_end) {
       tmem_ld_wait_regs(vb);
       if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
-      epilogue_chunk<KIND, OUT>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok, sab,
-                                stage, tmC, lane);
+      epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
+                                      sab, buf(), tmC, lane);
       if (c + 2 < c_end) tmem_ld_wait_regs(va);
     }
   }
@@ -443,7 +476,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;
     const int half = (warp - 4) >> 2;
     uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * kStageBytes;
-    int local = 0;
+    int local = 0, seq = 0;
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
@@ -458,8 +491,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      epilogue_tile<KIND, OUT>(args, tmem_base + static_cast<uint32_t>(slot * BN), mb * kBM,
-                               nb * BN, BN, quarter, half, sab, stage, &tmC, lane);
+      epilogue_tile<KIND, OUT, 1>(args, tmem_base + static_cast<uint32_t>(slot * BN), mb * kBM,
+                                  nb * BN, BN, quarter, half, sab, stage, seq, &tmC, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[slot]);
@@ -501,16 +534,21 @@ struct Cfg2 {
   static constexpr int A_BYTES = kBM * kBKBytes;
   static constexpr int B_BYTES = HALF_N * kBKBytes;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-#ifdef RB200_PAIR_STAGES  // stage-count override for tuning builds
-  static constexpr int STAGES = RB200_PAIR_STAGES;
-#else
-  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES > 8 ? 8 : (192 * 1024) / STAGE_BYTES;
-#endif
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int EPI_BYTES = 8 * kStageBytes;
+#ifndef RB200_PAIR_EPI_BUFS  // staging buffers per epilogue warp (tuning builds)
+#define RB200_PAIR_EPI_BUFS 1
+#endif
+  static constexpr int EPI_BUFS = RB200_PAIR_EPI_BUFS;
+  static constexpr int EPI_BYTES = 8 * EPI_BUFS * kStageBytes;
+  static constexpr int STAGE_ROOM = (232448 - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES;
+#ifdef RB200_PAIR_STAGES  // stage-count override for tuning builds
+  static constexpr int STAGES = RB200_PAIR_STAGES;
+#else
+  static constexpr int STAGES = STAGE_ROOM > 8 ? 8 : STAGE_ROOM;
+#endif
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
@@ -694,9 +732,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;
     const int half = (warp - 4) >> 2;
-    uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * kStageBytes;
+    uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * C::EPI_BUFS * kStageBytes;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);  // leader's tempty[0]
-    int local = 0;
+    int local = 0, seq = 0;
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
@@ -711,10 +749,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      epilogue_tile<KIND, OUT>(args, tmem_base + static_cast<uint32_t>(slot * BN),
-                               mb * 2 * kBM + static_cast<int>(rank) * kBM,
-                               nb * BN + part * (BN / parts), BN / parts, quarter, half, sab, stage,
-                               &tmC, lane);
+      epilogue_tile<KIND, OUT, C::EPI_BUFS>(args, tmem_base + static_cast<uint32_t>(slot * BN),
+                                            mb * 2 * kBM + static_cast<int>(rank) * kBM,
+                                            nb * BN + part * (BN / parts), BN / parts, quarter,
+                                            half, sab, stage, seq, &tmC, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
@@ -963,6 +1001,7 @@ int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int 
   g.ldc = Cout;
   g.bf16 = is_bf16 ? 1 : 0;
   g.bias = bias;
+  g.vec16 = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
   g.use_tma_store = vec_ok(Y, Cout, ROUGE_B200_OUT_F32);
   g.err = device_error_word();
   g.conv_cblocks = Cin / 64;
@@ -1000,6 +1039,7 @@ int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const in
   g.C = Cp; g.ldc = ldc;
   g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
   g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.vec16 = (reinterpret_cast<uintptr_t>(sb) & 15u) == 0;
   g.err = device_error_word();
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
@@ -1015,6 +1055,7 @@ int launch_gemm_i8_with_err(int M, int N, int K, const int8_t *A, long long lda,
   g.C = Cp; g.ldc = ldc;
   g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
   g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.vec16 = (reinterpret_cast<uintptr_t>(sb) & 15u) == 0;
   g.err = err;
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }

@@ -87,35 +87,6 @@ __device__ __forceinline__ uint32_t encode4_i8(float4 t, double inv, float inv_f
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
 
-// ---- paired single-precision arithmetic (sm_100 f32x2: two lanes of work per instruction)
-
-__device__ __forceinline__ void mul2(float &d0, float &d1, float a0, float a1, float b) {
-  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
-      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b));
-}
-
-__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
-      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-__device__ __forceinline__ void sub2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
-      "sub.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-__device__ __forceinline__ float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
 // encode4_i8 with paired arithmetic. Same codes: the product p = x * inv_f,
 // its nearest-even integer through the 1.5 * 2^23 constant, and the
 // distance d = p - rne(p) (exact: both subtractions are of nearby values)
