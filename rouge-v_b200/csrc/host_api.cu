@@ -3,9 +3,11 @@
 // numerics.h). Each call copies its operands into a library-owned device
 // workspace (padding rows where the kernels need 16-byte pitches), runs the
 // sm_100a kernels on the library stream, copies the result back and
-// synchronises. No CPU fallback: on a device failure the output is left
-// unwritten (or partly written) and the status is kept for
-// rouge_b200_last_error().
+// synchronises. Large operands move in row bands on three streams so that
+// the copies in, the kernels and the copies out overlap (with pinned host
+// buffers). No CPU fallback: on a device failure the output is left
+// unwritten or partly written (bands finished before the failure) and the
+// status is kept for rouge_b200_last_error().
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -81,6 +83,48 @@ int finish(cudaStream_t st) {
   return take_device_error(st);
 }
 
+// Ends a banded call: waits for all three streams (the copy-out stream
+// last depends on every band) and folds in device-side failures.
+int finish_bands(HostCallContext *ctx) {
+  int s = cuda_status(cudaStreamSynchronize(ctx->in_stream));
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaStreamSynchronize(ctx->out_stream));
+  if (s != ROUGE_B200_OK) return s;
+  return finish(ctx->stream);
+}
+
+// Row bands of a banded call: about 8 bands of at least `min_rows` rows
+// (a multiple of `multiple`), one band for small operands.
+int band_rows(int rows, size_t bytes, int min_rows, int multiple) {
+  if (bytes < (size_t(8) << 20)) return rows;
+  int r = (rows + 7) / 8;
+  r = (r + multiple - 1) / multiple * multiple;
+  return r < min_rows ? min_rows : r;
+}
+
+// Issues band b = 0, 1, ... of `rows` rows in bands of `step`: in(r0, n, s)
+// on the copy-in stream, then comp(r0, n, s) on the kernel stream once the
+// copy-in is done, then out(r0, n, s) on the copy-out stream once the
+// kernels are done. Work the caller queued on the copy-in stream before
+// this call precedes every band's kernels.
+template <class In, class Comp, class Out>
+int run_bands(HostCallContext *ctx, int rows, int step, In in, Comp comp, Out out) {
+  const int nb = (rows + step - 1) / step;
+  if (2 * nb > kBandEvents) return set_status(ROUGE_B200_EINVAL);
+  for (int b = 0; b < nb; ++b) {
+    const int r0 = b * step, n = rows - r0 < step ? rows - r0 : step;
+    cudaEvent_t e_in = ctx->ev[2 * b], e_comp = ctx->ev[2 * b + 1];
+    int s = in(r0, n, ctx->in_stream);
+    if (s == ROUGE_B200_OK) s = cuda_status(cudaEventRecord(e_in, ctx->in_stream));
+    if (s == ROUGE_B200_OK) s = cuda_status(cudaStreamWaitEvent(ctx->stream, e_in, 0));
+    if (s == ROUGE_B200_OK) s = comp(r0, n, ctx->stream);
+    if (s == ROUGE_B200_OK) s = cuda_status(cudaEventRecord(e_comp, ctx->stream));
+    if (s == ROUGE_B200_OK) s = cuda_status(cudaStreamWaitEvent(ctx->out_stream, e_comp, 0));
+    if (s == ROUGE_B200_OK) s = out(r0, n, ctx->out_stream);
+    if (s != ROUGE_B200_OK) return s;
+  }
+  return ROUGE_B200_OK;
+}
+
 // Generic float GEMM through the drop-in path. es = element size of A/B;
 // kind 0 = e4m3, 1 = f16, 2 = bf16.
 void gemm_codes_host(int kind, int M, int N, int K, const void *A, const void *B, float *C) {
@@ -98,29 +142,37 @@ void gemm_codes_host(int kind, int M, int N, int K, const void *A, const void *B
   void *dA = cv.take<uint8_t>(M * Kp * es);
   void *dB = cv.take<uint8_t>(Kp * Np * es);
   float *dC = cv.take<float>(static_cast<size_t>(M) * N);
-  cudaStream_t st = ctx->stream;
-  if (h2d_pitched(dA, Kp, A, M, K, es, st) != ROUGE_B200_OK) return;
+  // B and its padding first on the copy-in stream, then bands of A rows.
+  cudaStream_t sin = ctx->in_stream;
   if (Kp != static_cast<size_t>(K) || Np != static_cast<size_t>(N)) {
-    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np * es, st)) != ROUGE_B200_OK) return;
+    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np * es, sin)) != ROUGE_B200_OK) return;
   }
   if (cuda_status(cudaMemcpy2DAsync(dB, Np * es, B, N * es, N * es, K, cudaMemcpyHostToDevice,
-                                    st)) != ROUGE_B200_OK)
+                                    sin)) != ROUGE_B200_OK)
     return;
-  int s;
-  if (kind == 0)
-    s = launch_gemm_e4m3(M, N, static_cast<int>(Kp), static_cast<const uint8_t *>(dA), Kp,
-                         static_cast<const uint8_t *>(dB), Np, ROUGE_B200_B_KN, nullptr, nullptr,
-                         dC, N, ROUGE_B200_OUT_F32, st);
-  else
-    s = launch_gemm_f16(M, N, static_cast<int>(Kp), static_cast<const uint16_t *>(dA), Kp,
-                        static_cast<const uint16_t *>(dB), Np, ROUGE_B200_B_KN, kind == 2, dC, N,
-                        ROUGE_B200_OUT_F32, st);
-  if (s != ROUGE_B200_OK) return;
-  if (finish(st) != ROUGE_B200_OK) return;  // do not copy a result a kernel failed to finish
-  if (cuda_status(cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost,
-                                  st)) != ROUGE_B200_OK)
-    return;
-  finish(st);
+  const int step = band_rows(M, M * Kp * es + static_cast<size_t>(M) * N * 4, 256, 256);
+  const uint8_t *hA = static_cast<const uint8_t *>(A);
+  uint8_t *dA8 = static_cast<uint8_t *>(dA);
+  auto in = [&](int r0, int n, cudaStream_t s) {
+    return h2d_pitched(dA8 + r0 * Kp * es, Kp, hA + static_cast<size_t>(r0) * K * es, n, K, es, s);
+  };
+  auto comp = [&](int r0, int n, cudaStream_t s) {
+    if (kind == 0)
+      return launch_gemm_e4m3(n, N, static_cast<int>(Kp), dA8 + r0 * Kp, Kp,
+                              static_cast<const uint8_t *>(dB), Np, ROUGE_B200_B_KN, nullptr,
+                              nullptr, dC + static_cast<size_t>(r0) * N, N, ROUGE_B200_OUT_F32, s);
+    return launch_gemm_f16(n, N, static_cast<int>(Kp),
+                           reinterpret_cast<const uint16_t *>(dA8 + r0 * Kp * es), Kp,
+                           static_cast<const uint16_t *>(dB), Np, ROUGE_B200_B_KN, kind == 2,
+                           dC + static_cast<size_t>(r0) * N, N, ROUGE_B200_OUT_F32, s);
+  };
+  auto out = [&](int r0, int n, cudaStream_t s) {
+    return cuda_status(cudaMemcpyAsync(C + static_cast<size_t>(r0) * N,
+                                       dC + static_cast<size_t>(r0) * N,
+                                       static_cast<size_t>(n) * N * 4, cudaMemcpyDeviceToHost, s));
+  };
+  run_bands(ctx, M, step, in, comp, out);
+  finish_bands(ctx);
 }
 
 }  // namespace
@@ -149,14 +201,23 @@ int rouge_quantize_i8_channel(const float *x, int rows, int cols, float *scales,
   float *dx = cv.take<float>(rows * cp);
   int8_t *dq = cv.take<int8_t>(rows * cp);
   float *ds = cv.take<float>(rows);
-  cudaStream_t st = ctx->stream;
-  if (h2d_pitched(dx, cp, x, rows, cols, 4, st) != ROUGE_B200_OK) return 0;
-  if (launch_quant_i8_rows(dx, rows, static_cast<int>(cp), ds, dq, st) != ROUGE_B200_OK) return 0;
-  if (d2h_pitched(out, dq, cp, rows, cols, 1, st) != ROUGE_B200_OK) return 0;
-  if (cuda_status(cudaMemcpyAsync(scales, ds, rows * 4, cudaMemcpyDeviceToHost, st)) !=
-      ROUGE_B200_OK)
-    return 0;
-  return finish(st) == ROUGE_B200_OK ? 1 : 0;
+  // Bands of rows: copy in, quantize, copy codes and scales out.
+  const int step = band_rows(rows, rows * cp * 5, 64, 64);
+  auto in = [&](int r0, int n, cudaStream_t s) {
+    return h2d_pitched(dx + r0 * cp, cp, x + static_cast<size_t>(r0) * cols, n, cols, 4, s);
+  };
+  auto comp = [&](int r0, int n, cudaStream_t s) {
+    return launch_quant_i8_rows(dx + r0 * cp, n, static_cast<int>(cp), ds + r0, dq + r0 * cp, s);
+  };
+  auto outf = [&](int r0, int n, cudaStream_t s) {
+    int st = d2h_pitched(out + static_cast<size_t>(r0) * cols, dq + r0 * cp, cp, n, cols, 1, s);
+    if (st != ROUGE_B200_OK) return st;
+    return cuda_status(cudaMemcpyAsync(scales + r0, ds + r0, static_cast<size_t>(n) * 4,
+                                       cudaMemcpyDeviceToHost, s));
+  };
+  const int s1 = run_bands(ctx, rows, step, in, comp, outf);
+  const int s2 = finish_bands(ctx);
+  return s1 == ROUGE_B200_OK && s2 == ROUGE_B200_OK ? 1 : 0;
 }
 
 int rouge_quantize_i8_tensor(const float *x, int n, float *scale_out, int8_t *out) {
@@ -295,25 +356,35 @@ void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, const 
   float *dsa = cv.take<float>(na);
   float *dsb = cv.take<float>(nb);
   float *dC = cv.take<float>(static_cast<size_t>(M) * N);
-  cudaStream_t st = ctx->stream;
-  if (h2d_pitched(dA, Kp, A, M, K, 1, st) != ROUGE_B200_OK) return;
+  // B, its padding and the scales first on the copy-in stream, then bands
+  // of A rows: while band b's output is copied out, band b+1 computes and
+  // band b+2 is copied in.
+  cudaStream_t sin = ctx->in_stream;
   if (Kp != static_cast<size_t>(K) || Np != static_cast<size_t>(N)) {
-    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np, st)) != ROUGE_B200_OK) return;
+    if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np, sin)) != ROUGE_B200_OK) return;
   }
-  if (cuda_status(cudaMemcpy2DAsync(dB, Np, B, N, N, K, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+  if (cuda_status(cudaMemcpy2DAsync(dB, Np, B, N, N, K, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
     return;
-  if (cuda_status(cudaMemcpyAsync(dsa, scales_a, na * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+  if (cuda_status(cudaMemcpyAsync(dsa, scales_a, na * 4, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
     return;
-  if (cuda_status(cudaMemcpyAsync(dsb, scales_b, nb * 4, cudaMemcpyHostToDevice, st)) != ROUGE_B200_OK)
+  if (cuda_status(cudaMemcpyAsync(dsb, scales_b, nb * 4, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
     return;
-  if (launch_gemm_i8(M, N, static_cast<int>(Kp), dA, Kp, dB, Np, ROUGE_B200_B_KN, dsa, a_rows ? 1 : 0,
-                     dsb, b_cols ? 1 : 0, dC, N, ROUGE_B200_OUT_F32, st) != ROUGE_B200_OK)
-    return;
-  if (finish(st) != ROUGE_B200_OK) return;
-  if (cuda_status(cudaMemcpyAsync(C, dC, static_cast<size_t>(M) * N * 4, cudaMemcpyDeviceToHost,
-                                  st)) != ROUGE_B200_OK)
-    return;
-  finish(st);
+  const int step = band_rows(M, M * Kp + static_cast<size_t>(M) * N * 4, 256, 256);
+  auto in = [&](int r0, int n, cudaStream_t s) {
+    return h2d_pitched(dA + r0 * Kp, Kp, A + static_cast<size_t>(r0) * K, n, K, 1, s);
+  };
+  auto comp = [&](int r0, int n, cudaStream_t s) {
+    return launch_gemm_i8(n, N, static_cast<int>(Kp), dA + r0 * Kp, Kp, dB, Np, ROUGE_B200_B_KN,
+                          a_rows ? dsa + r0 : dsa, a_rows ? 1 : 0, dsb, b_cols ? 1 : 0,
+                          dC + static_cast<size_t>(r0) * N, N, ROUGE_B200_OUT_F32, s);
+  };
+  auto out = [&](int r0, int n, cudaStream_t s) {
+    return cuda_status(cudaMemcpyAsync(C + static_cast<size_t>(r0) * N,
+                                       dC + static_cast<size_t>(r0) * N,
+                                       static_cast<size_t>(n) * N * 4, cudaMemcpyDeviceToHost, s));
+  };
+  run_bands(ctx, M, step, in, comp, out);
+  finish_bands(ctx);
 }
 
 void rouge_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B, float *C,

@@ -196,12 +196,22 @@ HostCallContext *host_context() {
   current_device_index(&dev);
   DeviceState &d = devices()[dev];
   std::call_once(d.ctx_once, [&] {
-    cudaStream_t s = nullptr;
-    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
-      cudaGetLastError();
-      return;
+    cudaStream_t s[3] = {nullptr, nullptr, nullptr};
+    for (auto &x : s) {
+      if (cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+      }
     }
-    d.ctx.stream = s;
+    for (auto &e : d.ctx.ev) {
+      if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+      }
+    }
+    d.ctx.in_stream = s[1];
+    d.ctx.out_stream = s[2];
+    d.ctx.stream = s[0];  // set last: a context with a stream is complete
   });
   if (!d.ctx.stream) {
     set_status(ROUGE_B200_ECUDA);
@@ -213,7 +223,9 @@ HostCallContext *host_context() {
 int ensure_workspace(HostCallContext *ctx, size_t bytes) {
   if (bytes <= ctx->ws_bytes) return ROUGE_B200_OK;
   if (ctx->ws) {
+    cudaStreamSynchronize(ctx->in_stream);
     cudaStreamSynchronize(ctx->stream);
+    cudaStreamSynchronize(ctx->out_stream);
     cudaFree(ctx->ws);
     ctx->ws = nullptr;
     ctx->ws_bytes = 0;

@@ -51,12 +51,20 @@ int make_tmap_im2col_nhwc(CUtensorMap *tm, const void *x, CUtensorMapDataType dt
                           int h, int w, int c, int lower_w, int lower_h, int upper_w, int upper_h,
                           int channels, int pixels, int stride_w, int stride_h);
 
-// Library-owned resources for the synchronous host-pointer entries: one
-// non-blocking stream and a growable device workspace per device. Callers
-// hold `lock` for the whole call.
+// Library-owned resources for the synchronous host-pointer entries, per
+// device: three non-blocking streams, an event pool and a growable device
+// workspace. Callers hold `lock` for the whole call. Calls that move large
+// operands split them into row bands: band b's host-to-device copy runs on
+// in_stream, its kernels on `stream`, its device-to-host copy on
+// out_stream, so that copies in both directions and the kernels overlap;
+// events from `ev` order the three per band.
+constexpr int kBandEvents = 64;
 struct HostCallContext {
   std::mutex lock;
   cudaStream_t stream = nullptr;
+  cudaStream_t in_stream = nullptr;
+  cudaStream_t out_stream = nullptr;
+  cudaEvent_t ev[kBandEvents] = {};
   void *ws = nullptr;
   size_t ws_bytes = 0;
 };

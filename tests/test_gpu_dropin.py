@@ -93,3 +93,48 @@ def test_null_and_empty_are_noops(rb, cuda):
     out = np.full((4, 4), 3.0, np.float32)
     rb.lib().rouge_gemm_f16(0, 4, 4, None, None, out.ctypes.data, None)
     assert (out == 3.0).all()
+
+
+# Operands of 8 MB and more move in row bands on three streams (copy in,
+# kernels, copy out overlapping). These shapes give several bands with a
+# ragged last one; rows on both sides of every band edge are checked.
+
+def _band_rows(M, step):
+    edges = [r for b in range(step, M, step) for r in (b - 1, b)]
+    return np.unique(np.array([0, 1, M - 1] + edges, np.int32))
+
+
+@pytest.mark.parametrize("rows,cols", [(3000, 1000), (2500, 1003)])
+def test_quantize_i8_channel_banded(rb, orc, cuda, rows, cols):
+    rng = np.random.default_rng(rows + cols)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    x[rng.random((rows, cols)) < 0.01] *= 20.0
+    q, s = rb.host_quantize_i8_channel(x)
+    oq, os_ = orc.quantize_i8_rows(x)
+    assert (q == oq).all()
+    assert (s.view(np.uint32) == os_.view(np.uint32)).all()
+
+
+@pytest.mark.parametrize("M,N,K,a_rows", [(1000, 2048, 1024, 1), (1100, 2000, 1000, 0)])
+def test_gemm_i8_banded(rb, orc, cuda, M, N, K, a_rows):
+    rng = np.random.default_rng(M + N + K)
+    A = rng.integers(-127, 128, (M, K), dtype=np.int8)
+    B = rng.integers(-127, 128, (K, N), dtype=np.int8)   # [K][N], as rouge_gemm_i8 takes it
+    sa = rng.uniform(1e-3, 2e-2, M if a_rows else 1).astype(np.float32)
+    sb = rng.uniform(1e-3, 2e-2, N).astype(np.float32)
+    C = rb.host_gemm_i8(A, B, sa, a_rows, sb, 1)
+    rows = _band_rows(M, 256)
+    _, oc = orc.gemm_i8(A, B, False, sa, a_rows, sb, 1, rows=rows)
+    assert (C[rows].view(np.uint32) == oc.view(np.uint32)).all()
+
+
+def test_gemm_f16_banded(rb, orc, cuda):
+    M, N, K = 2000, 1024, 520
+    rng = np.random.default_rng(7)
+    a = orc.f16_encode(rng.uniform(-1, 1, (M, K)).astype(np.float32))
+    b = orc.f16_encode(rng.uniform(-1, 1, (K, N)).astype(np.float32))   # [K][N]
+    C = rb.host_gemm_f16(a, b)
+    rows = _band_rows(M, 256)
+    want = orc.gemm_f32(orc.f16_decode(a), orc.f16_decode(b), False, rows=rows)
+    err = rel_l2(C[rows], want)
+    assert err < 1e-2 and err < 1e-4, err
