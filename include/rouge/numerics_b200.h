@@ -199,6 +199,23 @@ void rouge_gemm_f16(int M, int N, int K, const uint16_t *A, const uint16_t *B,
 void rouge_gemm_bf16(int M, int N, int K, const uint16_t *A, const uint16_t *B,
                      float *C, const RougeGemmConfig *cfg);
 
+/* Replace rouge_conv2d_f32, numerics.h:76-79 (conv.cpp:26-66), and
+ * rouge_conv_implicit_f32, numerics.h:106-109 (conv_implicit.cpp:24-79):
+ * Y[N][Cout][OH][OW] = conv(X[N][Cin][H][W], Wt[Cout][Cin][KH][KW]) + bias,
+ * all NCHW f32, OH = (H + 2*pad - KH)/stride + 1; bias may be NULL; NULL
+ * X/Wt/Y or invalid sizes -> no-op. Computed on tf32 tensor cores with
+ * split operands (hi + lo, three products) for f32 accuracy. Not
+ * expressible by the im2col tensor map (no-op, status
+ * ROUGE_B200_EUNSUPPORTED): pad > 128, stride > 8, KH or KW above 256, above
+ * pad + 129 or above the padded input. cfg is accepted and ignored. */
+void rouge_conv2d_f32(int N, int Cin, int H, int W, int Cout, int KH, int KW,
+                      int stride, int pad, const float *X, const float *Wt,
+                      const float *bias, float *Y, const RougeGemmConfig *cfg);
+void rouge_conv_implicit_f32(int N, int Cin, int H, int W, int Cout, int KH,
+                             int KW, int stride, int pad, const float *X,
+                             const float *Wt, const float *bias, float *Y,
+                             const RougeGemmConfig *cfg);
+
 /* ------------------------------------------------------------------------ */
 /* rouge_b200_* device-pointer extensions                                   */
 /* ------------------------------------------------------------------------ */

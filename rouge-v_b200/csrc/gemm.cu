@@ -69,7 +69,7 @@ constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128
 
 template <MmaKind KIND, int BN, bool B_MN>
 struct Cfg {
-  static constexpr int ESIZE = KIND == MmaKind::F16 ? 2 : 1;
+  static constexpr int ESIZE = KIND == MmaKind::TF32 ? 4 : (KIND == MmaKind::F16 ? 2 : 1);
   static constexpr int BK = kBKBytes / ESIZE;       // elements of K per stage
   static constexpr int UMMA_K = 32 / ESIZE;         // elements of K per instruction
   static constexpr int A_BYTES = kBM * kBKBytes;
@@ -421,7 +421,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;  // S32 : F32
-    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : 0u;  // S8 / E4M3 / F16
+    // S8 (1) / E4M3 (0) / F16 (0) / TF32 (2); BF16 (1) below
+    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : (KIND == MmaKind::TF32 ? 2u : 0u);
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
     const uint32_t idesc = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, kBM, BN);
     int it = 0, local = 0;
@@ -527,7 +528,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //   tempty[2] leader only: 16 arrivals, one per epilogue warp of each CTA
 template <MmaKind KIND, int BN, bool B_MN>
 struct Cfg2 {
-  static constexpr int ESIZE = KIND == MmaKind::F16 ? 2 : 1;
+  static constexpr int ESIZE = KIND == MmaKind::TF32 ? 4 : (KIND == MmaKind::F16 ? 2 : 1);
   static constexpr int BK = kBKBytes / ESIZE;
   static constexpr int UMMA_K = 32 / ESIZE;
   static constexpr int HALF_N = BN / 2;  // B rows (K-major) / columns (MN-major) per CTA
@@ -675,7 +676,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ------------------------------------------------------------ MMA issuer (leader)
     constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;
-    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : 0u;
+    constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : (KIND == MmaKind::TF32 ? 2u : 0u);
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
     const uint32_t idesc_full = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
     const uint32_t idesc_part =
@@ -873,8 +874,9 @@ template <MmaKind KIND, int BN, bool B_MN, int OUT, bool PAIR>
 int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb, GemmArgs args,
                      cudaStream_t st) {
   using C = Cfg<KIND, BN, B_MN>;
-  const CUtensorMapDataType dt =
-      C::ESIZE == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapDataType dt = C::ESIZE == 4   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : C::ESIZE == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CUtensorMap ta;
   int s = make_tmap_2d(&ta, A, dt, args.K, args.M, static_cast<uint64_t>(lda) * C::ESIZE, C::BK,
                        kBM);
@@ -934,7 +936,7 @@ int launch_kind(const void *A, long long lda, const void *B, long long ldb, int 
   const int bm = pair ? 2 * kBM : kBM;
   args.num_m = (args.M + bm - 1) / bm;
   args.num_n = (args.N + bn - 1) / bn;
-  const int esize = KIND == MmaKind::F16 ? 2 : 1;
+  const int esize = KIND == MmaKind::TF32 ? 4 : (KIND == MmaKind::F16 ? 2 : 1);
   const int bk = kBKBytes / esize;
   args.num_k = (args.K + bk - 1) / bk;
   args.num_tiles = args.num_m * args.num_n;
@@ -972,39 +974,46 @@ int vec_ok(const void *Cp, long long ldc, int out_type) {
              : 0;
 }
 
-template <int BN, bool PAIR>
-int launch_conv_bn(const CUtensorMap &ta, const uint16_t *Wt, GemmArgs g, cudaStream_t st) {
+template <MmaKind KIND, int BN, bool PAIR>
+int launch_conv_bn(const CUtensorMap &ta, const void *Wt, GemmArgs g, cudaStream_t st) {
+  using C = Cfg<KIND, BN, false>;
   auto make_b = [&](int box_rows, CUtensorMap *tb) {
-    return make_tmap_2d(tb, Wt, CU_TENSOR_MAP_DATA_TYPE_UINT16, g.K, g.N,
-                        static_cast<uint64_t>(g.K) * 2, 64, box_rows);
+    return make_tmap_2d(tb, Wt,
+                        C::ESIZE == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                      : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                        g.K, g.N, static_cast<uint64_t>(g.K) * C::ESIZE, C::BK, box_rows);
   };
-  return launch_tiles<MmaKind::F16, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, make_b, g, st);
+  return launch_tiles<KIND, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, make_b, g, st);
 }
 
 }  // namespace
 
-// Implicit-GEMM convolution, NHWC f16/bf16 in, f32 NHWC out (+ bias).
+// Implicit-GEMM convolution, NHWC in, f32 NHWC out (+ bias): f16/bf16
+// inputs (kind::f16, 64 channels per k-block) or f32 inputs read as tf32
+// (kind::tf32, 32 channels per k-block).
 // GEMM view: M = N*OH*OW output pixels, N = Cout, K = KH*KW*Cin in
 // (kr, kc, c) order, so the weights [Cout][KH][KW][Cin] are the K-major B
 // operand as stored. The A tile of k-block (tap, c0) is one im2col TMA load:
-// 128 consecutive output pixels (crossing rows and images) x 64 channels of
-// filter tap (kr, kc), zeros in the padding.
-int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
-                    const uint16_t *X, const uint16_t *Wt, const float *bias, float *Y,
-                    int is_bf16, cudaStream_t st) {
+// 128 consecutive output pixels (crossing rows and images) x BK channels of
+// filter tap (kr, kc), zeros in the padding. Y has row pitch ldy >= Cout.
+template <MmaKind KIND>
+int launch_conv(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
+                const void *X, const void *Wt, const float *bias, float *Y, long long ldy,
+                int is_bf16, cudaStream_t st) {
+  using C0 = Cfg<KIND, 128, false>;
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   GemmArgs g{};
   g.M = N * OH * OW;
   g.N = Cout;
   g.K = KH * KW * Cin;
   g.C = Y;
-  g.ldc = Cout;
+  g.ldc = ldy;
   g.bf16 = is_bf16 ? 1 : 0;
   g.bias = bias;
   g.vec16 = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
-  g.use_tma_store = vec_ok(Y, Cout, ROUGE_B200_OUT_F32);
+  g.use_tma_store = vec_ok(Y, ldy, ROUGE_B200_OUT_F32);
   g.err = device_error_word();
-  g.conv_cblocks = Cin / 64;
+  g.conv_cblocks = Cin / C0::BK;
   g.conv_kw = KW;
   g.conv_oh = OH;
   g.conv_ow = OW;
@@ -1012,8 +1021,11 @@ int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int 
   g.conv_pad = pad;
   g.conv_cin = Cin;
   CUtensorMap ta;
-  int s = make_tmap_im2col_nhwc(&ta, X, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, N, H, W, Cin, -pad, -pad,
-                                pad - (KW - 1), pad - (KH - 1), 64, kBM, stride, stride);
+  int s = make_tmap_im2col_nhwc(&ta, X,
+                                C0::ESIZE == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                               : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                                C0::ESIZE, N, H, W, Cin, -pad, -pad, pad - (KW - 1), pad - (KH - 1),
+                                C0::BK, kBM, stride, stride);
   if (s != ROUGE_B200_OK) return s;
   const int sms = current_sm_count();
   const long long tiles256 = static_cast<long long>((g.M + kBM - 1) / kBM) * ((Cout + 255) / 256);
@@ -1026,9 +1038,25 @@ int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int 
   g.num_n = (Cout + bn - 1) / bn;
   g.num_k = KH * KW * g.conv_cblocks;
   g.num_tiles = g.num_m * g.num_n;
-  if (pair) return launch_conv_bn<256, true>(ta, Wt, g, st);
-  return bn == 256 ? launch_conv_bn<256, false>(ta, Wt, g, st)
-                   : launch_conv_bn<128, false>(ta, Wt, g, st);
+  if (pair) return launch_conv_bn<KIND, 256, true>(ta, Wt, g, st);
+  return bn == 256 ? launch_conv_bn<KIND, 256, false>(ta, Wt, g, st)
+                   : launch_conv_bn<KIND, 128, false>(ta, Wt, g, st);
+}
+
+int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
+                    const uint16_t *X, const uint16_t *Wt, const float *bias, float *Y,
+                    int is_bf16, cudaStream_t st) {
+  return launch_conv<MmaKind::F16>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, bias, Y, Cout,
+                                   is_bf16, st);
+}
+
+// f32 NHWC convolution with tf32 operands (Cin a multiple of 32, inputs of
+// at least 128 KB, 16-byte aligned X and Wt).
+int launch_conv_tf32(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
+                     const float *X, const float *Wt, const float *bias, float *Y, long long ldy,
+                     cudaStream_t st) {
+  return launch_conv<MmaKind::TF32>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, bias, Y, ldy,
+                                    0, st);
 }
 
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,

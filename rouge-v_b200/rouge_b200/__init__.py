@@ -86,6 +86,8 @@ _SIGS = {
     "rouge_gemm_e4m3": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_f16": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_bf16": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_conv2d_f32": (None, [_I] * 9 + [_P, _P, _P, _P, _P]),
+    "rouge_conv_implicit_f32": (None, [_I] * 9 + [_P, _P, _P, _P, _P]),
     "rouge_b200_quantize_i8_rows": (_I, [_P, _I, _I, _P, _P, _P]),
     "rouge_b200_dequantize_i8_rows": (_I, [_P, _I, _I, _P, _F, _P, _P]),
     "rouge_b200_absmax_f32": (_I, [_P, _SZ, _P, _P]),
@@ -361,6 +363,25 @@ def _host_gemm_codes(name, A, B_kn, dtype):
 
 def host_gemm_e4m3(A, B_kn):
     return _host_gemm_codes("rouge_gemm_e4m3", A, B_kn, np.uint8)
+
+
+def host_conv2d_f32(x, w, bias, stride, pad, implicit=False):
+    """rouge_conv2d_f32 / rouge_conv_implicit_f32: x[N][Cin][H][W],
+    w[Cout][Cin][KH][KW], bias[Cout] or None; returns y[N][Cout][OH][OW]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    N, Cin, H, W = x.shape
+    Cout, _, KH, KW = w.shape
+    OH = (H + 2 * pad - KH) // stride + 1
+    OW = (W + 2 * pad - KW) // stride + 1
+    y = np.full((N, Cout, OH, OW), np.nan, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    fn = lib().rouge_conv_implicit_f32 if implicit else lib().rouge_conv2d_f32
+    lib().rouge_b200_clear_error()
+    fn(N, Cin, H, W, Cout, KH, KW, stride, pad, _hp(x), _hp(w), None if b is None else _hp(b),
+       _hp(y), None)
+    _last_error("rouge_conv_implicit_f32" if implicit else "rouge_conv2d_f32")
+    return y
 
 
 def host_gemm_f16(A, B_kn):
