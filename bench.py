@@ -258,8 +258,8 @@ def run_ours(args, rank, world, local_rank):
                      "achieved": round(gemm_tops, 2), "peak": round(int8_peak, 1), "unit": "TOP/s",
                      "frac": round(gemm_tops / int8_peak, 4),
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch,
-                     # ncu capture summarised in profiles/gemm_tc_i8_w8a8_4096.md
-                     "traffic": 52.76e6, "traffic_unit": "bytes per launch (ncu)",
+                     # ncu capture summarised in profiles/gemm_tc2_i8_w8a8_4096.md
+                     "traffic": 56.28e6, "traffic_unit": "bytes per launch (ncu)",
                      "peak_source": f"2 x {peak_src} dense bf16 ({peaks['bf16_tflops']} TF/s); "
                                     "int8 dense rate is twice bf16 on B200",
                      "frac_of_datasheet_4500": round(gemm_tops / 4500.0, 4)},
