@@ -526,15 +526,47 @@ __global__ void __launch_bounds__(kThreads) absmax_kernel(const float *__restric
   if (threadIdx.x == 0 && m > 0.0f) atomicMax(amax_bits, __float_as_uint(m));
 }
 
-__device__ __forceinline__ uint32_t enc4(float4 v, float s) {
-  return static_cast<uint32_t>(encode_e4m3(x86_div(v.x, s))) |
-         (static_cast<uint32_t>(encode_e4m3(x86_div(v.y, s))) << 8) |
-         (static_cast<uint32_t>(encode_e4m3(x86_div(v.z, s))) << 16) |
-         (static_cast<uint32_t>(encode_e4m3(x86_div(v.w, s))) << 24);
+// Two f32 values to E4M3 codes with the hardware conversion (round to
+// nearest even, saturating to +-448): `lo` in bits 0-7, `hi` in bits 8-15.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// Four codes e4m3(x / s) (element 0 in the low byte) without a division:
+// q = x * r with r = 1/s correctly rounded lies within 2^-23 of the
+// reference quotient fl(x / s) (relative), so when the hardware codes of
+// q * (1 - 2^-21) and q * (1 + 2^-21) agree, every value between them,
+// fl(x / s) included, has that code (rounding is monotonic). Elements whose
+// bracket straddles a code boundary, non-finite quotients, and nonzero
+// quotients below 2^-9 (where the reference drops the sign of results that
+// underflow to zero and the hardware keeps it) are flagged in `redo` and
+// take the exact path (x86 division and the reference encoder).
+__device__ __forceinline__ uint32_t enc4_fast(float4 v, float r, uint32_t &redo) {
+  const float q[4] = {__fmul_rn(v.x, r), __fmul_rn(v.y, r), __fmul_rn(v.z, r), __fmul_rn(v.w, r)};
+  float lo[4], hi[4];
+  uint32_t bad = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    lo[k] = __fmul_rn(q[k], 0.99999952316284180f);  // 1 - 2^-21
+    hi[k] = __fmul_rn(q[k], 1.00000047683715820f);  // 1 + 2^-21
+    const float aq = fabsf(q[k]);
+    bad |= ((!(aq <= 3.0e38f)) || (aq < 0.001953125f && aq != 0.0f)) ? (1u << k) : 0u;
+  }
+  const uint32_t clo = cvt_e4m3x2(lo[0], lo[1]) | (cvt_e4m3x2(lo[2], lo[3]) << 16);
+  const uint32_t chi = cvt_e4m3x2(hi[0], hi[1]) | (cvt_e4m3x2(hi[2], hi[3]) << 16);
+  const uint32_t diff = clo ^ chi;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) bad |= ((diff >> (8 * k)) & 0xFFu) ? (1u << k) : 0u;
+  redo = bad;
+  return clo;
 }
 
 // out[i] = e4m3(x[i] / s), s = amax / 448 (1 when amax == 0). 16 elements
-// per thread per step: four 16-byte loads, one 16-byte store.
+// per thread per step: four 16-byte loads, one 16-byte store. When s is not
+// a finite normal float, or r = 1/s is not, every element takes the exact
+// path.
 __global__ void __launch_bounds__(kThreads) e4m3_scaled_kernel(const float *__restrict__ x,
                                                                size_t n,
                                                                const float *__restrict__ amax,
@@ -542,6 +574,9 @@ __global__ void __launch_bounds__(kThreads) e4m3_scaled_kernel(const float *__re
                                                                uint8_t *__restrict__ out) {
   const float a = __ldg(amax);
   const float s = a > 0.0f ? __fdiv_rn(a, 448.0f) : 1.0f;
+  const float r = __frcp_rn(s);
+  const bool exact_all = !(fabsf(s) >= 1.1754944e-38f && fabsf(s) <= 3.0e38f &&
+                           fabsf(r) >= 1.1754944e-38f && fabsf(r) <= 3.0e38f);
   const size_t tid = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   if (tid == 0 && scale_out) *scale_out = s;
   const size_t n16 = n / 16;
@@ -549,14 +584,28 @@ __global__ void __launch_bounds__(kThreads) e4m3_scaled_kernel(const float *__re
   const float4 *x4 = reinterpret_cast<const float4 *>(x);
   uint4 *o16 = reinterpret_cast<uint4 *>(out);
   for (size_t i = tid; i < n16; i += stride) {
-    const float4 a0 = __ldcs(x4 + 4 * i), a1 = __ldcs(x4 + 4 * i + 1);
-    const float4 a2 = __ldcs(x4 + 4 * i + 2), a3 = __ldcs(x4 + 4 * i + 3);
-    uint4 o;
-    o.x = enc4(a0, s);
-    o.y = enc4(a1, s);
-    o.z = enc4(a2, s);
-    o.w = enc4(a3, s);
-    o16[i] = o;
+    float4 v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = __ldcs(x4 + 4 * i + k);
+    uint32_t w[4], redo[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      w[k] = enc4_fast(v[k], r, redo[k]);
+      if (exact_all) redo[k] = 0xFu;
+    }
+    if (redo[0] | redo[1] | redo[2] | redo[3]) {  // rare: re-encode flagged elements exactly
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float e[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (redo[k] & (1u << j)) {
+            const uint32_t c = encode_e4m3(x86_div(e[j], s));
+            w[k] = (w[k] & ~(0xFFu << (8 * j))) | (c << (8 * j));
+          }
+      }
+    }
+    o16[i] = make_uint4(w[0], w[1], w[2], w[3]);
   }
   for (size_t t = n16 * 16 + tid; t < n; t += stride) out[t] = encode_e4m3(x86_div(x[t], s));
 }

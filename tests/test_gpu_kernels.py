@@ -205,6 +205,34 @@ def test_e4m3_per_tensor(rb, orc, cuda, n):
     assert (out.cpu().numpy() == oc).all()
 
 
+@pytest.mark.parametrize("amax", [3.7, 1000.0, 0.0123, 6.02e-5])
+def test_e4m3_per_tensor_near_code_boundaries(rb, orc, cuda, amax):
+    # Values a few ulps around (s * m) for every e4m3 midpoint and code value
+    # m, under scales that are not powers of two: the quotients the
+    # division-free encoder must hand to the exact path.
+    s = np.float32(np.float32(amax) / np.float32(448.0))
+    codes = orc.e4m3_decode(np.arange(256, dtype=np.uint8))
+    vals = np.unique(np.abs(codes[np.isfinite(codes)]).astype(np.float64))
+    mids = (vals[:-1] + vals[1:]) / 2
+    base = np.concatenate([vals, mids, [2.0 ** -10, 2.0 ** -9, 464.0]])
+    x = (base * float(s)).astype(np.float32)
+    x = np.concatenate([(x.view(np.int32) + d).view(np.float32) for d in range(-4, 5)])
+    x = np.concatenate([x, -x])
+    x = x[np.abs(x) < np.float32(amax)]
+    x = np.concatenate([[np.float32(amax)], x]).astype(np.float32)
+    x = np.resize(x, (x.size + 15) // 16 * 16)
+    xd = dev_tensor(x, cuda)
+    am = torch.empty(2, dtype=torch.float32, device=cuda)
+    out = torch.empty(x.size, dtype=torch.uint8, device=cuda)
+    rb.quantize_e4m3_tensor(xd, am[0:1], am[1:2], out)
+    rb.sync_status()
+    oc, os_, _ = orc.quantize_e4m3_tensor(x)
+    assert np.float32(am[1].item()) == np.float32(os_)
+    got = out.cpu().numpy()
+    bad = np.nonzero(got != oc)[0]
+    assert bad.size == 0, (x[bad[:8]], got[bad[:8]], oc[bad[:8]])
+
+
 def test_e4m3_per_tensor_special_values(rb, orc, cuda):
     # x86-64 results the reference produces: a NaN operand keeps its sign,
     # inf/inf is the negative default NaN, x/inf is +-0.
