@@ -515,12 +515,13 @@ __global__ void __launch_bounds__(kThreads) absmax_kernel(const float *__restric
   const float4 *x4 = reinterpret_cast<const float4 *>(x);
   float m0 = 0.0f, m1 = 0.0f;
   size_t i = tid;
-  for (; i + stride < n4; i += 2 * stride) {  // two independent loads in flight
+  for (; i + 3 * stride < n4; i += 4 * stride) {  // four independent loads in flight
     const float4 a = __ldcs(x4 + i), b = __ldcs(x4 + i + stride);
-    m0 = fmaxf(m0, absmax4(a));
-    m1 = fmaxf(m1, absmax4(b));
+    const float4 c = __ldcs(x4 + i + 2 * stride), d = __ldcs(x4 + i + 3 * stride);
+    m0 = fmaxf(m0, fmaxf(absmax4(a), absmax4(c)));
+    m1 = fmaxf(m1, fmaxf(absmax4(b), absmax4(d)));
   }
-  if (i < n4) m0 = fmaxf(m0, absmax4(__ldcs(x4 + i)));
+  for (; i < n4; i += stride) m0 = fmaxf(m0, absmax4(__ldcs(x4 + i)));
   for (size_t t = n4 * 4 + tid; t < n; t += stride) m1 = fmaxf(m1, fabsf(x[t]));
   const float m = block_max(fmaxf(m0, m1), red);
   if (threadIdx.x == 0 && m > 0.0f) atomicMax(amax_bits, __float_as_uint(m));
