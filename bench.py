@@ -289,19 +289,26 @@ M5, N5, K5 = 16384, 28672, 8192
 
 def run_sharded(args, rank, world, local_rank, flush):
     """W8A8 GEMM M=16384, K=8192, N=28672 with W split
-    N-wise over the `world` GPUs, int32 accumulation, dequant to bf16, NCCL
-    all-gather of the output shards (band by band, overlapped with the
-    GEMM), unshard to row-major C[M][N] on every rank. Strong scaling."""
+    N-wise over the `world` GPUs, int32 accumulation, dequant to bf16, the
+    output assembled row-major C[M][N] on every rank. Strong scaling. Two
+    implementations, each timed and checked:
+      fused  the all-gather fused into the GEMM epilogue: every tile is
+             written to every rank's C with NVLink multicast stores
+             (multimem, one per 16 bytes) into symmetric memory, then a
+             device-side barrier across the ranks;
+      nccl   the GEMM in row bands, each band's shard all-gathered by NCCL on
+             a communication stream (overlapping the next band), then a
+             layout kernel (unshard) into C."""
     import torch
     import rouge_b200 as rb
-    from rouge_b200.sharded import ShardedW8A8
+    from rouge_b200.sharded import FusedShardedW8A8, ShardedW8A8, shard_columns
     dist = None
     if world > 1:
         import torch.distributed as dist
     dev = torch.device("cuda", local_rank)
     peaks, peak_src = load_peaks()
-    sh = ShardedW8A8(M5, N5, K5, rank, world, dev, R=2048)
-    n0, n1 = sh.columns
+    ns, ranges = shard_columns(N5, world)
+    n0, n1 = ranges[rank]
     ncols = n1 - n0
     # activations: full X on every rank, quantized per token (setup)
     x = torch.from_numpy(rb.synth_normal(8, (M5, K5), 0.0, 1.0))
@@ -313,90 +320,124 @@ def run_sharded(args, rank, world, local_rank, flush):
     rb.quantize_i8_rows(xd, sx, qx)
     del xd
     # this rank's weight rows [n0, n1), quantized per output channel (setup)
-    w = torch.zeros((sh.ns, K5), dtype=torch.float32)
+    w = torch.zeros((ns, K5), dtype=torch.float32)
     if ncols > 0:
         w[:ncols] = torch.from_numpy(rb.synth_normal_at(9, n0 * K5, (ncols, K5), 0.0, 0.02))
     wd = w.to(dev)
     del w
-    qw = torch.empty((sh.ns, K5), dtype=torch.int8, device=dev)
-    sw = torch.empty(sh.ns, dtype=torch.float32, device=dev)
+    qw = torch.empty((ns, K5), dtype=torch.int8, device=dev)
+    sw = torch.empty(ns, dtype=torch.float32, device=dev)
     rb.quantize_i8_rows(wd, sw, qw)
     del wd
     torch.cuda.synchronize()
 
-    reserve = 8 if world > 1 else 0    # SMs left for the NCCL kernels
-    prev = rb.lib().rouge_b200_set_sm_budget(max(0, torch.cuda.get_device_properties(dev).multi_processor_count - reserve) if reserve else 0)
-    try:
-        for _ in range(2):
-            sh(qx, sx, qw, sw)
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        steps = max(3, min(args.steps, 10))
-        g_ms, t_ms = [], []
-        for _ in range(steps):
-            l2_flush(flush)
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            evd = {}
-            e0.record()
-            sh(qx, sx, qw, sw, events=evd)
-            e1.record()
-            torch.cuda.synchronize()
-            g_ms.append(e0.elapsed_time(evd["gemm_done"]))
-            t_ms.append(e0.elapsed_time(e1))
-        rb.sync_status()
-    finally:
-        rb.lib().rouge_b200_set_sm_budget(prev)
-    gm = sorted(g_ms)[len(g_ms) // 2]
-    tm = sorted(t_ms)[len(t_ms) // 2]
-    if dist:
-        t = torch.tensor([gm, tm], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        gm, tm = t.tolist()
-
-    # parity: this rank's columns of sampled rows, bit-exact against the oracle
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     orc = O.Oracle()
     rows = np.array([0, 1, 2047, 2048, 8191, 16383], np.int32)
-    ok = True
+    want = None
     if ncols > 0:
         _, c = orc.gemm_i8(qx[rows.tolist()].cpu().numpy(), qw[:ncols].cpu().numpy(), True,
                            sx[rows.tolist()].cpu().numpy(), 1, sw[:ncols].cpu().numpy(), 1)
-        got = sh.out[rows.tolist(), n0:n1].view(torch.int16).cpu().numpy().view(np.uint16)
-        ok = bool((got == orc.bf16_encode(c)).all())
-    # placement: every rank's block in this rank's output equals that rank's shard
-    placed = True
-    if dist:
-        mine = sh.shard[:, :sh.ns].float().sum(dim=1)
-        allsums = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(allsums, mine)
-        for q, (q0, q1) in enumerate(sh.ranges):
-            blk = torch.zeros((M5, sh.ns), dtype=torch.float32, device=dev)
-            blk[:, : q1 - q0] = sh.out[:, q0:q1].float()
-            placed &= bool(torch.equal(blk.sum(dim=1), allsums[q]))
-        flags = torch.tensor([int(ok), int(placed)], device=dev)
-        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
-        ok, placed = bool(flags[0].item()), bool(flags[1].item())
-
+        want = orc.bf16_encode(c)
     ops = 2.0 * M5 * N5 * K5
     tc8 = 2.0 * peaks["bf16_tflops"]
-    return {
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+
+    def measure(sh, reserve):
+        prev = rb.lib().rouge_b200_set_sm_budget(max(0, sms - reserve) if reserve else 0)
+        try:
+            for _ in range(2):
+                sh(qx, sx, qw, sw)
+            torch.cuda.synchronize()
+            if dist:
+                dist.barrier()
+            steps = max(3, min(args.steps, 10))
+            g_ms, t_ms = [], []
+            for _ in range(steps):
+                l2_flush(flush)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                evd = {}
+                e0.record()
+                out = sh(qx, sx, qw, sw, events=evd)
+                e1.record()
+                torch.cuda.synchronize()
+                g_ms.append(e0.elapsed_time(evd["gemm_done"]))
+                t_ms.append(e0.elapsed_time(e1))
+            rb.sync_status()
+        finally:
+            rb.lib().rouge_b200_set_sm_budget(prev)
+        gm = sum(g_ms) / len(g_ms)
+        tm = sum(t_ms) / len(t_ms)
+        if dist:
+            t = torch.tensor([gm, tm], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            gm, tm = t.tolist()
+        # parity: this rank's columns of sampled rows, bit-exact
+        ok = True
+        if ncols > 0:
+            got = out[rows.tolist(), n0:n1].view(torch.int16).cpu().numpy().view(np.uint16)
+            ok = bool((got == want).all())
+        # placement: every rank's block in this rank's output equals the
+        # block that rank computed (per-row checksums exchanged over NCCL)
+        placed = True
+        if dist:
+            mine = torch.zeros((M5, ns), dtype=torch.float32, device=dev)
+            mine[:, :ncols] = out[:, n0:n1].float()
+            mine = mine.sum(dim=1)
+            allsums = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(allsums, mine)
+            for q, (q0, q1) in enumerate(ranges):
+                blk = torch.zeros((M5, ns), dtype=torch.float32, device=dev)
+                blk[:, : q1 - q0] = out[:, q0:q1].float()
+                placed &= bool(torch.equal(blk.sum(dim=1), allsums[q]))
+            flags = torch.tensor([int(ok), int(placed)], device=dev)
+            dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+            ok, placed = bool(flags[0].item()), bool(flags[1].item())
+        return {
+            "gemm_ms": round(gm, 4), "total_ms": round(tm, 4),
+            "gemm_tops_per_gpu": round(2.0 * M5 * ns * K5 / (gm * 1e-3) / 1e12, 1),
+            "gemm_frac_per_gpu": round(2.0 * M5 * ns * K5 / (gm * 1e-3) / 1e12 / tc8, 4),
+            "e2e_tops": round(ops / (tm * 1e-3) / 1e12, 1),
+            "sms_for_gemm": sms - reserve,
+            "parity_rows_bit_exact": ok, "placement_checksum_ok": placed,
+        }
+
+    res = {
         "workload": "sharded W8A8 GEMM (BASELINE config 5): M=16384 K=8192 N=28672, "
-                    f"W split N-wise over {world} GPU(s), bf16 out, NCCL all-gather, row-major C",
-        "scaling": "strong", "g": world, "band_rows": sh.R, "shard_cols": sh.ns,
-        "gemm_ms": round(gm, 4), "total_ms": round(tm, 4),
-        "gemm_tops_per_gpu": round(2.0 * M5 * sh.ns * K5 / (gm * 1e-3) / 1e12, 1),
-        "gemm_frac_per_gpu": round(2.0 * M5 * sh.ns * K5 / (gm * 1e-3) / 1e12 / tc8, 4),
-        "gemm_tops_total": round(ops / (gm * 1e-3) / 1e12, 1),
-        "e2e_tops": round(ops / (tm * 1e-3) / 1e12, 1),
-        "gather_bytes_in_per_gpu": int(M5 * N5 * 2 * (world - 1) / world),
-        "nvlink_gbs_per_gpu": round(M5 * N5 * 2 * (world - 1) / world / max(tm - gm, 1e-6) / 1e6, 1)
-        if world > 1 else None,
-        "sms_for_gemm": torch.cuda.get_device_properties(dev).multi_processor_count - reserve,
-        "parity_rows_bit_exact": ok, "placement_checksum_ok": placed,
+                    f"W split N-wise over {world} GPU(s), bf16 out, row-major C[M][N] on every rank",
+        "scaling": "strong", "g": world, "shard_cols": ns,
+        "output_bytes_per_gpu_sent": int(M5 * ns * 2) if world > 1 else 0,
     }
+    notes = {"multimem": "epilogue stores every tile into every rank's C through the NVLink "
+                         "multicast address (one multimem.st per 16 B), then a device-side barrier",
+             "peer-stores": "epilogue stores every 32x32 tile into every rank's C with one TMA "
+                            "tile store per rank (peer pointers), then a device-side barrier",
+             "local": "one GPU: the GEMM writes C directly"}
+    for key, use_mc in (("fused", False), ("fused_multimem", True)):
+        if key == "fused_multimem" and world == 1:
+            continue
+        fused = FusedShardedW8A8(M5, N5, K5, rank, world, dev, use_multicast=use_mc)
+        r = measure(fused, 0)
+        r["mode"] = fused.mode
+        r["note"] = notes[fused.mode]
+        res[key] = r
+        fused.close()
+        del fused
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    sh = ShardedW8A8(M5, N5, K5, rank, world, dev, R=2048)
+    r = measure(sh, 8 if world > 1 else 0)
+    r["mode"] = "nccl all-gather per 2048-row band + unshard"
+    if world > 1:
+        r["nvlink_gbs_per_gpu"] = round(M5 * N5 * 2 * (world - 1) / world /
+                                        max(r["total_ms"] - r["gemm_ms"], 1e-6) / 1e6, 1)
+    res["nccl"] = r
+    del sh
+    res["e2e_tops"] = max(v["e2e_tops"] for k, v in res.items() if isinstance(v, dict))
+    return res
 
 
 # ------------------------------------------------------------------ configs 1, 3, 4

@@ -281,6 +281,24 @@ int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
                        const float *scales_b, int b_cols, void *C, int ldc,
                        int out_type, void *stream);
 
+/* rouge_b200_gemm_i8 with its output broadcast to every GPU of a sharded
+ * job (no reference counterpart: the reference has no multi-GPU code; this
+ * is the all-gather of the N-sharded W8A8 GEMM fused into the epilogue).
+ * Each output element (m, n) of this rank's M x N block is written to
+ * element (m, col_off + n) of every rank's [M][ldc] output:
+ *   C_mc != NULL: one multimem store per 16 bytes to the NVLink multicast
+ *                 address C_mc (the switch writes every bound GPU's copy);
+ *   C_mc == NULL: one store per entry of C_peers[0..npeers) (1..8 device
+ *                 pointers, this GPU's own output included).
+ * Requires N % 8 == 0, 16-byte row pitch and column offset, K % 16 == 0.
+ * The kernel ends with a system-scope fence; the caller synchronises the
+ * ranks (a device-side barrier) before anyone reads the output. */
+int rouge_b200_gemm_i8_bcast(int M, int N, int K, const int8_t *A, const int8_t *B,
+                             int b_layout, const float *scales_a, int a_rows,
+                             const float *scales_b, int b_cols, void *C_mc,
+                             void *const *C_peers, int npeers, long long ldc, int col_off,
+                             int out_type, void *stream);
+
 /* E4M3 GEMM on tcgen05 (kind::f8f6f4), f32 accumulation in TMEM.
  * C = acc * (scale_a[0] * scale_b[0]) when the scale pointers (device f32
  * scalars) are non-NULL, else acc. out_type F32 or BF16. Same layout and

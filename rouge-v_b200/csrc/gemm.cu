@@ -53,6 +53,17 @@ struct GemmArgs {
   int use_tma_store;      // C and ldc are 16-byte aligned: epilogue stores through TMA
   int vec16;              // scales_b / bias are 16-byte aligned: vector loads of 4 columns
   int *err;
+  // Broadcast output (the sharded W8A8 GEMM): instead of C, every output
+  // element goes to column col_off + n of row m of each rank's [M][bld]
+  // output, through one multimem store to the multicast address `bcast`
+  // (NVLink multicast: the switch writes every bound GPU's copy) or, when
+  // bcast is null, through one TMA tile store per entry of peers[0..npeers)
+  // (OutMaps built over each rank's block).
+  void *bcast;
+  void *peers[8];
+  int npeers;
+  int col_off;
+  long long bld;
   // Implicit-GEMM convolution (A gathered by im2col TMA): M = N*OH*OW
   // output pixels, K = KH*KW*Cin ordered (kr, kc, c), k-block = one filter
   // tap x 64 channels.
@@ -66,6 +77,15 @@ struct GemmArgs {
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
+
+// Output tensor maps of the epilogue's TMA stores: one (this GPU's C), or
+// one per rank when the output is broadcast through peer pointers (each
+// map covers that rank's copy of this GEMM's column block).
+constexpr int kMaxOutMaps = 8;
+struct alignas(64) OutMaps {
+  CUtensorMap m[kMaxOutMaps];
+  int n;
+};
 
 template <MmaKind KIND, int BN, bool B_MN>
 struct Cfg {
@@ -152,7 +172,7 @@ template <MmaKind KIND, int OUT, int NBUF>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint32_t (&v)[32],
                                                int col0, int row0, int row, bool row_ok, float sa,
                                                bool sa_ok, float sab, uint8_t *buf,
-                                               const CUtensorMap *tmC, int lane) {
+                                               const OutMaps *om, int lane) {
   uint32_t o[32];  // f32 / i32 bits, or bf16 pairs in o[0..15]
   if constexpr (OUT == ROUGE_B200_OUT_I32) {
 #pragma unroll
@@ -219,6 +239,27 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
     }
   }
 
+  if (args.bcast) {
+    if (!row_ok) return;
+    // 16-byte vectors of this row's chunk: 8 (f32) or 4 (bf16) of them, as
+    // far as the chunk lies inside N (N is a multiple of 8 in this mode).
+    constexpr int kVecElems = OUT == ROUGE_B200_OUT_BF16 ? 8 : 4;
+    const int cols = min(32, args.N - col0);
+    const int nvec = cols / kVecElems;
+    const size_t esz = OUT == ROUGE_B200_OUT_BF16 ? 2 : 4;
+    const size_t off =
+        (static_cast<size_t>(row) * args.bld + static_cast<size_t>(args.col_off + col0)) * esz;
+#pragma unroll
+    for (int q = 0; q < 32 / kVecElems; ++q) {
+      if (q >= nvec) break;
+      const uint64_t p = reinterpret_cast<uint64_t>(args.bcast) + off + 16 * q;
+      asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p),
+                   "r"(o[4 * q]), "r"(o[4 * q + 1]), "r"(o[4 * q + 2]), "r"(o[4 * q + 3])
+                   : "memory");
+    }
+    return;
+  }
+
   if (args.use_tma_store) {
     if (lane == 0) bulk_wait_read<NBUF - 1>();  // this buffer's previous store has read it
     __syncwarp();
@@ -241,7 +282,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-      if (row0 < args.M) tma_store_2d(tmC, buf, col0, row0);
+      if (row0 < args.M)
+        for (int r = 0; r < om->n; ++r) tma_store_2d(&om->m[r], buf, col0, row0);
       bulk_commit();
     }
     return;
@@ -271,7 +313,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
 template <MmaKind KIND, int OUT, int NBUF>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tcol, int m0, int col0,
                                               int width, int quarter, int half, float sab,
-                                              uint8_t *stage, int &seq, const CUtensorMap *tmC,
+                                              uint8_t *stage, int &seq, const OutMaps *om,
                                               int lane) {
   const int row0 = m0 + quarter * 32;
   const int row = row0 + lane;
@@ -296,12 +338,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   for (int c = c_beg; c < c_end; c += 2) {
     if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
     epilogue_chunk<KIND, OUT, NBUF>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab,
-                                    buf(), tmC, lane);
+                                    buf(), om, lane);
     if (c + 1 < c_end) {
       tmem_ld_wait_regs(vb);
       if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
       epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
-                                      sab, buf(), tmC, lane);
+                                      sab, buf(), om, lane);
       if (c + 2 < c_end) tmem_ld_wait_regs(va);
     }
   }
@@ -331,7 +373,7 @@ __device__ __forceinline__ void conv_kblock(const GemmArgs &args, int kb, int bk
 template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const GemmArgs args) {
+                   const __grid_constant__ OutMaps om, const GemmArgs args) {
   using C = Cfg<KIND, BN, B_MN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -493,12 +535,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_after_sync();
       epilogue_tile<KIND, OUT, 1>(args, tmem_base + static_cast<uint32_t>(slot * BN), mb * kBM,
-                                  nb * BN, BN, quarter, half, sab, stage, seq, &tmC, lane);
+                                  nb * BN, BN, quarter, half, sab, stage, seq, &om, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[slot]);
     }
     if (args.use_tma_store && lane == 0) bulk_wait_all();
+    // Broadcast stores reach other GPUs: order them before anything this
+    // thread's kernel completion releases (the cross-rank barrier after it).
+    if (args.bcast || args.npeers) asm volatile("fence.acq_rel.sys;" ::: "memory");
   }
 
   tc_fence_before_sync();
@@ -566,7 +611,7 @@ __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint3
 template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmC,
+                    const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ OutMaps om,
                     const GemmArgs args) {
   using C = Cfg2<KIND, BN, B_MN>;
   extern __shared__ uint8_t smem_raw[];
@@ -753,12 +798,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epilogue_tile<KIND, OUT, C::EPI_BUFS>(args, tmem_base + static_cast<uint32_t>(slot * BN),
                                             mb * 2 * kBM + static_cast<int>(rank) * kBM,
                                             nb * BN + part * (BN / parts), BN / parts, quarter,
-                                            half, sab, stage, seq, &tmC, lane);
+                                            half, sab, stage, seq, &om, lane);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
     }
     if (args.use_tma_store && lane == 0) bulk_wait_all();
+    // Broadcast stores reach other GPUs: order them before anything this
+    // thread's kernel completion releases (the cross-rank barrier after it).
+    if (args.bcast || args.npeers) asm volatile("fence.acq_rel.sys;" ::: "memory");
   }
 
   tc_fence_before_sync();
@@ -780,15 +828,28 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
   if (s != ROUGE_B200_OK) return s;
   // Output map for the epilogue's TMA stores: 32 x 32 boxes, swizzle
   // matching the staging layout (128 B rows for 4-byte, 64 B for bf16).
-  CUtensorMap tc;
+  // Broadcast through peer pointers: one map per rank over that rank's copy
+  // of this GEMM's column block (clipping at the block's edges).
+  OutMaps tc;
   std::memset(&tc, 0, sizeof(tc));
-  if (args.use_tma_store) {
-    const bool b16 = OUT == ROUGE_B200_OUT_BF16;
-    s = make_tmap_2d(&tc, args.C,
-                     b16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, args.N,
-                     args.M, static_cast<uint64_t>(args.ldc) * (b16 ? 2 : 4), 32, 32,
-                     b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool b16 = OUT == ROUGE_B200_OUT_BF16;
+  const CUtensorMapDataType odt = b16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+  const CUtensorMapSwizzle osw = b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  const int oes = b16 ? 2 : 4;
+  if (args.npeers) {
+    for (int r = 0; r < args.npeers; ++r) {
+      s = make_tmap_2d(&tc.m[r], static_cast<uint8_t *>(args.peers[r]) +
+                                     static_cast<size_t>(args.col_off) * oes,
+                       odt, args.N, args.M, static_cast<uint64_t>(args.bld) * oes, 32, 32, osw);
+      if (s != ROUGE_B200_OK) return s;
+    }
+    tc.n = args.npeers;
+    args.use_tma_store = 1;
+  } else if (args.use_tma_store) {
+    s = make_tmap_2d(&tc.m[0], args.C, odt, args.N, args.M,
+                     static_cast<uint64_t>(args.ldc) * oes, 32, 32, osw);
     if (s != ROUGE_B200_OK) return s;
+    tc.n = 1;
   }
 
   const unsigned long long bit = 1ull << (current_device() & 63);
@@ -1088,6 +1149,27 @@ int launch_gemm_i8_with_err(int M, int N, int K, const int8_t *A, long long lda,
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
 
+// The int8 GEMM with its output broadcast to every rank's C (see
+// GemmArgs::bcast): the sharded W8A8 GEMM's all-gather fused into the
+// epilogue.
+int launch_gemm_i8_bcast(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
+                         long long ldb, int b_layout, const float *sa, int a_rows,
+                         const float *sb, int b_cols, void *mc, void *const *peers, int npeers,
+                         long long ldc, int col_off, int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.scales_a = sa; g.scales_b = sb; g.a_rows = a_rows; g.b_cols = b_cols;
+  g.use_tma_store = 0;
+  g.vec16 = (reinterpret_cast<uintptr_t>(sb) & 15u) == 0;
+  g.err = device_error_word();
+  g.bcast = mc;
+  g.npeers = mc ? 0 : npeers;
+  for (int r = 0; r < g.npeers; ++r) g.peers[r] = peers[r];
+  g.col_off = col_off;
+  g.bld = ldc;
+  return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
 int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const uint8_t *B,
                      long long ldb, int b_layout, const float *scale_a, const float *scale_b,
                      void *Cp, long long ldc, int out_type, cudaStream_t st) {
@@ -1136,6 +1218,36 @@ int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, in
   const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
   return launch_gemm_i8(M, N, K, A, K, B, ldb, b_layout, scales_a, a_rows, scales_b, b_cols, C,
                         ldc, out_type, as_stream(stream));
+}
+
+int rouge_b200_gemm_i8_bcast(int M, int N, int K, const int8_t *A, const int8_t *B, int b_layout,
+                             const float *scales_a, int a_rows, const float *scales_b, int b_cols,
+                             void *C_mc, void *const *C_peers, int npeers, long long ldc,
+                             int col_off, int out_type, void *stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || col_off < 0 || ldc < static_cast<long long>(col_off) + N)
+    return set_status(ROUGE_B200_EINVAL);
+  if (b_layout != ROUGE_B200_B_KN && b_layout != ROUGE_B200_B_NK) return set_status(ROUGE_B200_EINVAL);
+  if (out_type != ROUGE_B200_OUT_F32 && out_type != ROUGE_B200_OUT_BF16 &&
+      out_type != ROUGE_B200_OUT_I32)
+    return set_status(ROUGE_B200_EINVAL);
+  if (out_type != ROUGE_B200_OUT_I32 && (!scales_a || !scales_b)) return set_status(ROUGE_B200_EINVAL);
+  if (!C_mc && (!C_peers || npeers < 1 || npeers > 8)) return set_status(ROUGE_B200_EINVAL);
+  const long long esz = out_type == ROUGE_B200_OUT_BF16 ? 2 : 4;
+  // 16-byte vectors: row pitch, column offset and width in whole vectors.
+  if ((ldc * esz) % 16 || (col_off * esz) % 16 || N % 8 || K % 16 ||
+      (b_layout == ROUGE_B200_B_KN && N % 16) ||
+      (reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
+      (reinterpret_cast<uintptr_t>(C_mc) & 15u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  if (!C_mc)
+    for (int r = 0; r < npeers; ++r)
+      if (!C_peers[r] || (reinterpret_cast<uintptr_t>(C_peers[r]) & 15u))
+        return set_status(ROUGE_B200_EINVAL);
+  int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
+  return launch_gemm_i8_bcast(M, N, K, A, K, B, ldb, b_layout, scales_a, a_rows, scales_b, b_cols,
+                              C_mc, C_peers, npeers, ldc, col_off, out_type, as_stream(stream));
 }
 
 int rouge_b200_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B, int b_layout,

@@ -97,6 +97,8 @@ _SIGS = {
     "rouge_b200_convert_f32_to_bf16": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_convert_e4m3_to_f32": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_gemm_i8": (_I, [_I, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P]),
+    "rouge_b200_gemm_i8_bcast": (_I, [_I, _I, _I, _P, _P, _I, _P, _I, _P, _I, _P, _P, _I,
+                                      C.c_longlong, _I, _I, _P]),
     "rouge_b200_gemm_e4m3": (_I, [_I, _I, _I, _P, _P, _I, _P, _P, _P, _I, _I, _P]),
     "rouge_b200_gemm_f16": (_I, [_I, _I, _I, _P, _P, _I, _I, _P, _I, _I, _P]),
     "rouge_b200_conv2d_nhwc_f16": (_I, [_I] * 9 + [_P, _P, _P, _P, _I, _P]),
@@ -210,6 +212,20 @@ def gemm_i8(A, B, b_layout, C_, out_type, scales_a=None, a_rows=1, scales_b=None
     _check("rouge_b200_gemm_i8", lib().rouge_b200_gemm_i8(
         M, N, K, _dp(A), _dp(B), b_layout, _dp(scales_a), a_rows, _dp(scales_b), b_cols,
         _dp(C_), C_.stride(0), out_type, _stream()))
+
+
+def gemm_i8_bcast(A, B, b_layout, out_type, scales_a, a_rows, scales_b, b_cols, mc_ptr=0,
+                  peer_ptrs=(), ldc=0, col_off=0):
+    """rouge_b200_gemm_i8_bcast: this rank's M x N block written to column
+    col_off of every rank's [M][ldc] output, through the multicast address
+    mc_ptr (an int) or the list of peer pointers peer_ptrs (ints)."""
+    M, K = A.shape
+    N = B.shape[0] if b_layout == B_NK else B.shape[1]
+    peers = (C.c_void_p * 8)(*[C.c_void_p(p) for p in peer_ptrs]) if not mc_ptr else None
+    _check("rouge_b200_gemm_i8_bcast", lib().rouge_b200_gemm_i8_bcast(
+        M, N, K, _dp(A), _dp(B), b_layout, _dp(scales_a), a_rows, _dp(scales_b), b_cols,
+        C.c_void_p(mc_ptr) if mc_ptr else None, peers, 0 if mc_ptr else len(peer_ptrs), ldc,
+        col_off, out_type, _stream()))
 
 
 def gemm_e4m3(A, B, b_layout, C_, out_type, scale_a=None, scale_b=None):

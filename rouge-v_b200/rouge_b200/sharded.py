@@ -115,3 +115,87 @@ class ShardedW8A8:
             cur.wait_stream(self.comm)
         self.unshard(self.gathered, self.out, self.M, self.N, self.world, self.ns, R)
         return self.out
+
+
+class FusedShardedW8A8:
+    """The same product as ShardedW8A8 with the all-gather fused into the
+    GEMM: every rank's output C[M][N] is a symmetric-memory buffer (one
+    allocation per rank, mapped into every rank's address space), and the
+    GEMM epilogue writes each tile of this rank's column block [n0, n1) into
+    every rank's C at once -- one multimem store per 16 bytes to the buffer's
+    NVLink multicast address (the NVSwitch replicates it to every GPU), or,
+    where the allocation has no multicast support, one store per rank
+    through the peer pointers. No separate exchange, no layout step: the
+    tiles land row-major at their final place. A device-side barrier across
+    the ranks (signal pads, system scope) ends each call, after which every
+    rank's C is complete.
+
+    Requires N % 16 == 0 (16-byte vectors at every shard's column offset).
+    """
+
+    def __init__(self, M: int, N: int, K: int, rank: int, world: int, device, group=None,
+                 use_multicast: bool = True):
+        import torch
+        import torch.distributed as dist
+        from . import OUT_BF16, B_NK, gemm_i8, gemm_i8_bcast
+
+        assert N % 16 == 0, "fused sharding needs N % 16 == 0"
+        self.M, self.N, self.K = M, N, K
+        self.rank, self.world = rank, world
+        self.device = torch.device(device)
+        self.ns, self.ranges = shard_columns(N, world)
+        self._gemm, self._bcast, self._bf16, self._nk = gemm_i8, gemm_i8_bcast, OUT_BF16, B_NK
+        self.handle = None
+        self.mc = 0
+        self.peers = ()
+        if world == 1:
+            self.out = torch.empty((M, N), dtype=torch.bfloat16, device=self.device)
+            self.mode = "local"
+            return
+        import torch.distributed._symmetric_memory as symm
+        g = group if group is not None else dist.group.WORLD
+        self.out = symm.empty((M, N), dtype=torch.bfloat16, device=self.device)
+        self.handle = symm.rendezvous(self.out, g)
+        has_mc = use_multicast and bool(symm._SymmetricMemory.has_multicast_support(
+            symm.DeviceType.CUDA, self.device.index or 0))
+        # The handle's pointers address the start of each rank's allocation;
+        # the tensor starts `delta` bytes into it (0 when it owns the whole
+        # allocation). Every store stays inside [delta, delta + M*N*2).
+        delta = self.out.data_ptr() - int(self.handle.buffer_ptrs[rank])
+        if delta < 0 or delta + M * N * 2 > int(self.handle.buffer_size):
+            raise RuntimeError("symmetric buffer does not cover the output")
+        mc = int(self.handle.multicast_ptr) if has_mc else 0
+        if mc:
+            self.mc, self.mode = mc + delta, "multimem"
+        else:
+            self.peers = tuple(int(p) + delta for p in self.handle.buffer_ptrs)
+            self.mode = "peer-stores"
+
+    @property
+    def columns(self) -> Tuple[int, int]:
+        return self.ranges[self.rank]
+
+    def __call__(self, a, sa, w_shard, sw_shard, events=None):
+        """a[M][K] int8, sa[M] f32, w_shard[ns][K] int8 (rows beyond this
+        rank's columns ignored), sw_shard[ns] f32. Returns C[M][N] bf16."""
+        import torch
+        n0, n1 = self.columns
+        ncols = n1 - n0
+        cur = torch.cuda.current_stream(self.device)
+        if self.world == 1:
+            self._gemm(a, w_shard[:ncols], self._nk, self.out, self._bf16, sa, 1, sw_shard[:ncols], 1)
+        elif ncols > 0:
+            self._bcast(a, w_shard[:ncols], self._nk, self._bf16, sa, 1, sw_shard[:ncols], 1,
+                        mc_ptr=self.mc, peer_ptrs=self.peers, ldc=self.N, col_off=n0)
+        if events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(cur)
+            events["gemm_done"] = ev
+        if self.handle is not None:
+            self.handle.barrier(channel=0, timeout_ms=10000)
+        return self.out
+
+    def close(self):
+        """Drop the symmetric-memory buffer (every rank, after the last call)."""
+        self.handle = None
+        self.out = None
