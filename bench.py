@@ -410,13 +410,17 @@ def run_sharded(args, rank, world, local_rank, flush):
         "scaling": "strong", "g": world, "shard_cols": ns,
         "output_bytes_per_gpu_sent": int(M5 * ns * 2) if world > 1 else 0,
     }
-    notes = {"multimem": "epilogue stores every tile into every rank's C through the NVLink "
-                         "multicast address (one multimem.st per 16 B), then a device-side barrier",
+    notes = {"multimem": "epilogue stages 128-byte row segments and stores them into every rank's "
+                         "C through the NVLink multicast address (multimem.st, 16 B each), then a "
+                         "device-side barrier",
              "peer-stores": "epilogue stores every 32x32 tile into every rank's C with one TMA "
                             "tile store per rank (peer pointers), then a device-side barrier",
              "local": "one GPU: the GEMM writes C directly"}
-    for key, use_mc in (("fused", False), ("fused_multimem", True)):
-        if key == "fused_multimem" and world == 1:
+    # "fused": the form the library picks for this rank count (TMA stores to
+    # each peer at 2 ranks, multicast from 4); "fused_alt": the other form.
+    auto_mc = world >= 4
+    for key, use_mc in (("fused", auto_mc), ("fused_alt", not auto_mc)):
+        if key == "fused_alt" and world == 1:
             continue
         fused = FusedShardedW8A8(M5, N5, K5, rank, world, dev, use_multicast=use_mc)
         r = measure(fused, 0)

@@ -240,23 +240,17 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 
   if (args.bcast) {
-    if (!row_ok) return;
-    // 16-byte vectors of this row's chunk: 8 (f32) or 4 (bf16) of them, as
-    // far as the chunk lies inside N (N is a multiple of 8 in this mode).
-    constexpr int kVecElems = OUT == ROUGE_B200_OUT_BF16 ? 8 : 4;
-    const int cols = min(32, args.N - col0);
-    const int nvec = cols / kVecElems;
-    const size_t esz = OUT == ROUGE_B200_OUT_BF16 ? 2 : 4;
-    const size_t off =
-        (static_cast<size_t>(row) * args.bld + static_cast<size_t>(args.col_off + col0)) * esz;
+    // Stage the chunk as row `lane` of the warp's line buffer: 32 rows of
+    // 128 bytes (one 64-column bf16 line, chunk pairs in its two halves, or
+    // one 32-column f32 line), 16-byte units XOR-swizzled by row.
+    // bcast_flush writes the buffer out along rows.
+    constexpr int kUnits = OUT == ROUGE_B200_OUT_BF16 ? 4 : 8;
+    const int ubase = OUT == ROUGE_B200_OUT_BF16 ? ((col0 >> 5) & 1) * 4 : 0;
+    const uint32_t rbase = smem_u32(buf) + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
-    for (int q = 0; q < 32 / kVecElems; ++q) {
-      if (q >= nvec) break;
-      const uint64_t p = reinterpret_cast<uint64_t>(args.bcast) + off + 16 * q;
-      asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p),
-                   "r"(o[4 * q]), "r"(o[4 * q + 1]), "r"(o[4 * q + 2]), "r"(o[4 * q + 3])
-                   : "memory");
-    }
+    for (int q = 0; q < kUnits; ++q)
+      st_shared_v4(rbase + ((static_cast<uint32_t>(ubase + q) ^ (static_cast<uint32_t>(lane) & 7u)) << 4),
+                   o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
     return;
   }
 
@@ -305,6 +299,32 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
   }
 }
 
+// Writes the warp's staged line buffer (see epilogue_chunk) to the
+// multicast address: line_col0 = first column of the 128-byte line,
+// `units` = mask of the staged 16-byte units. Each store instruction covers
+// 4 rows x 128 contiguous bytes (8 lanes per row).
+template <int OUT>
+__device__ __forceinline__ void bcast_flush(const GemmArgs &args, const uint8_t *buf, int row0,
+                                            int line_col0, uint32_t units, int lane) {
+  constexpr int kEpu = OUT == ROUGE_B200_OUT_BF16 ? 8 : 4;  // elements per 16-byte unit
+  constexpr size_t kEsz = OUT == ROUGE_B200_OUT_BF16 ? 2 : 4;
+  __syncwarp();
+  const int u = lane & 7;
+  const bool unit_ok = ((units >> u) & 1u) && line_col0 + u * kEpu < args.N;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    if (unit_ok && row0 + r < args.M) {
+      const uint4 v = ld_shared_v4(smem_u32(buf) + static_cast<uint32_t>(r) * 128u +
+                                   ((static_cast<uint32_t>(u) ^ (static_cast<uint32_t>(r) & 7u)) << 4));
+      const size_t off = (static_cast<size_t>(row0 + r) * args.bld +
+                          static_cast<size_t>(args.col_off + line_col0 + u * kEpu)) * kEsz;
+      multimem_st_v4(reinterpret_cast<uint64_t>(args.bcast) + off, v);
+    }
+  }
+  __syncwarp();
+}
+
 // One epilogue warp's share of one accumulator tile of `width` columns
 // (C columns col0 ..) held from TMEM column tcol: TMEM lanes
 // [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`.
@@ -333,17 +353,37 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   uint32_t va[32], vb[32];
   tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
   tmem_ld_wait_regs(va);
-  // staging buffer of this warp's seq-th chunk
-  auto buf = [&]() { return stage + (NBUF > 1 ? (seq++ & 1) * kStageBytes : 0); };
+  // staging buffer of this warp's seq-th chunk (the multicast output stages
+  // whole lines in the first buffer)
+  auto buf = [&]() {
+    return args.bcast ? stage : stage + (NBUF > 1 ? (seq++ & 1) * kStageBytes : 0);
+  };
+  // multicast output: flush after chunk c when its line is complete
+  uint32_t staged = 0;
+  auto after = [&](int c) {
+    if (!args.bcast) return;
+    const int cc = col0 + c * 32;
+    if (OUT == ROUGE_B200_OUT_BF16) {
+      staged |= ((cc >> 5) & 1) ? 0xF0u : 0x0Fu;
+      if (((cc >> 5) & 1) || c + 1 == c_end) {
+        bcast_flush<OUT>(args, stage, row0, cc & ~63, staged, lane);
+        staged = 0;
+      }
+    } else {
+      bcast_flush<OUT>(args, stage, row0, cc, 0xFFu, lane);
+    }
+  };
   for (int c = c_beg; c < c_end; c += 2) {
     if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
     epilogue_chunk<KIND, OUT, NBUF>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab,
                                     buf(), om, lane);
+    after(c);
     if (c + 1 < c_end) {
       tmem_ld_wait_regs(vb);
       if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
       epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
                                       sab, buf(), om, lane);
+      after(c + 1);
       if (c + 2 < c_end) tmem_ld_wait_regs(va);
     }
   }

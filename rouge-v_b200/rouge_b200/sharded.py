@@ -122,10 +122,10 @@ class FusedShardedW8A8:
     GEMM: every rank's output C[M][N] is a symmetric-memory buffer (one
     allocation per rank, mapped into every rank's address space), and the
     GEMM epilogue writes each tile of this rank's column block [n0, n1) into
-    every rank's C at once -- one multimem store per 16 bytes to the buffer's
-    NVLink multicast address (the NVSwitch replicates it to every GPU), or,
-    where the allocation has no multicast support, one store per rank
-    through the peer pointers. No separate exchange, no layout step: the
+    every rank's C at once -- either one TMA tile store per rank through the
+    peer pointers, or multimem stores (16 bytes each, staged so that every
+    store instruction covers whole 128-byte row segments) to the buffer's
+    NVLink multicast address, which the NVSwitch replicates to every GPU. No separate exchange, no layout step: the
     tiles land row-major at their final place. A device-side barrier across
     the ranks (signal pads, system scope) ends each call, after which every
     rank's C is complete.
@@ -134,7 +134,7 @@ class FusedShardedW8A8:
     """
 
     def __init__(self, M: int, N: int, K: int, rank: int, world: int, device, group=None,
-                 use_multicast: bool = True):
+                 use_multicast: Optional[bool] = None):
         import torch
         import torch.distributed as dist
         from . import OUT_BF16, B_NK, gemm_i8, gemm_i8_bcast
@@ -156,6 +156,11 @@ class FusedShardedW8A8:
         g = group if group is not None else dist.group.WORLD
         self.out = symm.empty((M, N), dtype=torch.bfloat16, device=self.device)
         self.handle = symm.rendezvous(self.out, g)
+        # Multicast sends each tile once whatever the rank count; peer TMA
+        # stores send it world - 1 times but move it in larger writes. At 2
+        # ranks the TMA form is faster, from 4 ranks on the multicast form.
+        if use_multicast is None:
+            use_multicast = world >= 4
         has_mc = use_multicast and bool(symm._SymmetricMemory.has_multicast_support(
             symm.DeviceType.CUDA, self.device.index or 0))
         # The handle's pointers address the start of each rank's allocation;
