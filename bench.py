@@ -441,6 +441,17 @@ def run_sharded(args, rank, world, local_rank, flush):
     res["nccl"] = r
     del sh
     res["e2e_tops"] = max(v["e2e_tops"] for k, v in res.items() if isinstance(v, dict))
+    # Roofline of the fused compute + collective step: the slower of the
+    # GEMM at the measured tensor peak and the NVLink ingress every GPU must
+    # receive ((g-1)/g of C) at the pool's measured 770 GB/s peer bandwidth.
+    ingress = M5 * N5 * 2 * (world - 1) / world
+    bound_ms = max(ops / world / (tc8 * 1e12), ingress / 770e9) * 1e3
+    res["roofline"] = {"bound_ms": round(bound_ms, 4),
+                       "bound": "nvlink ingress" if ingress / 770e9 > ops / world / (tc8 * 1e12)
+                       else "tensor",
+                       "ingress_bytes_per_gpu": int(ingress),
+                       "frac_fused": round(bound_ms / res["fused"]["total_ms"], 4),
+                       "peaks": "GEMM 2 x measured bf16; NVLink 770 GB/s measured peer copy"}
     return res
 
 
