@@ -214,21 +214,26 @@ __global__ void __launch_bounds__(kThreads) quant_i8_rows_kernel(const float *__
 }
 
 // One warp per row with the whole row in registers (VPL float4 per lane,
-// rows up to VPL * 128 elements): one coalesced read of the row, the
-// maximum by warp shuffles, the scale computed redundantly by every lane,
-// then the encode from registers. One CTA per SM owns a contiguous range of
-// rows; its warps take the range's rows one at a time from a shared-memory
-// counter, so every SM finishes within about one row-time of the others
-// whatever the row count. A warp claims its next row before it reads the
-// current one and asks L2 to prefetch it (cp.async.bulk.prefetch), so HBM
-// reads stay in flight while the warp waits and computes, without holding
-// registers or shared memory for them. No block-level synchronisation
-// after the counter is set up.
+// rows up to VPL * 128 elements), fed by bulk copies. One CTA per SM owns a
+// contiguous range of rows; its 12 warps take the range's rows one at a time
+// from a shared-memory counter, so every SM finishes within about one
+// row-time of the others. Each warp owns one shared-memory row slot: it
+// copies the slot into registers, claims its next row and (lane 0) starts
+// that row's cp.async.bulk into the same slot, then reduces (warp
+// shuffles), computes the scale in double exactly as the reference, and
+// encodes from registers while the copy runs -- so the warp's next row
+// streams in during its compute. The encode is branch-free (paired f32x2
+// instructions); words near a rounding tie are re-encoded in double
+// afterwards from a second read of their inputs. The time-bounded slot
+// waits report ROUGE_B200_ETIMEOUT through *err; a warp that gives up waits
+// (bounded) for its copy in flight before it exits.
 template <int VPL>
-__global__ void __launch_bounds__(VPL > 16 ? 384 : 512, 1)
-    quant_i8_rows_warp_kernel(const float *__restrict__ x, int rows, int cols,
-                              float *__restrict__ scales, int8_t *__restrict__ out, int pf) {
+__global__ void __launch_bounds__(384, 1)
+    quant_i8_rows_tma_kernel(const float *__restrict__ x, int rows, int cols,
+                             float *__restrict__ scales, int8_t *__restrict__ out, int *err) {
   static_assert(VPL >= 1 && VPL <= 32, "one bit per word of a lane in the fix-up mask");
+  extern __shared__ __align__(128) uint8_t qsm[];
+  __shared__ __align__(8) uint64_t bars[12];
   __shared__ int next_row;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -237,28 +242,56 @@ __global__ void __launch_bounds__(VPL > 16 ? 384 : 512, 1)
   const int per = rows / static_cast<int>(gridDim.x);
   const int extra = rows % static_cast<int>(gridDim.x);
   const int b = static_cast<int>(blockIdx.x);
-  const int r_end = b * per + min(b, extra) + per + (b < extra ? 1 : 0);
-  int r = b * per + min(b, extra) + warp;  // first row: static
-  if (threadIdx.x == 0) next_row = r - warp + static_cast<int>(blockDim.x >> 5);
+  const int r_beg = b * per + min(b, extra);
+  const int r_end = r_beg + per + (b < extra ? 1 : 0);
+  uint8_t *slot = qsm + static_cast<size_t>(warp) * row_bytes;
+  uint64_t *bar = &bars[warp];
+  if (threadIdx.x == 0) {
+    next_row = r_beg + static_cast<int>(blockDim.x >> 5);
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mbar_init(&bars[w], 1);
+    mbar_init_fence();
+  }
   __syncthreads();
-  for (; r < r_end;) {
-    int rn = 0;
-    if (lane == 0) {
-      rn = atomicAdd(&next_row, 1);
-      if (pf && rn < r_end) bulk_prefetch_l2(x + static_cast<size_t>(rn) * cols, row_bytes);
+  int r = r_beg + warp;
+  if (lane == 0 && r < r_end) {
+    mbar_arrive_expect_tx(bar, row_bytes);
+    bulk_load(slot, x + static_cast<size_t>(r) * cols, row_bytes, bar);
+  }
+  const volatile int never = 0;
+  uint32_t phase = 0;
+  bool in_flight = r < r_end;
+  while (r < r_end) {
+    const bool got = mbar_wait(bar, phase, &never);
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0 && err) atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
+      break;
     }
-    rn = __shfl_sync(0xffffffffu, rn, 0);
-    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols);
+    phase ^= 1u;
+    in_flight = false;
+    const float4 *row = reinterpret_cast<const float4 *>(slot);
     float4 v[VPL];
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       const int i = j * 32 + lane;
-      v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[j] = i < nvec ? row[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float amax = 0.0f;
 #pragma unroll
     for (int j = 0; j < VPL; ++j)
       amax = max3(amax, max3(fabsf(v[j].x), fabsf(v[j].y), fabsf(v[j].z)), fabsf(v[j].w));
+    // Every lane's copy of the slot is in registers (the maximum used all of
+    // it): the slot takes this warp's next row.
+    __syncwarp();
+    int rn = 0;
+    if (lane == 0) {
+      rn = atomicAdd(&next_row, 1);
+      if (rn < r_end) {
+        mbar_arrive_expect_tx(bar, row_bytes);
+        bulk_load(slot, x + static_cast<size_t>(rn) * cols, row_bytes, bar);
+      }
+    }
+    rn = __shfl_sync(0xffffffffu, rn, 0);
+    in_flight = rn < r_end;
 #pragma unroll
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     // quant_int8.cpp:82-84: scale and its reciprocal in double.
@@ -269,11 +302,7 @@ __global__ void __launch_bounds__(VPL > 16 ? 384 : 512, 1)
     const bool exact_row = isinf(inv_f);
     if (lane == 0) scales[r] = s;
     uint32_t *orow = reinterpret_cast<uint32_t *>(out + static_cast<size_t>(r) * cols);
-    // Branch-free encode of every word (independent chains the scheduler
-    // can interleave); words near a tie are left out and marked, then
-    // re-encoded in double from a second read of their inputs (rare: about
-    // one word in 500, or every word of a row whose reciprocal scale
-    // overflows f32).
+    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<size_t>(r) * cols);
     uint32_t redo = 0;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
@@ -292,6 +321,7 @@ __global__ void __launch_bounds__(VPL > 16 ? 384 : 512, 1)
     }
     r = rn;
   }
+  if (in_flight && lane == 0) mbar_wait(bar, phase, &never);  // let the last copy land
 }
 
 // Row pipeline through shared memory: thread 0 keeps `stages` rows in
@@ -684,6 +714,26 @@ int resident_ctas(K kernel, int &cache) {
   return cache * current_sm_count();
 }
 
+// One CTA of 12 warps per SM (grid), 12 row slots of shared memory; the
+// shared-memory opt-in is set once per device and kernel instance.
+template <int VPL>
+int launch_quant_tma(const float *x, int rows, int cols, float *scales, int8_t *out, int grid,
+                     cudaStream_t st) {
+  constexpr int kWarps = 12;
+  auto kern = quant_i8_rows_tma_kernel<VPL>;
+  static std::atomic<unsigned long long> attr_done{0};
+  const unsigned long long bit = 1ull << (current_device() & 63);
+  if (!(attr_done.load() & bit)) {
+    int s = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kWarps * VPL * 128 * 4));
+    if (s != ROUGE_B200_OK) return s;
+    attr_done.fetch_or(bit);
+  }
+  kern<<<grid, 32 * kWarps, kWarps * cols * 4, st>>>(x, rows, cols, scales, out,
+                                                      device_error_word());
+  return cuda_status(cudaGetLastError());
+}
+
 int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8_t *out,
                          cudaStream_t st) {
   static int occ4 = 0, occ8 = 0;
@@ -691,24 +741,11 @@ int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8
   const size_t row_bytes = static_cast<size_t>(cols) * 4;
   const int sms = current_sm_count();
   if (nvec <= 1024 && rows >= 2 * sms) {
-    // Warp per row, row in registers: one CTA per SM, 12 warps (rows up to
-    // 4096 elements) or 16 warps.
-#ifndef RB200_QUANT_WARPS  // warps per CTA and L2 prefetch overrides for tuning builds
-#define RB200_QUANT_WARPS 0
-#endif
-#ifndef RB200_QUANT_PF
-#define RB200_QUANT_PF 1
-#endif
+    // Bulk-copy-fed warps: one CTA of 12 warps per SM, one row slot each.
     const int grid = std::min(sms, rows);
-    const int pf = RB200_QUANT_PF;
-    const int wq = RB200_QUANT_WARPS;
-    if (nvec <= 256)
-      quant_i8_rows_warp_kernel<8><<<grid, wq ? 32 * wq : 512, 0, st>>>(x, rows, cols, scales, out, pf);
-    else if (nvec <= 512)
-      quant_i8_rows_warp_kernel<16><<<grid, wq ? 32 * wq : 512, 0, st>>>(x, rows, cols, scales, out, pf);
-    else
-      quant_i8_rows_warp_kernel<32><<<grid, wq ? 32 * wq : 384, 0, st>>>(x, rows, cols, scales, out, pf);
-    return cuda_status(cudaGetLastError());
+    if (nvec <= 256) return launch_quant_tma<8>(x, rows, cols, scales, out, grid, st);
+    if (nvec <= 512) return launch_quant_tma<16>(x, rows, cols, scales, out, grid, st);
+    return launch_quant_tma<32>(x, rows, cols, scales, out, grid, st);
   }
   if (row_bytes <= 32768) {
     // Shared-memory row pipeline: 64 KB of rows in flight per CTA (96 KB
