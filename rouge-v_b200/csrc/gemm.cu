@@ -454,6 +454,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above overlaps the previous kernel's tail when this launch
+  // is programmatically serialised; its outputs (A, the scales) are read
+  // only after this point.
+  grid_dependency_wait();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -698,6 +702,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised, both TMEM allocations done
   tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above overlaps the previous kernel's tail when this launch
+  // is programmatically serialised; its outputs (A, the scales) are read
+  // only after this point.
+  grid_dependency_wait();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -906,22 +914,33 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
       attr_done.fetch_or(bit);
     }
     const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-    kern<<<grid, kGemmThreads, C::SMEM, st>>>(ta, tb, tc, args);
-    return cuda_status(cudaGetLastError());
-  } else {
-    using C = Cfg2<KIND, BN, B_MN>;
-    auto kern = gemm_tc2_kernel<KIND, BN, B_MN, OUT, CONV>;
     cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(kGemmThreads, 1, 1);
     cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
+  } else {
+    using C = Cfg2<KIND, BN, B_MN>;
+    auto kern = gemm_tc2_kernel<KIND, BN, B_MN, OUT, CONV>;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kGemmThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     // Per device: the shared-memory opt-in, then how many 2-CTA clusters of
     // this kernel fit on the GPU at once (SM pairs of one TPC).
     static std::atomic<unsigned long long> attr_done{0};

@@ -181,6 +181,22 @@ __device__ __forceinline__ void multimem_st_v4(uint64_t addr, uint4 v) {
                : "memory");
 }
 
+// ------------------------------------------- programmatic dependent launch
+//
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream is still running; it must call
+// grid_dependency_wait before touching anything that kernel writes (the
+// wait returns at once when the previous kernel did not allow an early
+// start). grid_launch_dependents lets the next such kernel start early.
+
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {

@@ -246,6 +246,9 @@ __global__ void __launch_bounds__(384, 1)
   const int r_end = r_beg + per + (b < extra ? 1 : 0);
   uint8_t *slot = qsm + static_cast<size_t>(warp) * row_bytes;
   uint64_t *bar = &bars[warp];
+  // The GEMM that consumes these codes may start its prologue now; it waits
+  // for this grid's completion before it reads them.
+  grid_launch_dependents();
   if (threadIdx.x == 0) {
     next_row = r_beg + static_cast<int>(blockDim.x >> 5);
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mbar_init(&bars[w], 1);
