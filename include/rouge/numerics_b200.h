@@ -281,6 +281,31 @@ int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
                        const float *scales_b, int b_cols, void *C, int ldc,
                        int out_type, void *stream);
 
+/* Column-major BLAS GEMM (the semantics of cublasSgemm / cublasGemmEx; the
+ * reference implements them on its CPU GEMM, cublas_shim.cpp:36-65,199-211):
+ *   C (m x n, column-major, ldc) = alpha * op(A) * op(B) + beta * C
+ * transa / transb: 0 = N, 1 = T. Operand type ab_type (A and B alike) and
+ * output c_type:
+ *   F32  -> F32  tf32 tensor cores with split operands (3xTF32: hi*hi +
+ *                hi*lo + lo*hi), f32-accurate
+ *   F16 / BF16 / E4M3 -> F32   f32 accumulation
+ *   I8   -> I32  exact int32 (alpha must be 1, beta 0)
+ * The operands are packed (transposed as needed) into `workspace`
+ * (256-byte aligned, at least rouge_b200_gemm_colmajor_workspace bytes;
+ * ROUGE_B200_ETOOBIG otherwise). beta == 0 never reads C. Asynchronous on
+ * `stream`. Device pointers. */
+#define ROUGE_B200_T_F32 0
+#define ROUGE_B200_T_F16 1
+#define ROUGE_B200_T_BF16 2
+#define ROUGE_B200_T_E4M3 3
+#define ROUGE_B200_T_I8 4
+#define ROUGE_B200_T_I32 5
+size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k);
+int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type,
+                             float alpha, const void *A, int lda, const void *B, int ldb,
+                             float beta, void *C, int c_type, int ldc, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
 /* rouge_b200_gemm_i8 with its output broadcast to every GPU of a sharded
  * job (no reference counterpart: the reference has no multi-GPU code; this
  * is the all-gather of the N-sharded W8A8 GEMM fused into the epilogue).

@@ -1,0 +1,199 @@
+// Column-major BLAS GEMM on the tcgen05 kernels (the semantics of
+// cublasSgemm / cublasGemmEx, which the reference implements on its CPU
+// GEMM in cublas_shim.cpp:36-65,199-211):
+//     C (m x n, column-major, ldc) = alpha * op(A) * op(B) + beta * C
+// The row-major kernels compute the transposed triple C^T = op(B)^T op(A)^T
+// straight into C's memory (a column-major m x n matrix with pitch ldc is a
+// row-major n x m matrix with pitch ldc):
+//     A' [n][Kp]  row j = column j of op(B)         (the kernel's A, K-major)
+//     B' [m][Kp]  row i = row i of op(A)            (the kernel's B, K-major)
+// Both are packed into a caller-provided workspace by one transposing copy
+// (16-byte aligned, K padded with zeros to the kernel's pitch), whatever the
+// transposes and leading dimensions. f32 operands are split for "3xTF32":
+// A' = [B_hi | B_hi | B_lo], B' = [A_hi | A_lo | A_hi] along K (hi = tf32
+// round-to-nearest of x, lo = x - hi), so one tf32 GEMM over 3 Kp
+// accumulates hi*hi + hi*lo + lo*hi, f32-accurate.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "runtime.cuh"
+
+namespace rb200 {
+
+int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
+                     long long ldb, int b_layout, float alpha, float beta, float *Cp,
+                     long long ldc, cudaStream_t st);
+int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
+                   long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
+                   int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st);
+
+namespace {
+
+constexpr int kT = 32;
+
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// out[r][p] (row pitch kp_out elements of T) = src[r * sr + p * sp] for
+// r < R, p < K, zero for K <= p < Kp. split: 0 plain copy; 1 f32 as
+// [hi | hi | lo]; 2 f32 as [hi | lo | hi] (blocks of Kp). 32 x 32 tiles
+// through shared memory, read along whichever of r / p is contiguous.
+template <class T>
+__global__ void pack_kernel(const T *__restrict__ src, long long sr, long long sp, int R, int K,
+                            int Kp, int split, T *__restrict__ out, long long kp_out) {
+  __shared__ T t[kT][kT + 1];
+  const int r0 = blockIdx.y * kT, p0 = blockIdx.x * kT;
+  const bool along_r = sr == 1;  // source contiguous along r: read by r, write by p
+  for (int i = threadIdx.y; i < kT; i += blockDim.y) {
+    const int r = along_r ? r0 + threadIdx.x : r0 + i;
+    const int p = along_r ? p0 + i : p0 + threadIdx.x;
+    T v = T(0);
+    if (r < R && p < K) v = src[r * sr + p * sp];
+    if (along_r)
+      t[threadIdx.x][i] = v;
+    else
+      t[i][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < kT; i += blockDim.y) {
+    const int r = r0 + i, p = p0 + threadIdx.x;
+    if (r >= R || p >= Kp) continue;
+    const T v = t[i][threadIdx.x];
+    T *row = out + r * kp_out;
+    if constexpr (sizeof(T) == 4) {
+      if (split) {
+        const float x = __int_as_float(static_cast<int>(v));
+        const float hi = tf32_round(x);
+        const float lo = x - hi;
+        row[p] = static_cast<T>(__float_as_int(hi));
+        row[Kp + p] = static_cast<T>(__float_as_int(split == 1 ? hi : lo));
+        row[2 * Kp + p] = static_cast<T>(__float_as_int(split == 1 ? lo : hi));
+        continue;
+      }
+    }
+    row[p] = v;
+  }
+}
+
+// C (m x n column-major, ldc) = beta * C, zero when beta == 0 (k == 0 or
+// alpha == 0: no product to add).
+__global__ void scale_kernel(float *C, int m, int n, long long ldc, float beta) {
+  const long long total = static_cast<long long>(m) * n;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float *c = C + (i / m) * ldc + i % m;
+    *c = beta == 0.0f ? 0.0f : beta * *c;
+  }
+}
+
+template <class T>
+int pack(const void *src, long long sr, long long sp, int R, int K, int Kp, int split, void *out,
+         long long kp_out, cudaStream_t st) {
+  const dim3 grid((Kp + kT - 1) / kT, (R + kT - 1) / kT);
+  pack_kernel<T><<<grid, dim3(kT, 8), 0, st>>>(static_cast<const T *>(src), sr, sp, R, K, Kp, split,
+                                                 static_cast<T *>(out), kp_out);
+  return cuda_status(cudaGetLastError());
+}
+
+size_t rup(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int esize_of(int type) {
+  switch (type) {
+    case ROUGE_B200_T_E4M3: case ROUGE_B200_T_I8: return 1;
+    case ROUGE_B200_T_F16: case ROUGE_B200_T_BF16: return 2;
+    case ROUGE_B200_T_F32: return 4;
+    default: return 0;
+  }
+}
+
+// Padded K (elements): 16-byte rows for every type, and the kernel's
+// 128-byte k-block for f32 so that the three split blocks stay aligned.
+int padded_k(int type, int k) {
+  const int es = esize_of(type);
+  return static_cast<int>(rup(k, type == ROUGE_B200_T_F32 ? 32 : 16 / es));
+}
+
+}  // namespace
+}  // namespace rb200
+
+using namespace rb200;
+
+extern "C" {
+
+size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k) {
+  const int es = esize_of(ab_type);
+  if (!es || m <= 0 || n <= 0 || k <= 0) return 0;
+  const size_t kp = padded_k(ab_type, k) * (ab_type == ROUGE_B200_T_F32 ? 3 : 1);
+  return rup(static_cast<size_t>(n) * kp * es, 256) + rup(static_cast<size_t>(m) * kp * es, 256);
+}
+
+int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
+                             const void *A, int lda, const void *B, int ldb, float beta, void *C,
+                             int c_type, int ldc, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  const int es = esize_of(ab_type);
+  if (!es || (transa != 0 && transa != 1) || (transb != 0 && transb != 1))
+    return set_status(ROUGE_B200_EINVAL);
+  if (m < 0 || n < 0 || k < 0 || ldc < (m > 1 ? m : 1)) return set_status(ROUGE_B200_EINVAL);
+  // op(A) is m x k: stored k x m when transposed; op(B) is k x n.
+  if (lda < ((transa ? k : m) > 1 ? (transa ? k : m) : 1) ||
+      ldb < ((transb ? n : k) > 1 ? (transb ? n : k) : 1))
+    return set_status(ROUGE_B200_EINVAL);
+  const bool int8 = ab_type == ROUGE_B200_T_I8;
+  if (int8 ? c_type != ROUGE_B200_T_I32 : c_type != ROUGE_B200_T_F32)
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  if (int8 && (alpha != 1.0f || beta != 0.0f)) return set_status(ROUGE_B200_EUNSUPPORTED);
+  if (m == 0 || n == 0) return ROUGE_B200_OK;
+  if (!C || (k > 0 && (!A || !B))) return set_status(ROUGE_B200_EINVAL);
+  int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  cudaStream_t st = as_stream(stream);
+  if (k == 0 || (!int8 && alpha == 0.0f)) {
+    if (int8) return cuda_status(cudaMemset2DAsync(C, static_cast<size_t>(ldc) * 4, 0,
+                                                   static_cast<size_t>(m) * 4, n, st));
+    scale_kernel<<<512, 256, 0, st>>>(static_cast<float *>(C), m, n, ldc, beta);
+    return cuda_status(cudaGetLastError());
+  }
+  if (!workspace || workspace_bytes < rouge_b200_gemm_colmajor_workspace(ab_type, m, n, k) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return set_status(ROUGE_B200_ETOOBIG);
+  const int Kp = padded_k(ab_type, k);
+  const bool f32 = ab_type == ROUGE_B200_T_F32;
+  const long long kp_row = static_cast<long long>(Kp) * (f32 ? 3 : 1);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  void *Ap = ws;                                                      // A' [n][kp_row]
+  void *Bp = ws + rup(static_cast<size_t>(n) * kp_row * es, 256);     // B' [m][kp_row]
+  // A'[j][p] = op(B)[p][j]: B[p + j*ldb] (N) or B[j + p*ldb] (T).
+  const long long a_sr = transb ? 1 : ldb, a_sp = transb ? ldb : 1;
+  // B'[i][p] = op(A)[i][p]: A[i + p*lda] (N) or A[p + i*lda] (T).
+  const long long b_sr = transa ? lda : 1, b_sp = transa ? 1 : lda;
+  switch (es) {
+    case 1:
+      s = pack<uint8_t>(B, a_sr, a_sp, n, k, Kp, 0, Ap, kp_row, st);
+      if (s == ROUGE_B200_OK) s = pack<uint8_t>(A, b_sr, b_sp, m, k, Kp, 0, Bp, kp_row, st);
+      break;
+    case 2:
+      s = pack<uint16_t>(B, a_sr, a_sp, n, k, Kp, 0, Ap, kp_row, st);
+      if (s == ROUGE_B200_OK) s = pack<uint16_t>(A, b_sr, b_sp, m, k, Kp, 0, Bp, kp_row, st);
+      break;
+    default:
+      s = pack<uint32_t>(B, a_sr, a_sp, n, k, Kp, 1, Ap, kp_row, st);
+      if (s == ROUGE_B200_OK) s = pack<uint32_t>(A, b_sr, b_sp, m, k, Kp, 2, Bp, kp_row, st);
+      break;
+  }
+  if (s != ROUGE_B200_OK) return s;
+  if (int8)
+    return launch_gemm_i8(n, m, static_cast<int>(kp_row), static_cast<const int8_t *>(Ap), kp_row,
+                          static_cast<const int8_t *>(Bp), kp_row, ROUGE_B200_B_NK, nullptr, 0,
+                          nullptr, 0, C, ldc, ROUGE_B200_OUT_I32, st);
+  const int kind = ab_type == ROUGE_B200_T_E4M3 ? 0 : ab_type == ROUGE_B200_T_F16 ? 1
+                   : ab_type == ROUGE_B200_T_BF16 ? 2 : 3;
+  return launch_gemm_blas(kind, n, m, static_cast<int>(kp_row), Ap, kp_row, Bp, kp_row,
+                          ROUGE_B200_B_NK, alpha, beta, static_cast<float *>(C), ldc, st);
+}
+
+}  // extern "C"

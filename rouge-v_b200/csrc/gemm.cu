@@ -64,6 +64,10 @@ struct GemmArgs {
   int npeers;
   int col_off;
   long long bld;
+  // BLAS epilogue (f32 output of the f16 / tf32 / e4m3 kinds, blas != 0):
+  // C = alpha * acc + beta * C; the old C is read only when beta != 0.
+  int blas;
+  float alpha, beta;
   // Implicit-GEMM convolution (A gathered by im2col TMA): M = N*OH*OW
   // output pixels, K = KH*KW*Cin ordered (kr, kc, c), k-block = one filter
   // tap x 64 channels.
@@ -222,6 +226,28 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
 #pragma unroll
       for (int j = 0; j < 32; j += 2)
         mul2(f[j], f[j + 1], __uint_as_float(v[j]), __uint_as_float(v[j + 1]), sab);
+    }
+    // BLAS form C = alpha * acc + beta * C (f32 output): sab holds alpha; the
+    // old C is read only when beta != 0 (it need not be valid otherwise).
+    if constexpr (OUT == ROUGE_B200_OUT_F32 && KIND != MmaKind::I8) {
+      if (args.blas && args.beta != 0.0f && row_ok) {
+        const float *crow = static_cast<const float *>(args.C) + static_cast<long long>(row) * args.ldc;
+        const bool whole = col0 + 32 <= args.N && (args.ldc % 4) == 0 &&
+                           (reinterpret_cast<uintptr_t>(args.C) & 15u) == 0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float c4[4];
+          if (whole) {
+            const float4 t = *reinterpret_cast<const float4 *>(crow + col0 + j);
+            c4[0] = t.x; c4[1] = t.y; c4[2] = t.z; c4[3] = t.w;
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) c4[q] = col0 + j + q < args.N ? crow[col0 + j + q] : 0.0f;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) f[j + q] = __fmaf_rn(args.beta, c4[q], f[j + q]);
+        }
+      }
     }
     if constexpr (OUT == ROUGE_B200_OUT_F32) {
 #pragma unroll
@@ -567,6 +593,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
+      if (args.blas) sab = args.alpha;
     }
     for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
       int mb, nb;
@@ -832,6 +859,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
+      if (args.blas) sab = args.alpha;
     }
     for (int t = cluster; t < args.num_tiles; t += nclusters, ++local) {
       int mb, nb, part, parts;
@@ -1251,6 +1279,36 @@ int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const
   g.use_tma_store = vec_ok(Cp, ldc, out_type);
   g.err = device_error_word();
   return launch_kind<MmaKind::F16>(A, lda, B, ldb, b_layout, g, out_type, st);
+}
+
+// BLAS-form GEMM on the f16 / bf16 / tf32 / e4m3 kinds:
+// C[M][N] (f32, row pitch ldc) = alpha * A[M][K] . B^T + beta * C, A K-major
+// (row pitch lda), B per b_layout (tf32 needs ROUGE_B200_B_NK).
+// kind: 0 e4m3, 1 f16, 2 bf16, 3 tf32.
+int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
+                     long long ldb, int b_layout, float alpha, float beta, float *Cp,
+                     long long ldc, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.blas = 1;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.bf16 = kind == 2 ? 1 : 0;
+  g.use_tma_store = vec_ok(Cp, ldc, ROUGE_B200_OUT_F32);
+  g.err = device_error_word();
+  switch (kind) {
+    case 0:
+      return launch_kind<MmaKind::F8F6F4>(A, lda, B, ldb, b_layout, g, ROUGE_B200_OUT_F32, st);
+    case 1:
+    case 2:
+      return launch_kind<MmaKind::F16>(A, lda, B, ldb, b_layout, g, ROUGE_B200_OUT_F32, st);
+    case 3:
+      if (b_layout != ROUGE_B200_B_NK) return set_status(ROUGE_B200_EUNSUPPORTED);
+      return launch_kind<MmaKind::TF32>(A, lda, B, ldb, b_layout, g, ROUGE_B200_OUT_F32, st);
+    default:
+      return set_status(ROUGE_B200_EINVAL);
+  }
 }
 
 }  // namespace rb200

@@ -106,3 +106,22 @@ def test_synth_is_deterministic_and_distributed(rb):
     x = np.ones(1 << 20, np.float32)
     n = rb.synth_outliers(1, x, 0.01, 20.0)
     assert abs(n / x.size - 0.01) < 1e-3 and (x == 20.0).sum() == n
+
+
+def test_cublas_shim_exports_declared_api():
+    import ctypes as C
+    import os
+    import re
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    L = C.CDLL(os.path.join(root, "rouge-v_b200", "lib", "librouge_b200_cublas.so"))
+    text = open(os.path.join(root, "include", "rouge", "cublas_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = sorted(set(re.findall(r"\b(cublas\w+)\s*\(", text)))
+    assert len(names) >= 11
+    for n in names:
+        assert hasattr(L, n), n
+    h = C.c_void_p()
+    # without an sm_100 device the handle cannot be created (no CPU fallback)
+    import torch
+    if not torch.cuda.is_available():
+        assert L.cublasCreate_v2(C.byref(h)) == 1   # CUBLAS_STATUS_NOT_INITIALIZED
