@@ -566,6 +566,44 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
         "frac_of_bf16_peak": round(fl / (t * 1e-3) / 1e12 / tc16, 4),
         "rel_l2_first_256_pixels": err,
         "kernel": "gemm_tc2_kernel<F16, conv> (2-CTA pairs, im2col TMA A, fused bias)"}
+    del xd, wd, y
+
+    # cuBLAS-API shim: cublasSgemm_v2 (f32, 3xTF32 on tcgen05) at 8192^3,
+    # against torch's own f32 matmul (cuBLAS SGEMM, TF32 off) on the same data
+    import ctypes as C_
+    shim = C_.CDLL(os.path.join(ROOT, "rouge-v_b200", "lib", "librouge_b200_cublas.so"))
+    h = C_.c_void_p()
+    if shim.cublasCreate_v2(C_.byref(h)) == 0:
+        shim.cublasSetStream_v2(h, C_.c_void_p(torch.cuda.current_stream().cuda_stream))
+        ns = 8192
+        As = torch.randn((ns, ns), device=dev)
+        Bs = torch.randn((ns, ns), device=dev)
+        Cs = torch.empty((ns, ns), device=dev)
+        one, zero = C_.c_float(1.0), C_.c_float(0.0)
+
+        def sgemm():
+            st = shim.cublasSgemm_v2(h, 0, 0, ns, ns, ns, C_.byref(one), C_.c_void_p(As.data_ptr()),
+                                     ns, C_.c_void_p(Bs.data_ptr()), ns, C_.byref(zero),
+                                     C_.c_void_p(Cs.data_ptr()), ns)
+            assert st == 0, st
+        t_s = time_launch(torch, sgemm, flush)
+        prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+        torch.backends.cuda.matmul.allow_tf32 = False
+        Ct = torch.empty_like(Cs)
+        t_t = time_launch(torch, lambda: torch.matmul(Bs, As, out=Ct), flush)  # same column-major product
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+        rows = torch.arange(0, ns, 1024, device=dev)
+        ref = (Bs[rows].double() @ As.double())          # rows of the row-major view = columns of C
+        err = float((Cs[rows].double() - ref).norm() / ref.norm())
+        fl = 2.0 * ns ** 3
+        out["cublas_shim_sgemm_8192"] = {
+            "ms": round(t_s, 4), "tflops": round(fl / (t_s * 1e-3) / 1e12, 1),
+            "torch_f32_matmul_ms": round(t_t, 4),
+            "torch_f32_matmul_tflops": round(fl / (t_t * 1e-3) / 1e12, 1),
+            "rel_l2_sampled_columns_vs_f64": err,
+            "kernel": "pack (hi/lo split) + gemm_tc2_kernel<TF32> over 3K (3xTF32)"}
+        del As, Bs, Cs, Ct
+        shim.cublasDestroy_v2(h)
     return out
 
 
