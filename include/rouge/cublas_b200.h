@@ -6,8 +6,11 @@
  * on its CPU GEMM, so that programs written against cuBLAS run unchanged.
  * This library exports the same API names with the same argument meaning
  * and status codes, computing on the sm_100a tensor-core kernels of
- * librouge_b200.so (through rouge_b200_gemm_colmajor). Pointers are device
- * pointers; calls are asynchronous on the handle's stream, as in cuBLAS.
+ * librouge_b200.so (through rouge_b200_gemm_colmajor). Device pointers are
+ * used in place and calls are asynchronous on the handle's stream, as in
+ * cuBLAS. Host pointers (the memory the reference's CPU shim works on) are
+ * accepted too: those operands are copied to the device and the result
+ * back, and the call returns when done.
  *
  * Covered: handle management, streams, pointer mode, cublasSgemm_v2 and
  * cublasSgemmStridedBatched (f32 on tf32 tensor cores with split operands,

@@ -352,6 +352,32 @@ int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, i
                                int stride, int pad, const uint16_t *X, const uint16_t *Wt,
                                const float *bias, float *Y, int is_bf16, void *stream);
 
+/* Convolution forward with cuDNN's semantics (the operation the reference
+ * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU
+ * conv): Y = alpha * conv(X, Wt) + beta * Y, cross-correlation, symmetric
+ * stride and zero padding, OH = (H + 2*pad - KH)/stride + 1. X, Wt and Y
+ * are device arrays of one element type `type`: ROUGE_B200_T_F32 (tf32
+ * tensor cores with split operands, f32-accurate), ROUGE_B200_T_F16 or
+ * ROUGE_B200_T_BF16 (f32 accumulation, result rounded to nearest even).
+ * Layouts: X [N][Cin][H][W] (NCHW) or [N][H][W][Cin] (NHWC); Wt
+ * [Cout][Cin][KH][KW] (NCHW) or [Cout][KH][KW][Cin] (NHWC); Y likewise.
+ * Y is read only when beta != 0. Workspace: at least
+ * rouge_b200_conv2d_forward_workspace(...) bytes, 256-byte aligned (0 for
+ * 16-bit NHWC data with Cin % 64 == 0, Cout % 8 == 0, X of at least
+ * 128 KB and 16-byte aligned pointers: the kernel then reads X and Wt as
+ * they are and writes Y from its epilogue); too little -> ROUGE_B200_ETOOBIG.
+ * Limits (EUNSUPPORTED): pad <= 128, KH, KW <= min(256, pad + 129),
+ * stride <= 8. Asynchronous on `stream`. */
+#define ROUGE_B200_NCHW 0
+#define ROUGE_B200_NHWC 1
+size_t rouge_b200_conv2d_forward_workspace(int N, int Cin, int H, int W, int Cout, int KH, int KW,
+                                           int stride, int pad, int type, int x_layout,
+                                           int w_layout, int y_layout);
+int rouge_b200_conv2d_forward(int N, int Cin, int H, int W, int Cout, int KH, int KW, int stride,
+                              int pad, int type, float alpha, const void *X, int x_layout,
+                              const void *Wt, int w_layout, float beta, void *Y, int y_layout,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
 /* N-sharded GEMM, layout step after the all-gather:
  * rank r of g owns output columns [r*ns, (r+1)*ns); shards gathered in
  * bands of R rows arrive as src[M/R][g][R][ns]; this writes them to

@@ -17,6 +17,7 @@
 
 #include <cstdint>
 
+#include "pack.cuh"
 #include "runtime.cuh"
 
 namespace rb200 {
@@ -29,55 +30,6 @@ int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const in
                    int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st);
 
 namespace {
-
-constexpr int kT = 32;
-
-__device__ __forceinline__ float tf32_round(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-// out[r][p] (row pitch kp_out elements of T) = src[r * sr + p * sp] for
-// r < R, p < K, zero for K <= p < Kp. split: 0 plain copy; 1 f32 as
-// [hi | hi | lo]; 2 f32 as [hi | lo | hi] (blocks of Kp). 32 x 32 tiles
-// through shared memory, read along whichever of r / p is contiguous.
-template <class T>
-__global__ void pack_kernel(const T *__restrict__ src, long long sr, long long sp, int R, int K,
-                            int Kp, int split, T *__restrict__ out, long long kp_out) {
-  __shared__ T t[kT][kT + 1];
-  const int r0 = blockIdx.y * kT, p0 = blockIdx.x * kT;
-  const bool along_r = sr == 1;  // source contiguous along r: read by r, write by p
-  for (int i = threadIdx.y; i < kT; i += blockDim.y) {
-    const int r = along_r ? r0 + threadIdx.x : r0 + i;
-    const int p = along_r ? p0 + i : p0 + threadIdx.x;
-    T v = T(0);
-    if (r < R && p < K) v = src[r * sr + p * sp];
-    if (along_r)
-      t[threadIdx.x][i] = v;
-    else
-      t[i][threadIdx.x] = v;
-  }
-  __syncthreads();
-  for (int i = threadIdx.y; i < kT; i += blockDim.y) {
-    const int r = r0 + i, p = p0 + threadIdx.x;
-    if (r >= R || p >= Kp) continue;
-    const T v = t[i][threadIdx.x];
-    T *row = out + r * kp_out;
-    if constexpr (sizeof(T) == 4) {
-      if (split) {
-        const float x = __int_as_float(static_cast<int>(v));
-        const float hi = tf32_round(x);
-        const float lo = x - hi;
-        row[p] = static_cast<T>(__float_as_int(hi));
-        row[Kp + p] = static_cast<T>(__float_as_int(split == 1 ? hi : lo));
-        row[2 * Kp + p] = static_cast<T>(__float_as_int(split == 1 ? lo : hi));
-        continue;
-      }
-    }
-    row[p] = v;
-  }
-}
 
 // C (m x n column-major, ldc) = beta * C, zero when beta == 0 (k == 0 or
 // alpha == 0: no product to add).
@@ -93,10 +45,7 @@ __global__ void scale_kernel(float *C, int m, int n, long long ldc, float beta) 
 template <class T>
 int pack(const void *src, long long sr, long long sp, int R, int K, int Kp, int split, void *out,
          long long kp_out, cudaStream_t st) {
-  const dim3 grid((Kp + kT - 1) / kT, (R + kT - 1) / kT);
-  pack_kernel<T><<<grid, dim3(kT, 8), 0, st>>>(static_cast<const T *>(src), sr, sp, R, K, Kp, split,
-                                                 static_cast<T *>(out), kp_out);
-  return cuda_status(cudaGetLastError());
+  return pack_launch<T>(src, 0, sr, sp, R, K, Kp, split, out, 0, kp_out, 1, st);
 }
 
 size_t rup(size_t v, size_t a) { return (v + a - 1) / a * a; }

@@ -1,9 +1,11 @@
 // librouge_b200_cublas.so: the cuBLAS GEMM API subset of
 // include/rouge/cublas_b200.h on rouge_b200_gemm_colmajor (tcgen05 kernels).
 // The reference's shim (cublas_shim.cpp) keeps the same entry names and
-// statuses on its CPU GEMM; here the pointers are device pointers and the
-// work is queued on the handle's stream. Each handle owns a growable
-// device workspace for the packed operands.
+// statuses on its CPU GEMM; here device pointers are used in place and the
+// work is queued on the handle's stream, and host pointers (what the
+// reference's callers pass) are staged through device memory, the call
+// returning when the result is back. Each handle owns a growable device
+// workspace for the packed operands and one for staged host operands.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -13,6 +15,7 @@
 
 #include "rouge/cublas_b200.h"
 #include "rouge/numerics_b200.h"
+#include "shim_stage.h"
 
 struct rouge_b200_cublas_ctx {
   int magic;
@@ -20,6 +23,7 @@ struct rouge_b200_cublas_ctx {
   cublasPointerMode_t mode;
   void *ws;
   size_t ws_bytes;
+  rb200shim::DevBuf stage;
   std::mutex lock;
 };
 
@@ -75,15 +79,33 @@ bool ensure_ws(cublasHandle_t h, size_t bytes) {
   return true;
 }
 
+// Elements spanned by a column-major rows x cols matrix with pitch ld.
+size_t extent(int rows, int cols, int ld) {
+  return rows <= 0 || cols <= 0 || ld < rows ? 0 : static_cast<size_t>(cols - 1) * ld + rows;
+}
+
+size_t esize_of(int t) {
+  return t == ROUGE_B200_T_F32 || t == ROUGE_B200_T_I32 ? 4
+         : t == ROUGE_B200_T_F16 || t == ROUGE_B200_T_BF16 ? 2 : 1;
+}
+
 cublasStatus_t gemm(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n,
                     int k, int ab_type, float alpha, const void *A, int lda, const void *B, int ldb,
                     float beta, void *C, int c_type, int ldc) {
   const size_t need = rouge_b200_gemm_colmajor_workspace(ab_type, m, n, k);
   if (need && !ensure_ws(h, need)) return CUBLAS_STATUS_ALLOC_FAILED;
-  const int s = rouge_b200_gemm_colmajor(ta == CUBLAS_OP_N ? 0 : 1, tb == CUBLAS_OP_N ? 0 : 1, m,
-                                         n, k, ab_type, alpha, A, lda, B, ldb, beta, C, c_type, ldc,
-                                         h->ws, h->ws_bytes, h->stream);
-  return map_status(s);
+  const bool an = ta == CUBLAS_OP_N, bn = tb == CUBLAS_OP_N;
+  rb200shim::Staging sg(h->stage, h->stream);
+  sg.add(A, extent(an ? m : k, an ? k : m, lda) * esize_of(ab_type), true, false);
+  sg.add(B, extent(bn ? k : n, bn ? n : k, ldb) * esize_of(ab_type), true, false);
+  sg.add(C, extent(m, n, ldc) * esize_of(c_type), beta != 0.0f, true);
+  if (!sg.begin()) return CUBLAS_STATUS_ALLOC_FAILED;
+  const int s = rouge_b200_gemm_colmajor(an ? 0 : 1, bn ? 0 : 1, m, n, k, ab_type, alpha, sg.dev(A),
+                                         lda, sg.dev(B), ldb, beta, sg.dev(C), c_type, ldc, h->ws,
+                                         h->ws_bytes, h->stream);
+  const bool ok = sg.finish();
+  if (s != ROUGE_B200_OK) return map_status(s);
+  return ok ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
 int ab_type_of(cudaDataType_t t) {
@@ -137,6 +159,7 @@ cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
     cudaStreamSynchronize(handle->stream);
     cudaFree(handle->ws);
   }
+  handle->stage.release(handle->stream);
   handle->magic = 0;
   delete handle;
   return CUBLAS_STATUS_SUCCESS;

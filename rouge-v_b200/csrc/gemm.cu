@@ -20,6 +20,7 @@
 // Tiles are walked in groups of 16 M-blocks so that the CTAs of one wave
 // share A and B panels in L2.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -64,10 +65,14 @@ struct GemmArgs {
   int npeers;
   int col_off;
   long long bld;
-  // BLAS epilogue (f32 output of the f16 / tf32 / e4m3 kinds, blas != 0):
-  // C = alpha * acc + beta * C; the old C is read only when beta != 0.
+  // BLAS epilogue (f32 or 16-bit output of the f16 / tf32 / e4m3 kinds,
+  // blas != 0): C = alpha * acc + beta * C; the old C is read only when
+  // beta != 0.
   int blas;
   float alpha, beta;
+  // 16-bit output (OUT_BF16 template) holds IEEE half instead of bf16
+  // (cuDNN HALF tensors): hardware round to nearest even.
+  int f16out;
   // Implicit-GEMM convolution (A gathered by im2col TMA): M = N*OH*OW
   // output pixels, K = KH*KW*Cin ordered (kr, kc, c), k-block = one filter
   // tap x 64 channels.
@@ -227,8 +232,37 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
       for (int j = 0; j < 32; j += 2)
         mul2(f[j], f[j + 1], __uint_as_float(v[j]), __uint_as_float(v[j + 1]), sab);
     }
-    // BLAS form C = alpha * acc + beta * C (f32 output): sab holds alpha; the
-    // old C is read only when beta != 0 (it need not be valid otherwise).
+    // BLAS form C = alpha * acc + beta * C: sab holds alpha; the old C is
+    // read only when beta != 0 (it need not be valid otherwise).
+    if constexpr (OUT == ROUGE_B200_OUT_BF16 && KIND != MmaKind::I8) {
+      if (args.blas && args.beta != 0.0f && row_ok) {
+        const uint16_t *crow =
+            static_cast<const uint16_t *>(args.C) + static_cast<long long>(row) * args.ldc;
+        const bool whole = col0 + 32 <= args.N && (args.ldc % 8) == 0 &&
+                           (reinterpret_cast<uintptr_t>(args.C) & 15u) == 0;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint32_t h[4];
+          if (whole) {
+            const uint4 t = *reinterpret_cast<const uint4 *>(crow + col0 + j);
+            h[0] = t.x; h[1] = t.y; h[2] = t.z; h[3] = t.w;
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int c = col0 + j + 2 * q;
+              h[q] = (c < args.N ? crow[c] : 0u) | ((c + 1 < args.N ? crow[c + 1] : 0u) << 16);
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint32_t bits = (h[q >> 1] >> ((q & 1) * 16)) & 0xFFFFu;
+            const float c = args.f16out ? __half2float(__ushort_as_half(static_cast<unsigned short>(bits)))
+                                        : __uint_as_float(bits << 16);
+            f[j + q] = __fmaf_rn(args.beta, c, f[j + q]);
+          }
+        }
+      }
+    }
     if constexpr (OUT == ROUGE_B200_OUT_F32 && KIND != MmaKind::I8) {
       if (args.blas && args.beta != 0.0f && row_ok) {
         const float *crow = static_cast<const float *>(args.C) + static_cast<long long>(row) * args.ldc;
@@ -252,6 +286,9 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
     if constexpr (OUT == ROUGE_B200_OUT_F32) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(f[j]);
+    } else if (args.f16out) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = f16x2_rn(f[2 * j], f[2 * j + 1]);
     } else {
 #pragma unroll
       for (int j = 0; j < 16; ++j) o[j] = bf16x2_rn(f[2 * j], f[2 * j + 1]);
@@ -1122,7 +1159,7 @@ int vec_ok(const void *Cp, long long ldc, int out_type) {
              : 0;
 }
 
-template <MmaKind KIND, int BN, bool PAIR>
+template <MmaKind KIND, int BN, bool PAIR, int OUT>
 int launch_conv_bn(const CUtensorMap &ta, const void *Wt, GemmArgs g, cudaStream_t st) {
   using C = Cfg<KIND, BN, false>;
   auto make_b = [&](int box_rows, CUtensorMap *tb) {
@@ -1131,7 +1168,7 @@ int launch_conv_bn(const CUtensorMap &ta, const void *Wt, GemmArgs g, cudaStream
                                       : CU_TENSOR_MAP_DATA_TYPE_UINT16,
                         g.K, g.N, static_cast<uint64_t>(g.K) * C::ESIZE, C::BK, box_rows);
   };
-  return launch_tiles<KIND, BN, false, ROUGE_B200_OUT_F32, true, PAIR>(ta, make_b, g, st);
+  return launch_tiles<KIND, BN, false, OUT, true, PAIR>(ta, make_b, g, st);
 }
 
 }  // namespace
@@ -1143,11 +1180,15 @@ int launch_conv_bn(const CUtensorMap &ta, const void *Wt, GemmArgs g, cudaStream
 // (kr, kc, c) order, so the weights [Cout][KH][KW][Cin] are the K-major B
 // operand as stored. The A tile of k-block (tap, c0) is one im2col TMA load:
 // 128 consecutive output pixels (crossing rows and images) x BK channels of
-// filter tap (kr, kc), zeros in the padding. Y has row pitch ldy >= Cout.
+// filter tap (kr, kc), zeros in the padding. Y has row pitch ldy >= Cout
+// and element type out_type: f32, or 16-bit (kind::f16 only) holding bf16
+// or, with f16out, IEEE half. blas != 0: Y = alpha * acc + beta * Y (no
+// bias), the old Y read only when beta != 0.
 template <MmaKind KIND>
 int launch_conv(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
-                const void *X, const void *Wt, const float *bias, float *Y, long long ldy,
-                int is_bf16, cudaStream_t st) {
+                const void *X, const void *Wt, const float *bias, void *Y, long long ldy,
+                int is_bf16, int out_type, int f16out, int blas, float alpha, float beta,
+                cudaStream_t st) {
   using C0 = Cfg<KIND, 128, false>;
   const int OH = (H + 2 * pad - KH) / stride + 1, OW = (W + 2 * pad - KW) / stride + 1;
   GemmArgs g{};
@@ -1159,7 +1200,11 @@ int launch_conv(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stri
   g.bf16 = is_bf16 ? 1 : 0;
   g.bias = bias;
   g.vec16 = (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
-  g.use_tma_store = vec_ok(Y, ldy, ROUGE_B200_OUT_F32);
+  g.use_tma_store = vec_ok(Y, ldy, out_type);
+  g.f16out = f16out;
+  g.blas = blas;
+  g.alpha = alpha;
+  g.beta = beta;
   g.err = device_error_word();
   g.conv_cblocks = Cin / C0::BK;
   g.conv_kw = KW;
@@ -1186,16 +1231,24 @@ int launch_conv(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stri
   g.num_n = (Cout + bn - 1) / bn;
   g.num_k = KH * KW * g.conv_cblocks;
   g.num_tiles = g.num_m * g.num_n;
-  if (pair) return launch_conv_bn<KIND, 256, true>(ta, Wt, g, st);
-  return bn == 256 ? launch_conv_bn<KIND, 256, false>(ta, Wt, g, st)
-                   : launch_conv_bn<KIND, 128, false>(ta, Wt, g, st);
+  if constexpr (KIND == MmaKind::F16) {
+    if (out_type == ROUGE_B200_OUT_BF16) {
+      if (pair) return launch_conv_bn<KIND, 256, true, ROUGE_B200_OUT_BF16>(ta, Wt, g, st);
+      return bn == 256 ? launch_conv_bn<KIND, 256, false, ROUGE_B200_OUT_BF16>(ta, Wt, g, st)
+                       : launch_conv_bn<KIND, 128, false, ROUGE_B200_OUT_BF16>(ta, Wt, g, st);
+    }
+  }
+  if (out_type != ROUGE_B200_OUT_F32) return set_status(ROUGE_B200_EUNSUPPORTED);
+  if (pair) return launch_conv_bn<KIND, 256, true, ROUGE_B200_OUT_F32>(ta, Wt, g, st);
+  return bn == 256 ? launch_conv_bn<KIND, 256, false, ROUGE_B200_OUT_F32>(ta, Wt, g, st)
+                   : launch_conv_bn<KIND, 128, false, ROUGE_B200_OUT_F32>(ta, Wt, g, st);
 }
 
 int launch_conv_f16(int N, int H, int W, int Cin, int Cout, int KH, int KW, int stride, int pad,
                     const uint16_t *X, const uint16_t *Wt, const float *bias, float *Y,
                     int is_bf16, cudaStream_t st) {
   return launch_conv<MmaKind::F16>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, bias, Y, Cout,
-                                   is_bf16, st);
+                                   is_bf16, ROUGE_B200_OUT_F32, 0, 0, 1.0f, 0.0f, st);
 }
 
 // f32 NHWC convolution with tf32 operands (Cin a multiple of 32, inputs of
@@ -1204,7 +1257,24 @@ int launch_conv_tf32(int N, int H, int W, int Cin, int Cout, int KH, int KW, int
                      const float *X, const float *Wt, const float *bias, float *Y, long long ldy,
                      cudaStream_t st) {
   return launch_conv<MmaKind::TF32>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, bias, Y, ldy,
-                                    0, st);
+                                    0, ROUGE_B200_OUT_F32, 0, 0, 1.0f, 0.0f, st);
+}
+
+// The cuDNN-forward form: Y (row pitch ldy, element type y_type: T_F32,
+// T_F16 or T_BF16) = alpha * conv(X, Wt) + beta * Y. ab_type T_F16 / T_BF16
+// (kind::f16, Cin % 64 == 0) or T_F32 (kind::tf32, Cin % 32 == 0; the
+// caller splits operands for f32 accuracy). Checked by the caller.
+int launch_conv_blas(int ab_type, int N, int H, int W, int Cin, int Cout, int KH, int KW,
+                     int stride, int pad, const void *X, const void *Wt, float alpha, float beta,
+                     void *Y, long long ldy, int y_type, cudaStream_t st) {
+  const int out = y_type == ROUGE_B200_T_F32 ? ROUGE_B200_OUT_F32 : ROUGE_B200_OUT_BF16;
+  const int f16out = y_type == ROUGE_B200_T_F16 ? 1 : 0;
+  if (ab_type == ROUGE_B200_T_F32)
+    return launch_conv<MmaKind::TF32>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, nullptr, Y,
+                                      ldy, 0, out, f16out, 1, alpha, beta, st);
+  return launch_conv<MmaKind::F16>(N, H, W, Cin, Cout, KH, KW, stride, pad, X, Wt, nullptr, Y, ldy,
+                                   ab_type == ROUGE_B200_T_BF16 ? 1 : 0, out, f16out, 1, alpha, beta,
+                                   st);
 }
 
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,

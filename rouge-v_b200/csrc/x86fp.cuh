@@ -41,6 +41,14 @@ __device__ __forceinline__ uint32_t bf16x2_rn(float lo, float hi) {
   return r;
 }
 
+// Two f32 values to packed IEEE half (lo in bits 0-15), hardware round to
+// nearest even with overflow to infinity.
+__device__ __forceinline__ uint32_t f16x2_rn(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // x86_mul with the NaN handling moved off the common path: one multiply
 // and one NaN test, the full rule only when the product is NaN.
 __device__ __forceinline__ float x86_mul_fast(float a, float b) {
