@@ -604,6 +604,74 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
             "kernel": "pack (hi/lo split) + gemm_tc2_kernel<TF32> over 3K (3xTF32)"}
         del As, Bs, Cs, Ct
         shim.cublasDestroy_v2(h)
+
+    # cuDNN-API library: cudnnConvolutionForward at the config-4 shape
+    # (N=32, 56x56, 256 -> 256, 3x3 s1 p1), HALF + NHWC (direct: no
+    # workspace, alpha / beta in the epilogue, f16 out) and FLOAT + NCHW
+    # (3xTF32), each against torch's conv2d (cuDNN) on the same tensors:
+    # channels-last f16, and f32 with TF32 off.
+    dnn = C_.CDLL(os.path.join(ROOT, "rouge-v_b200", "lib", "librouge_b200_cudnn.so"))
+    hd = C_.c_void_p()
+    if dnn.cudnnCreate(C_.byref(hd)) == 0:
+        dnn.cudnnSetStream(hd, C_.c_void_p(torch.cuda.current_stream().cuda_stream))
+        F = torch.nn.functional
+
+        def desc(kind, *vals):
+            d = C_.c_void_p()
+            assert getattr(dnn, f"cudnnCreate{kind}Descriptor")(C_.byref(d)) == 0
+            setter = {"Tensor": dnn.cudnnSetTensor4dDescriptor, "Filter": dnn.cudnnSetFilter4dDescriptor,
+                      "Convolution": dnn.cudnnSetConvolution2dDescriptor}[kind]
+            assert setter(d, *[C_.c_int(v) for v in vals]) == 0
+            return d
+
+        cdsc = desc("Convolution", 1, 1, 1, 1, 1, 1, 0, 0)
+        fl = 2.0 * Nn * H * W_ * Co * 9 * Ci
+        for name, dtype, fmt in (("cudnn_shim_conv_nhwc_f16", 2, 1), ("cudnn_shim_conv_nchw_f32", 0, 0)):
+            tdt = torch.float16 if dtype == 2 else torch.float32
+            xt = torch.randn((Nn, Ci, H, W_), device=dev).to(tdt)
+            wt = (torch.randn((Co, Ci, 3, 3), device=dev) * 0.03).to(tdt)
+            if fmt == 1:
+                xt = xt.contiguous(memory_format=torch.channels_last)
+                wt = wt.contiguous(memory_format=torch.channels_last)
+            yt = torch.zeros((Nn, Co, H, W_), device=dev, dtype=tdt)
+            if fmt == 1:
+                yt = yt.contiguous(memory_format=torch.channels_last)
+            xdsc = desc("Tensor", fmt, dtype, Nn, Ci, H, W_)
+            ydsc = desc("Tensor", fmt, dtype, Nn, Co, H, W_)
+            wdsc = desc("Filter", dtype, fmt, Co, Ci, 3, 3)
+            ws_n = C_.c_size_t(0)
+            assert dnn.cudnnGetConvolutionForwardWorkspaceSize(hd, xdsc, wdsc, cdsc, ydsc, 0,
+                                                               C_.byref(ws_n)) == 0
+            wsb = torch.empty(max(ws_n.value, 256), dtype=torch.uint8, device=dev)
+            al, be = C_.c_float(1.0), C_.c_float(0.0)
+
+            def fwd():
+                st = dnn.cudnnConvolutionForward(
+                    hd, C_.byref(al), xdsc, C_.c_void_p(xt.data_ptr()), wdsc,
+                    C_.c_void_p(wt.data_ptr()), cdsc, 0, C_.c_void_p(wsb.data_ptr()),
+                    C_.c_size_t(ws_n.value), C_.byref(be), ydsc, C_.c_void_p(yt.data_ptr()))
+                assert st == 0, st
+            t_d = time_launch(torch, fwd, flush)
+            prev = torch.backends.cudnn.allow_tf32
+            torch.backends.cudnn.allow_tf32 = False
+            torch.backends.cudnn.benchmark = True
+            F.conv2d(xt, wt, padding=1)
+            t_t = time_launch(torch, lambda: F.conv2d(xt, wt, padding=1), flush)
+            want = F.conv2d(xt[:2].double(), wt.double(), padding=1)   # first two images
+            torch.backends.cudnn.allow_tf32 = prev
+            torch.backends.cudnn.benchmark = False
+            err = float((yt[:2].double() - want).norm() / want.norm())
+            out[name] = {
+                "ms": round(t_d, 4), "tflops": round(fl / (t_d * 1e-3) / 1e12, 1),
+                "workspace_bytes": ws_n.value,
+                "torch_cudnn_conv2d_ms": round(t_t, 4),
+                "torch_cudnn_conv2d_tflops": round(fl / (t_t * 1e-3) / 1e12, 1),
+                "rel_l2_vs_f64_first_2_images": err,
+                "kernel": ("gemm_tc2_kernel<F16, conv, f16 out> (direct, alpha/beta epilogue)"
+                           if dtype == 2 else
+                           "pack (NCHW -> NHWC hi/lo split) + gemm_tc2_kernel<TF32, conv> + NCHW finish")}
+            del xt, wt, yt, wsb, want
+        dnn.cudnnDestroy(hd)
     return out
 
 

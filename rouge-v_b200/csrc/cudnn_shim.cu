@@ -201,7 +201,8 @@ __device__ __forceinline__ double warp_sum(double v) {
 }
 
 // One block per row of `len` contiguous values (INSTANCE mode: an image).
-__global__ void softmax_rows_kernel(const float *__restrict__ x, float *y, size_t len, int is_log,
+constexpr int kSoftmaxThreads = 512;
+__global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_kernel(const float *__restrict__ x, float *y, size_t len, int is_log,
                                     float alpha, float beta) {
   __shared__ double red[32];
   const float *xr = x + blockIdx.x * len;
@@ -644,7 +645,7 @@ cudnnStatus_t cudnnSoftmaxForward(cudnnHandle_t handle, cudnnSoftmaxAlgorithm_t 
   float *dy = static_cast<float *>(sg.dev(y));
   const long long HW = static_cast<long long>(xD->h) * xD->w;
   if (mode == CUDNN_SOFTMAX_MODE_INSTANCE)
-    softmax_rows_kernel<<<xD->n, 1024, 0, handle->stream>>>(dx, dy, n / xD->n, is_log, al, be);
+    softmax_rows_kernel<<<xD->n, kSoftmaxThreads, 0, handle->stream>>>(dx, dy, n / xD->n, is_log, al, be);
   else
     softmax_channel_kernel<<<grid_for(static_cast<size_t>(xD->n) * HW), 256, 0, handle->stream>>>(
         dx, dy, xD->n, xD->c, HW, xD->format == CUDNN_TENSOR_NHWC ? 1 : 0, is_log, al, be);
