@@ -63,6 +63,13 @@ class Oracle:
             ("or_absmax", _F, [_P, _SZ]),
             ("or_quantize_e4m3_scaled", _F, [_P, _SZ, _F, _P]),
             ("or_conv2d_nhwc", None, [_I] * 9 + [_P, _P, _P, C.c_long, C.c_long, _P]),
+            ("or_narrow_encode_n", None, [_P, _SZ, _I, _I, _P]),
+            ("or_narrow_decode_n", None, [_P, _SZ, _I, _P]),
+            ("or_e8m0_encode", C.c_uint8, [_F]),
+            ("or_e8m0_decode", _F, [C.c_uint8]),
+            ("or_mx_quantize", _I, [_P, _I, _I, _P, _P]),
+            ("or_nvfp4_quantize", _I, [_P, _I, _F, _P, _P]),
+            ("or_mx_dequantize", None, [_P, _P, _I, _I, _P]),
         ]:
             fn = getattr(lib, name)
             fn.restype = res
@@ -185,6 +192,47 @@ class Oracle:
         s = self.lib.or_quantize_e4m3_scaled(_ptr(x), x.size, amax, _ptr(out))
         return out, float(np.float32(s)), amax
 
+    # -- narrow formats and MX / NVFP4 blocks (narrow.cpp) -----------------------
+    # fmt: 0 e4m3, 1 e5m2, 2 e3m2, 3 e2m3, 4 e2m1 (codes in the low bits)
+    NARROW = {"e4m3": 0, "e5m2": 1, "e3m2": 2, "e2m3": 3, "e2m1": 4}
+
+    def narrow_encode(self, x, fmt, nan_to_max=None):
+        f = self.NARROW[fmt]
+        if nan_to_max is None:
+            nan_to_max = f >= 2   # narrow.cpp:172-196: the 6/4-bit formats map NaN to +MAX
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        out = np.empty(x.size, np.uint8)
+        self.lib.or_narrow_encode_n(_ptr(x), x.size, f, int(nan_to_max), _ptr(out))
+        return out
+
+    def narrow_decode(self, c, fmt):
+        c = np.ascontiguousarray(c, dtype=np.uint8).ravel()
+        out = np.empty(c.size, np.float32)
+        self.lib.or_narrow_decode_n(_ptr(c), c.size, self.NARROW[fmt], _ptr(out))
+        return out
+
+    def mx_quantize(self, x, fmt):
+        """MXFP8 (fmt e4m3 / e5m2) or MXFP4 (e2m1): codes, E8M0 scales per 32."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.empty(x.size, np.uint8)
+        sc = np.empty((x.size + 31) // 32, np.uint8)
+        assert self.lib.or_mx_quantize(_ptr(x), x.size, self.NARROW[fmt], _ptr(q), _ptr(sc)) == sc.size
+        return q, sc
+
+    def nvfp4_quantize(self, x, gs):
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.empty(x.size, np.uint8)
+        sc = np.empty((x.size + 15) // 16, np.uint8)
+        assert self.lib.or_nvfp4_quantize(_ptr(x), x.size, gs, _ptr(q), _ptr(sc)) == sc.size
+        return q, sc
+
+    def mx_dequantize(self, q, sc, fmt):
+        q = np.ascontiguousarray(q, dtype=np.uint8).ravel()
+        sc = np.ascontiguousarray(sc, dtype=np.uint8).ravel()
+        out = np.empty(q.size, np.float32)
+        self.lib.or_mx_dequantize(_ptr(q), _ptr(sc), q.size, self.NARROW[fmt], _ptr(out))
+        return out
+
     # -- conv -------------------------------------------------------------------
     def conv2d_nhwc(self, x, w, bias, stride, pad, p0=0, p1=None):
         """x[N][H][W][Cin] f32, w[Cout][KH][KW][Cin] f32 -> y rows [p1-p0][Cout]."""
@@ -231,6 +279,17 @@ class Reference:
             ("rouge_gemm_bf16", None, [_I, _I, _I, _P, _P, _P, _P]),
             ("rouge_gemm_e4m3", None, [_I, _I, _I, _P, _P, _P, _P]),
             ("rouge_conv2d_f32", None, [_I] * 9 + [_P, _P, _P, _P, _P]),
+            ("rouge_quantize_e5m2", C.c_uint8, [_F]), ("rouge_dequantize_e5m2", _F, [C.c_uint8]),
+            ("rouge_quantize_e3m2", C.c_uint8, [_F]), ("rouge_dequantize_e3m2", _F, [C.c_uint8]),
+            ("rouge_quantize_e2m3", C.c_uint8, [_F]), ("rouge_dequantize_e2m3", _F, [C.c_uint8]),
+            ("rouge_quantize_e2m1", C.c_uint8, [_F]), ("rouge_dequantize_e2m1", _F, [C.c_uint8]),
+            ("rouge_mx_quantize_f32", _I, [_P, _I, _I, _P, _P]),
+            ("ref_narrow_encode_n", None, [_P, _SZ, _I, _P]),
+            ("ref_narrow_decode_n", None, [_P, _SZ, _I, _P]),
+            ("rouge_mx_quantize_f32_e2m1", _I, [_P, _I, _P, _P]),
+            ("rouge_nvfp4_quantize_f32", _I, [_P, _I, _F, _P, _P]),
+            ("rouge_mx_dequantize_f32", None, [_P, _P, _I, _I, _P]),
+            ("rouge_mx_dequantize_f32_e2m1", None, [_P, _P, _I, _P]),
             ("ref_hw_threads", _I, []),
             ("ref_quantize_i8_channel_mt", _I, [_P, _I, _I, _P, _P, _I]),
             ("ref_gemm_i8_mt", None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P, _I]),
@@ -340,6 +399,49 @@ class Reference:
         self.lib.rouge_conv2d_f32(N, Cin, H, W, Cout, KH, KW, stride, pad, _ptr(x), _ptr(w),
                                   _ptr(b) if b is not None else None, _ptr(y), None)
         return y
+
+    def narrow_encode(self, x, fmt):
+        """rouge_quantize_{e5m2,e3m2,e2m3,e2m1} over an array."""
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        out = np.empty(x.size, np.uint8)
+        self.lib.ref_narrow_encode_n(_ptr(x), x.size, Oracle.NARROW[fmt], _ptr(out))
+        return out
+
+    def narrow_decode(self, c, fmt):
+        c = np.ascontiguousarray(c, dtype=np.uint8).ravel()
+        out = np.empty(c.size, np.float32)
+        self.lib.ref_narrow_decode_n(_ptr(c), c.size, Oracle.NARROW[fmt], _ptr(out))
+        return out
+
+    def mx_quantize(self, x, fmt):
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.empty(x.size, np.uint8)
+        sc = np.empty((x.size + 31) // 32, np.uint8)
+        if fmt == "e2m1":
+            nb = self.lib.rouge_mx_quantize_f32_e2m1(_ptr(x), x.size, _ptr(q), _ptr(sc))
+        else:
+            nb = self.lib.rouge_mx_quantize_f32(_ptr(x), x.size, 1 if fmt == "e4m3" else 2, _ptr(q),
+                                                _ptr(sc))
+        assert nb == sc.size
+        return q, sc
+
+    def nvfp4_quantize(self, x, gs):
+        x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+        q = np.empty(x.size, np.uint8)
+        sc = np.empty((x.size + 15) // 16, np.uint8)
+        assert self.lib.rouge_nvfp4_quantize_f32(_ptr(x), x.size, gs, _ptr(q), _ptr(sc)) == sc.size
+        return q, sc
+
+    def mx_dequantize(self, q, sc, fmt):
+        q = np.ascontiguousarray(q, dtype=np.uint8).ravel()
+        sc = np.ascontiguousarray(sc, dtype=np.uint8).ravel()
+        out = np.empty(q.size, np.float32)
+        if fmt == "e2m1":
+            self.lib.rouge_mx_dequantize_f32_e2m1(_ptr(q), _ptr(sc), q.size, _ptr(out))
+        else:
+            self.lib.rouge_mx_dequantize_f32(_ptr(q), _ptr(sc), q.size, 1 if fmt == "e4m3" else 2,
+                                             _ptr(out))
+        return out
 
     def encode_n(self, fmt, x):
         """Bulk reference encode: fmt in {"e4m3", "f16", "bf16"}."""

@@ -22,6 +22,14 @@ int rouge_quantize_i8_channel(const float *x, int rows, int cols, float *scales,
 void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
                    const float *scales_a, int a_rows, const float *scales_b, int b_cols,
                    float *C);
+uint8_t rouge_quantize_e5m2(float f);
+float rouge_dequantize_e5m2(uint8_t u);
+uint8_t rouge_quantize_e3m2(float f);
+float rouge_dequantize_e3m2(uint8_t u);
+uint8_t rouge_quantize_e2m3(float f);
+float rouge_dequantize_e2m3(uint8_t u);
+uint8_t rouge_quantize_e2m1(float f);
+float rouge_dequantize_e2m1(uint8_t u);
 }
 
 namespace {
@@ -94,6 +102,19 @@ void ref_e4m3_decode_n(const uint8_t *c, size_t n, float *out) {
 }
 void ref_f16_decode_n(const uint16_t *c, size_t n, float *out) {
   for (size_t i = 0; i < n; ++i) out[i] = rouge_dequantize_f16(c[i]);
+}
+
+/* Bulk forms of the narrow-format codecs (numerics.h:257-264);
+ * fmt 1 e5m2, 2 e3m2, 3 e2m3, 4 e2m1. */
+void ref_narrow_encode_n(const float *x, size_t n, int fmt, uint8_t *out) {
+  uint8_t (*enc)(float) = fmt == 1 ? rouge_quantize_e5m2 : fmt == 2 ? rouge_quantize_e3m2
+                        : fmt == 3 ? rouge_quantize_e2m3 : rouge_quantize_e2m1;
+  for (size_t i = 0; i < n; ++i) out[i] = enc(x[i]);
+}
+void ref_narrow_decode_n(const uint8_t *c, size_t n, int fmt, float *out) {
+  float (*dec)(uint8_t) = fmt == 1 ? rouge_dequantize_e5m2 : fmt == 2 ? rouge_dequantize_e3m2
+                        : fmt == 3 ? rouge_dequantize_e2m3 : rouge_dequantize_e2m1;
+  for (size_t i = 0; i < n; ++i) out[i] = dec(c[i]);
 }
 
 /* Exact int32 accumulators of rows [r0, r1) of A[M][K] x B[K][N]: the loop

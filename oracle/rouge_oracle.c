@@ -327,3 +327,163 @@ void or_conv2d_nhwc(int N, int H, int W, int Cin, int Cout, int KH, int KW, int 
     }
   }
 }
+
+/* ---- narrow formats of narrow.cpp (e4m3 / e5m2 / e3m2 / e2m3 / e2m1) ----
+ * narrow.cpp:46-65 (format table), :67-106 (decode), :108-144 (encode).
+ * Codes are the format's field in the low bits of a byte. This is the
+ * generic encoder the MX / NVFP4 quantizers use; it differs from fp8.cpp's
+ * e4m3 encoder: a rounded result that lands on 0x7F (values in [464, 512))
+ * is kept, i.e. encodes NaN, instead of saturating to 0x7E. */
+typedef struct {
+  int exp_bits, man_bits, bias;
+  uint32_t max_bits, nan_bits;
+  int width;
+} or_narrow_fmt;
+
+/* fmt: 0 e4m3, 1 e5m2, 2 e3m2, 3 e2m3, 4 e2m1 */
+static const or_narrow_fmt OR_NARROW[5] = {
+    {4, 3, 7, 0x7Eu, 0x7Fu, 8}, {5, 2, 15, 0x7Bu, 0x7Fu, 8}, {3, 2, 3, 0x1Fu, 0x00u, 6},
+    {2, 3, 1, 0x1Fu, 0x00u, 6}, {2, 1, 1, 0x07u, 0x00u, 4}};
+
+float or_narrow_decode(uint32_t bits, int fmt) {
+  const or_narrow_fmt *F = &OR_NARROW[fmt];
+  const uint32_t fsign = ((bits >> (F->width - 1)) & 1u) << 31;
+  const uint32_t maxe = (1u << F->exp_bits) - 1u;
+  const uint32_t e = (bits >> F->man_bits) & maxe, m = bits & ((1u << F->man_bits) - 1u);
+  if (e == 0) {
+    if (m == 0) return u2f(fsign);
+    /* subnormal: m * 2^(1 - bias - man_bits), normalised */
+    uint32_t mm = m;
+    int sh = 0;
+    while (!(mm & (1u << F->man_bits))) { mm <<= 1; ++sh; }
+    mm &= (1u << F->man_bits) - 1u;
+    return u2f(fsign | ((uint32_t)(128 - F->bias - sh) << 23) | (mm << (23 - F->man_bits)));
+  }
+  if (e == maxe && F->nan_bits) {
+    /* a format whose all-ones exponent is not a normal binade (e5m2) has
+     * Inf at mantissa 0 and NaN otherwise; e4m3 only NaN at mantissa all-ones */
+    const int top_normal = ((F->max_bits >> F->man_bits) & maxe) == maxe;
+    if (!top_normal) return u2f(fsign | (m ? 0x7fc00000u : 0x7f800000u));
+    if (m == (1u << F->man_bits) - 1u) return u2f(fsign | 0x7fc00000u);
+  }
+  return u2f(fsign | ((uint32_t)((int)e - F->bias + 127) << 23) | (m << (23 - F->man_bits)));
+}
+
+uint32_t or_narrow_encode(float f, int fmt, int nan_to_max) {
+  const or_narrow_fmt *F = &OR_NARROW[fmt];
+  const uint32_t x = f2u(f), e = (x >> 23) & 0xffu, m = x & 0x7fffffu;
+  const uint32_t sbit = ((x >> 31) & 1u) << (F->width - 1);
+  const int M = F->man_bits;
+  const uint32_t maxe = (1u << F->exp_bits) - 1u, field = (1u << F->width) - 1u;
+  if (e == 0xffu && m) return nan_to_max ? F->max_bits : (sbit | F->nan_bits);
+  if (e == 0xffu) return sbit | F->max_bits; /* Inf saturates */
+  if (e == 0 && m == 0) return sbit;
+  const int te = (int)e - 127 + F->bias;
+  if (te > (int)maxe) return sbit | F->max_bits;
+  if (te <= 0) {
+    if (te < -M) return 0; /* narrow.cpp:128: too small -> +0, sign dropped */
+    const uint32_t full = 0x800000u | m;
+    const int sh = 1 - te + (23 - M);
+    uint32_t q = full >> sh;
+    const uint32_t r = full & ((1u << sh) - 1u), h = 1u << (sh - 1);
+    if (r > h || (r == h && (q & 1u))) ++q;
+    return sbit | (q & field);
+  }
+  uint32_t q = ((uint32_t)te << M) | (m >> (23 - M));
+  const uint32_t r = m & ((1u << (23 - M)) - 1u), h = 1u << (22 - M);
+  if (r > h || (r == h && (q & 1u))) {
+    ++q;
+    if ((q >> M) > maxe) return sbit | F->max_bits;
+  }
+  return sbit | (q & field);
+}
+
+void or_narrow_encode_n(const float *x, size_t n, int fmt, int nan_to_max, uint8_t *out) {
+  for (size_t i = 0; i < n; ++i) out[i] = (uint8_t)or_narrow_encode(x[i], fmt, nan_to_max);
+}
+void or_narrow_decode_n(const uint8_t *c, size_t n, int fmt, float *out) {
+  for (size_t i = 0; i < n; ++i) out[i] = or_narrow_decode(c[i], fmt);
+}
+
+/* ---- E8M0 block scales: narrow.cpp:146-163 ----------------------------- */
+
+float or_e8m0_decode(uint8_t c) {
+  if (c == 255) return u2f(0x7fc00000u);
+  if (c == 0) return u2f(0x00400000u); /* 2^-127, subnormal */
+  return u2f((uint32_t)c << 23);
+}
+
+/* frexp's exponent of a positive finite scale, clamped to [-126, 127] and
+ * biased by 127. For a power of two 2^p frexp gives p + 1, so the code is
+ * p + 128: the stored scale is twice the chosen one (the reference's
+ * behaviour, kept). Non-positive or non-finite scales give 127 (1.0). */
+uint8_t or_e8m0_encode(float s) {
+  if (!(s > 0.0f) || !isfinite(s)) return 127;
+  int e = 0;
+  frexpf(s, &e);
+  if (e < -126) e = -126;
+  if (e > 127) e = 127;
+  return (uint8_t)(e + 127);
+}
+
+/* smallest p >= 0 (at most 127) with amax <= emax * 2^p: narrow.cpp:213-216 */
+static int or_block_pow(float amax, float emax) {
+  int p = 0;
+  while (amax > ldexpf(emax, p) && p < 127) ++p;
+  return p;
+}
+
+/* MXFP8 / MXFP4: narrow.cpp:200-265. fmt 0 (e4m3), 1 (e5m2) or 4 (e2m1,
+ * NaN -> +MAX); blocks of 32, the last one partial. Returns the block count. */
+int or_mx_quantize(const float *x, int n, int fmt, uint8_t *out, uint8_t *scales) {
+  const int nan_to_max = fmt == 4;
+  const float emax = or_narrow_decode(OR_NARROW[fmt].max_bits, fmt);
+  for (int base = 0; base < n; base += 32) {
+    const int cnt = n - base < 32 ? n - base : 32;
+    float amax = 0.0f;
+    for (int i = 0; i < cnt; ++i) {
+      const float a = fabsf(x[base + i]);
+      if (a > amax) amax = a;
+    }
+    const float scale = amax > 0.0f ? ldexpf(1.0f, or_block_pow(amax, emax)) : 1.0f;
+    const uint8_t sc = or_e8m0_encode(scale);
+    scales[base / 32] = sc;
+    const float inv = 1.0f / or_e8m0_decode(sc);
+    for (int i = 0; i < cnt; ++i) {
+      const uint32_t q = or_narrow_encode(x[base + i] * inv, fmt, nan_to_max);
+      out[base + i] = (uint8_t)(fmt == 4 ? (q & 0x0Fu) : q);
+    }
+  }
+  return (n + 31) / 32;
+}
+
+/* NVFP4: narrow.cpp:270-300. Blocks of 16 e2m1 codes; block scale 2^p coded
+ * in e4m3 by the generic encoder (2^9 and above saturate to 448); amax over
+ * |x| * gs, elements x * (1 / (scale * gs)); gs <= 0 (or NaN) becomes 1. */
+int or_nvfp4_quantize(const float *x, int n, float gs, uint8_t *out, uint8_t *scales) {
+  if (!(gs > 0.0f)) gs = 1.0f;
+  const float emax = or_narrow_decode(OR_NARROW[0].max_bits, 0);
+  for (int base = 0; base < n; base += 16) {
+    const int cnt = n - base < 16 ? n - base : 16;
+    float amax = 0.0f;
+    for (int i = 0; i < cnt; ++i) {
+      const float a = fabsf(x[base + i]) * gs;
+      if (a > amax) amax = a;
+    }
+    const float bs = amax > 0.0f ? ldexpf(1.0f, or_block_pow(amax, emax)) : 1.0f;
+    const uint8_t sc = (uint8_t)or_narrow_encode(bs, 0, 0);
+    scales[base / 16] = sc;
+    const float inv = 1.0f / (or_narrow_decode(sc, 0) * gs);
+    for (int i = 0; i < cnt; ++i)
+      out[base + i] = (uint8_t)(or_narrow_encode(x[base + i] * inv, 4, 1) & 0x0Fu);
+  }
+  return (n + 15) / 16;
+}
+
+/* narrow.cpp:304-331: element decode times the block's E8M0 scale. */
+void or_mx_dequantize(const uint8_t *in, const uint8_t *scales, int n, int fmt, float *out) {
+  for (int i = 0; i < n; ++i) {
+    const uint32_t c = fmt == 4 ? (in[i] & 0x0Fu) : in[i];
+    out[i] = or_narrow_decode(c, fmt) * or_e8m0_decode(scales[i / 32]);
+  }
+}
