@@ -352,6 +352,45 @@ int rouge_b200_conv2d_nhwc_f16(int N, int H, int W, int Cin, int Cout, int KH, i
                                int stride, int pad, const uint16_t *X, const uint16_t *Wt,
                                const float *bias, float *Y, int is_bf16, void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Narrow formats and MX / NVFP4 block quantization (narrow.cpp)            */
+/* ------------------------------------------------------------------------ */
+/* Replace numerics.h:257-264 (narrow.cpp:166-198): single-value codecs,
+ * codes in the low bits (e2m1: 4-bit field, sign in bit 3). */
+uint8_t rouge_quantize_e5m2(float f);
+float rouge_dequantize_e5m2(uint8_t u);
+uint8_t rouge_quantize_e3m2(float f);
+float rouge_dequantize_e3m2(uint8_t u);
+uint8_t rouge_quantize_e2m3(float f);
+float rouge_dequantize_e2m3(uint8_t u);
+uint8_t rouge_quantize_e2m1(float f);
+float rouge_dequantize_e2m1(uint8_t u);
+
+/* Replace numerics.h:278-289 (narrow.cpp:200-331), host pointers,
+ * synchronous: MXFP8 (elem_bytes 1: e4m3, 2: e5m2) and MXFP4 (e2m1) in
+ * blocks of 32 with E8M0 scales, NVFP4 (e2m1) in blocks of 16 with e4m3
+ * block scales and a global scale. Return the block count (0 and nothing
+ * written on invalid arguments or a device failure). */
+int rouge_mx_quantize_f32(const float *x, int n, int elem_bytes, uint8_t *out,
+                          uint8_t *scale_out);
+int rouge_mx_quantize_f32_e2m1(const float *x, int n, uint8_t *out, uint8_t *scale_out);
+int rouge_nvfp4_quantize_f32(const float *x, int n, float global_scale, uint8_t *out,
+                             uint8_t *scale_out);
+void rouge_mx_dequantize_f32(const uint8_t *in, const uint8_t *scales, int n, int elem_bytes,
+                             float *out);
+void rouge_mx_dequantize_f32_e2m1(const uint8_t *in, const uint8_t *scales, int n, float *out);
+
+/* Device-pointer forms (asynchronous on `stream`); fmt ROUGE_B200_FMT_*. */
+#define ROUGE_B200_FMT_E4M3 0
+#define ROUGE_B200_FMT_E5M2 1
+#define ROUGE_B200_FMT_E2M1 4
+int rouge_b200_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_t *scales,
+                           void *stream);
+int rouge_b200_nvfp4_quantize(const float *x, size_t n, float global_scale, uint8_t *codes,
+                              uint8_t *scales, void *stream);
+int rouge_b200_mx_dequantize(const uint8_t *codes, const uint8_t *scales, size_t n, int fmt,
+                             float *out, void *stream);
+
 /* Convolution forward with cuDNN's semantics (the operation the reference
  * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU
  * conv): Y = alpha * conv(X, Wt) + beta * Y, cross-correlation, symmetric

@@ -1,0 +1,313 @@
+// MX / NVFP4 block quantizers and the narrow-format codecs (narrow.cpp:
+// 166-331): the reference's host entries (rouge_mx_quantize_f32, ...,
+// rouge_quantize_e5m2, ...) and their device-pointer forms.
+//
+// Blocks are 32 (MX) or 16 (NVFP4) consecutive elements of a flat array,
+// the last block partial, exactly as the reference walks them; for an
+// [M][K] matrix with K % 32 == 0 they are the per-row K-blocks a
+// block-scaled GEMM consumes. Kernels: 8 (MX) or 4 (NVFP4) lanes per block,
+// one float4 per lane, block maximum by shuffles, scale, encode 4 elements
+// to one 32-bit store; memory-bound (4 B read, 1 B + 1/32 B written per
+// element).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "narrow.cuh"
+#include "runtime.cuh"
+#include "x86fp.cuh"
+
+namespace rb200 {
+namespace {
+
+constexpr int kMxThreads = 256;
+
+__device__ __forceinline__ float4 load4(const float *__restrict__ x, size_t e0, size_t n,
+                                        bool vec) {
+  if (vec && e0 + 4 <= n) return __ldg(reinterpret_cast<const float4 *>(x + e0));
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (e0 < n) v.x = x[e0];
+  if (e0 + 1 < n) v.y = x[e0 + 1];
+  if (e0 + 2 < n) v.z = x[e0 + 2];
+  if (e0 + 3 < n) v.w = x[e0 + 3];
+  return v;
+}
+
+__device__ __forceinline__ void store4(uint8_t *__restrict__ q, size_t e0, size_t n, bool vec,
+                                       uint32_t w) {
+  if (vec && e0 + 4 <= n) {
+    *reinterpret_cast<uint32_t *>(q + e0) = w;
+    return;
+  }
+  for (int i = 0; i < 4; ++i)
+    if (e0 + i < n) q[e0 + i] = static_cast<uint8_t>(w >> (8 * i));
+}
+
+__device__ __forceinline__ float amax4(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+
+// MXFP8 (ID e4m3 / e5m2) and MXFP4 (e2m1): narrow.cpp:200-265. The block
+// maximum ignores NaN (the reference's strict comparison does);
+// scale 2^p with the smallest p >= 0 such that amax <= emax * 2^p, stored
+// as E8M0 code p + 128, elements encoded from x * 2^(127 - code).
+template <int ID>
+__global__ void __launch_bounds__(kMxThreads)
+    mx_quant_kernel(const float *__restrict__ x, size_t n, uint8_t *__restrict__ codes,
+                    uint8_t *__restrict__ scales, int vec_in, int vec_out) {
+  constexpr float kEmax = ID == kE4M3 ? 448.0f : ID == kE5M2 ? 57344.0f : 6.0f;
+  const size_t nblk = (n + 31) / 32;
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+  for (size_t b0 = ((static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 4;
+       b0 < nblk; b0 += nwarps * 4) {
+    const size_t blk = b0 + (lane >> 3);
+    const size_t e0 = blk * 32 + sub * 4;
+    const float4 v = blk < nblk ? load4(x, e0, n, vec_in) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float a = amax4(v);
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+    const uint32_t sc = mx_scale_code(a > 0.0f ? block_pow(a, kEmax) : 0);
+    const float inv = e8m0_inverse(sc);
+    if (blk >= nblk) continue;
+    if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
+    const float4 s = make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
+                                 __fmul_rn(v.w, inv));
+    uint32_t w;
+    if constexpr (ID == kE2M1)
+      w = encode_e2m1(s.x) | (encode_e2m1(s.y) << 8) | (encode_e2m1(s.z) << 16) |
+          (encode_e2m1(s.w) << 24);
+    else
+      w = encode4_f8<ID>(s);
+    store4(codes, e0, n, vec_out, w);
+  }
+}
+
+// NVFP4: narrow.cpp:270-300. Blocks of 16 e2m1 codes, 4 lanes per block;
+// block maximum of |x| * gs, block scale 2^p coded by the generic e4m3
+// encoder (2^9 and above saturate to 448), elements x * (1 / (scale * gs)).
+__global__ void __launch_bounds__(kMxThreads)
+    nvfp4_quant_kernel(const float *__restrict__ x, size_t n, float gs,
+                       uint8_t *__restrict__ codes, uint8_t *__restrict__ scales, int vec_in,
+                       int vec_out) {
+  const size_t nblk = (n + 15) / 16;
+  const int lane = threadIdx.x & 31, sub = lane & 3;
+  const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
+  for (size_t b0 = ((static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 8;
+       b0 < nblk; b0 += nwarps * 8) {
+    const size_t blk = b0 + (lane >> 2);
+    const size_t e0 = blk * 16 + sub * 4;
+    const float4 v = blk < nblk ? load4(x, e0, n, vec_in) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float a = fmaxf(fmaxf(__fmul_rn(fabsf(v.x), gs), __fmul_rn(fabsf(v.y), gs)),
+                    fmaxf(__fmul_rn(fabsf(v.z), gs), __fmul_rn(fabsf(v.w), gs)));
+    // elements past n are zeros: 0 * gs = 0 leaves the maximum unchanged
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+    const int p = a > 0.0f ? block_pow(a, 448.0f) : 0;
+    const uint32_t sc = narrow_encode(__uint_as_float(static_cast<uint32_t>(p + 127) << 23), kE4M3,
+                                      false);
+    const float inv = __fdiv_rn(1.0f, __fmul_rn(narrow_decode(sc, kE4M3), gs));
+    if (blk >= nblk) continue;
+    if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
+    const uint32_t w = encode_e2m1(__fmul_rn(v.x, inv)) | (encode_e2m1(__fmul_rn(v.y, inv)) << 8) |
+                       (encode_e2m1(__fmul_rn(v.z, inv)) << 16) |
+                       (encode_e2m1(__fmul_rn(v.w, inv)) << 24);
+    store4(codes, e0, n, vec_out, w);
+  }
+}
+
+// narrow.cpp:304-331: out = decode(code) * 2^(scale - 127), the product with
+// x86's NaN rules (a NaN code keeps its sign and payload).
+template <int ID>
+__global__ void __launch_bounds__(kMxThreads)
+    mx_dequant_kernel(const uint8_t *__restrict__ codes, const uint8_t *__restrict__ scales,
+                      size_t n, float *__restrict__ out, int vec) {
+  __shared__ float lut[256];
+  for (int c = threadIdx.x; c < 256; c += blockDim.x)
+    lut[c] = narrow_decode(ID == kE2M1 ? (c & 0x0F) : c, ID);
+  __syncthreads();
+  for (size_t e0 = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4; e0 < n;
+       e0 += static_cast<size_t>(gridDim.x) * blockDim.x * 4) {
+    const float s = e8m0_decode(scales[e0 / 32]);
+    if (vec && e0 + 4 <= n) {
+      const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(codes + e0));
+      *reinterpret_cast<float4 *>(out + e0) =
+          make_float4(x86_mul(lut[w & 0xFF], s), x86_mul(lut[(w >> 8) & 0xFF], s),
+                      x86_mul(lut[(w >> 16) & 0xFF], s), x86_mul(lut[w >> 24], s));
+    } else {
+      for (int i = 0; i < 4 && e0 + i < n; ++i) out[e0 + i] = x86_mul(lut[codes[e0 + i]], s);
+    }
+  }
+}
+
+unsigned grid_for(size_t work_items, int per_block) {
+  const size_t need = (work_items + per_block - 1) / per_block;
+  const size_t cap = static_cast<size_t>(current_sm_count()) * 8;
+  return static_cast<unsigned>(need < 1 ? 1 : (need < cap ? need : cap));
+}
+
+bool a16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool a4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+}  // namespace
+
+int launch_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_t *scales,
+                       cudaStream_t st) {
+  const unsigned grid = grid_for((n + 31) / 32, kMxThreads / 8);
+  const int vi = a16(x), vo = a4(codes);
+  switch (fmt) {
+    case kE4M3: mx_quant_kernel<kE4M3><<<grid, kMxThreads, 0, st>>>(x, n, codes, scales, vi, vo); break;
+    case kE5M2: mx_quant_kernel<kE5M2><<<grid, kMxThreads, 0, st>>>(x, n, codes, scales, vi, vo); break;
+    default: mx_quant_kernel<kE2M1><<<grid, kMxThreads, 0, st>>>(x, n, codes, scales, vi, vo); break;
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_nvfp4_quantize(const float *x, size_t n, float gs, uint8_t *codes, uint8_t *scales,
+                          cudaStream_t st) {
+  const unsigned grid = grid_for((n + 15) / 16, kMxThreads / 4);
+  nvfp4_quant_kernel<<<grid, kMxThreads, 0, st>>>(x, n, gs, codes, scales, a16(x), a4(codes));
+  return cuda_status(cudaGetLastError());
+}
+
+int launch_mx_dequantize(const uint8_t *codes, const uint8_t *scales, size_t n, int fmt,
+                         float *out, cudaStream_t st) {
+  const unsigned grid = grid_for((n + 3) / 4, kMxThreads);
+  const int v = a4(codes) && a16(out);
+  switch (fmt) {
+    case kE4M3: mx_dequant_kernel<kE4M3><<<grid, kMxThreads, 0, st>>>(codes, scales, n, out, v); break;
+    case kE5M2: mx_dequant_kernel<kE5M2><<<grid, kMxThreads, 0, st>>>(codes, scales, n, out, v); break;
+    default: mx_dequant_kernel<kE2M1><<<grid, kMxThreads, 0, st>>>(codes, scales, n, out, v); break;
+  }
+  return cuda_status(cudaGetLastError());
+}
+
+namespace {
+
+bool valid_mx_fmt(int fmt) { return fmt == kE4M3 || fmt == kE5M2 || fmt == kE2M1; }
+
+// Ends a host-pointer call: waits for the stream, folds in device failures.
+int call_finish(cudaStream_t st) {
+  const int s = cuda_status(cudaStreamSynchronize(st));
+  return s != ROUGE_B200_OK ? s : take_device_error(st);
+}
+
+// Host-pointer call: x (n floats) in, codes (n bytes) and scales out.
+int host_quantize(const float *x, int n, int fmt, float gs, bool nv, uint8_t *out,
+                  uint8_t *scale_out) {
+  HostCallContext *ctx = host_context();
+  if (!ctx) return 0;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t nn = static_cast<size_t>(n);
+  const size_t nblk = nv ? (nn + 15) / 16 : (nn + 31) / 32;
+  const size_t need = round_up(nn * 4, 256) + round_up(nn, 256) + round_up(nblk, 256);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return 0;
+  uint8_t *base = static_cast<uint8_t *>(ctx->ws);
+  float *dx = reinterpret_cast<float *>(base);
+  uint8_t *dq = base + round_up(nn * 4, 256);
+  uint8_t *ds = dq + round_up(nn, 256);
+  cudaStream_t st = ctx->stream;
+  int s = cuda_status(cudaMemcpyAsync(dx, x, nn * 4, cudaMemcpyHostToDevice, st));
+  if (s == ROUGE_B200_OK)
+    s = nv ? launch_nvfp4_quantize(dx, nn, gs, dq, ds, st) : launch_mx_quantize(dx, nn, fmt, dq, ds, st);
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(out, dq, nn, cudaMemcpyDeviceToHost, st));
+  if (s == ROUGE_B200_OK)
+    s = cuda_status(cudaMemcpyAsync(scale_out, ds, nblk, cudaMemcpyDeviceToHost, st));
+  const int f = call_finish(st);
+  return s == ROUGE_B200_OK && f == ROUGE_B200_OK ? static_cast<int>(nblk) : 0;
+}
+
+void host_dequantize(const uint8_t *in, const uint8_t *scales, int n, int fmt, float *out) {
+  HostCallContext *ctx = host_context();
+  if (!ctx) return;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t nn = static_cast<size_t>(n), nblk = (nn + 31) / 32;
+  const size_t need = round_up(nn * 4, 256) + round_up(nn, 256) + round_up(nblk, 256);
+  if (ensure_workspace(ctx, need) != ROUGE_B200_OK) return;
+  uint8_t *base = static_cast<uint8_t *>(ctx->ws);
+  float *dout = reinterpret_cast<float *>(base);
+  uint8_t *dq = base + round_up(nn * 4, 256);
+  uint8_t *ds = dq + round_up(nn, 256);
+  cudaStream_t st = ctx->stream;
+  int s = cuda_status(cudaMemcpyAsync(dq, in, nn, cudaMemcpyHostToDevice, st));
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(ds, scales, nblk, cudaMemcpyHostToDevice, st));
+  if (s == ROUGE_B200_OK) s = launch_mx_dequantize(dq, ds, nn, fmt, dout, st);
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(out, dout, nn * 4, cudaMemcpyDeviceToHost, st));
+  call_finish(st);
+}
+
+}  // namespace
+}  // namespace rb200
+
+using namespace rb200;
+
+extern "C" {
+
+// numerics.h:257-264: single-value codecs (host), narrow.cpp:166-198.
+uint8_t rouge_quantize_e5m2(float f) { return static_cast<uint8_t>(narrow_encode(f, kE5M2, false)); }
+float rouge_dequantize_e5m2(uint8_t u) { return narrow_decode(u, kE5M2); }
+uint8_t rouge_quantize_e3m2(float f) { return static_cast<uint8_t>(narrow_encode(f, kE3M2, true) & 0x3Fu); }
+float rouge_dequantize_e3m2(uint8_t u) { return narrow_decode(u & 0x3Fu, kE3M2); }
+uint8_t rouge_quantize_e2m3(float f) { return static_cast<uint8_t>(narrow_encode(f, kE2M3, true) & 0x3Fu); }
+float rouge_dequantize_e2m3(uint8_t u) { return narrow_decode(u & 0x3Fu, kE2M3); }
+uint8_t rouge_quantize_e2m1(float f) { return static_cast<uint8_t>(narrow_encode(f, kE2M1, true) & 0x0Fu); }
+float rouge_dequantize_e2m1(uint8_t u) { return narrow_decode(u & 0x0Fu, kE2M1); }
+
+// numerics.h:278-289 (narrow.cpp:200-331). Invalid arguments: 0 / no write.
+int rouge_mx_quantize_f32(const float *x, int n, int elem_bytes, uint8_t *out, uint8_t *scale_out) {
+  if (!x || !out || !scale_out || n <= 0 || (elem_bytes != 1 && elem_bytes != 2)) return 0;
+  return host_quantize(x, n, elem_bytes == 1 ? kE4M3 : kE5M2, 1.0f, false, out, scale_out);
+}
+
+int rouge_mx_quantize_f32_e2m1(const float *x, int n, uint8_t *out, uint8_t *scale_out) {
+  if (!x || !out || !scale_out || n <= 0) return 0;
+  return host_quantize(x, n, kE2M1, 1.0f, false, out, scale_out);
+}
+
+int rouge_nvfp4_quantize_f32(const float *x, int n, float global_scale, uint8_t *out,
+                             uint8_t *scale_out) {
+  if (!x || !out || !scale_out || n <= 0) return 0;
+  if (!(global_scale > 0.0f)) global_scale = 1.0f;
+  return host_quantize(x, n, kE2M1, global_scale, true, out, scale_out);
+}
+
+void rouge_mx_dequantize_f32(const uint8_t *in, const uint8_t *scales, int n, int elem_bytes,
+                             float *out) {
+  if (!in || !scales || !out || n <= 0 || (elem_bytes != 1 && elem_bytes != 2)) return;
+  host_dequantize(in, scales, n, elem_bytes == 1 ? kE4M3 : kE5M2, out);
+}
+
+void rouge_mx_dequantize_f32_e2m1(const uint8_t *in, const uint8_t *scales, int n, float *out) {
+  if (!in || !scales || !out || n <= 0) return;
+  host_dequantize(in, scales, n, kE2M1, out);
+}
+
+// Device-pointer forms (asynchronous on `stream`).
+int rouge_b200_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_t *scales,
+                           void *stream) {
+  if (!x || !codes || !scales || n == 0 || !valid_mx_fmt(fmt)) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_mx_quantize(x, n, fmt, codes, scales, as_stream(stream));
+}
+
+int rouge_b200_nvfp4_quantize(const float *x, size_t n, float global_scale, uint8_t *codes,
+                              uint8_t *scales, void *stream) {
+  if (!x || !codes || !scales || n == 0) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  if (!(global_scale > 0.0f)) global_scale = 1.0f;
+  return launch_nvfp4_quantize(x, n, global_scale, codes, scales, as_stream(stream));
+}
+
+int rouge_b200_mx_dequantize(const uint8_t *codes, const uint8_t *scales, size_t n, int fmt,
+                             float *out, void *stream) {
+  if (!codes || !scales || !out || n == 0 || !valid_mx_fmt(fmt)) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_mx_dequantize(codes, scales, n, fmt, out, as_stream(stream));
+}
+
+}  // extern "C"

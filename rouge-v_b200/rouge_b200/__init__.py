@@ -93,6 +93,18 @@ _SIGS = {
     "rouge_b200_absmax_f32": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_quantize_e4m3_scaled": (_I, [_P, _SZ, _P, _P, _P, _P]),
     "rouge_b200_quantize_e4m3_tensor": (_I, [_P, _SZ, _P, _P, _P, _P]),
+    "rouge_b200_mx_quantize": (_I, [_P, _SZ, _I, _P, _P, _P]),
+    "rouge_b200_nvfp4_quantize": (_I, [_P, _SZ, C.c_float, _P, _P, _P]),
+    "rouge_b200_mx_dequantize": (_I, [_P, _P, _SZ, _I, _P, _P]),
+    "rouge_quantize_e5m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e5m2": (C.c_float, [C.c_uint8]),
+    "rouge_quantize_e3m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e3m2": (C.c_float, [C.c_uint8]),
+    "rouge_quantize_e2m3": (C.c_uint8, [C.c_float]), "rouge_dequantize_e2m3": (C.c_float, [C.c_uint8]),
+    "rouge_quantize_e2m1": (C.c_uint8, [C.c_float]), "rouge_dequantize_e2m1": (C.c_float, [C.c_uint8]),
+    "rouge_mx_quantize_f32": (_I, [_P, _I, _I, _P, _P]),
+    "rouge_mx_quantize_f32_e2m1": (_I, [_P, _I, _P, _P]),
+    "rouge_nvfp4_quantize_f32": (_I, [_P, _I, C.c_float, _P, _P]),
+    "rouge_mx_dequantize_f32": (None, [_P, _P, _I, _I, _P]),
+    "rouge_mx_dequantize_f32_e2m1": (None, [_P, _P, _I, _P]),
     "rouge_b200_convert_f32_to_f16": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_convert_f32_to_bf16": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_convert_e4m3_to_f32": (_I, [_P, _SZ, _P, _P]),
@@ -189,6 +201,25 @@ def quantize_e4m3_scaled(x, amax, scale_out, out):
 def quantize_e4m3_tensor(x, amax_out, scale_out, out):
     _check("rouge_b200_quantize_e4m3_tensor", lib().rouge_b200_quantize_e4m3_tensor(
         _dp(x), x.numel(), _dp(amax_out), _dp(scale_out), _dp(out), _stream()))
+
+
+FMT_E4M3, FMT_E5M2, FMT_E2M1 = 0, 1, 4
+
+
+def mx_quantize(x, fmt, codes, scales):
+    """MXFP8 / MXFP4 block quantization of a flat f32 tensor (blocks of 32)."""
+    _check("rouge_b200_mx_quantize", lib().rouge_b200_mx_quantize(
+        _dp(x), x.numel(), fmt, _dp(codes), _dp(scales), _stream()))
+
+
+def nvfp4_quantize(x, global_scale, codes, scales):
+    _check("rouge_b200_nvfp4_quantize", lib().rouge_b200_nvfp4_quantize(
+        _dp(x), x.numel(), global_scale, _dp(codes), _dp(scales), _stream()))
+
+
+def mx_dequantize(codes, scales, fmt, out):
+    _check("rouge_b200_mx_dequantize", lib().rouge_b200_mx_dequantize(
+        _dp(codes), _dp(scales), codes.numel(), fmt, _dp(out), _stream()))
 
 
 def convert_f32_to_f16(x, out):
