@@ -73,8 +73,9 @@ __global__ void __launch_bounds__(kMxThreads)
     const float inv = e8m0_inverse(sc);
     if (blk >= nblk) continue;
     if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
-    const float4 s = make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
-                                 __fmul_rn(v.w, inv));
+    // x86 products: a NaN element keeps its sign (the code is sign|0x7F)
+    const float4 s = make_float4(x86_mul_fast(v.x, inv), x86_mul_fast(v.y, inv),
+                                 x86_mul_fast(v.z, inv), x86_mul_fast(v.w, inv));
     uint32_t w;
     if constexpr (ID == kE2M1)
       w = encode_e2m1(s.x) | (encode_e2m1(s.y) << 8) | (encode_e2m1(s.z) << 16) |

@@ -32,6 +32,15 @@ def _same_bits(a, b):
     return bool((np.asarray(a).view(np.uint32) == np.asarray(b).view(np.uint32)).all())
 
 
+def _eq(got, want, x=None):
+    """Array equality with the first mismatches in the failure message."""
+    bad = np.nonzero(got != want)[0]
+    if bad.size:
+        rows = [(int(i), None if x is None else float(x[i]) if i < x.size else None,
+                 int(got[i]), int(want[i])) for i in bad[:8]]
+        raise AssertionError(f"{bad.size} mismatches (index, x, got, want): {rows}")
+
+
 @pytest.mark.parametrize("fmt", ["e4m3", "e5m2", "e2m1"])
 @pytest.mark.parametrize("n,offset", [(32, 0), (4096, 0), (1000, 0), (4099, 0), (777, 1),
                                       (1 << 20, 0), (1 << 20, 3)])
@@ -47,8 +56,8 @@ def test_mx_quantize_bit_exact(rb, orc, cuda, fmt, n, offset):
     s = torch.full(((n + 31) // 32,), 0xAA, dtype=torch.uint8, device=cuda)
     rb.mx_quantize(xd, FMT[fmt], q, s)
     wq, ws = orc.mx_quantize(x, fmt)
-    assert (q.cpu().numpy() == wq).all()
-    assert (s.cpu().numpy() == ws).all()
+    _eq(q.cpu().numpy(), wq, x)
+    _eq(s.cpu().numpy(), ws)
     assert (qb[:offset].cpu().numpy() == 0xAA).all() and (qb[offset + n:].cpu().numpy() == 0xAA).all()
     out = torch.empty(n, dtype=torch.float32, device=cuda)
     rb.mx_dequantize(q, s, FMT[fmt], out)
@@ -65,7 +74,8 @@ def test_nvfp4_quantize_bit_exact(rb, orc, cuda, gs, n):
     s = torch.empty((n + 15) // 16, dtype=torch.uint8, device=cuda)
     rb.nvfp4_quantize(torch.from_numpy(x).to(cuda), gs, q, s)
     wq, ws = orc.nvfp4_quantize(x, gs)
-    assert (q.cpu().numpy() == wq).all() and (s.cpu().numpy() == ws).all()
+    _eq(q.cpu().numpy(), wq, x)
+    _eq(s.cpu().numpy(), ws)
 
 
 def test_full_size_block_quantizers(rb, orc, cuda):
