@@ -391,6 +391,22 @@ int rouge_b200_nvfp4_quantize(const float *x, size_t n, float global_scale, uint
 int rouge_b200_mx_dequantize(const uint8_t *codes, const uint8_t *scales, size_t n, int fmt,
                              float *out, void *stream);
 
+/* Block-scaled MXFP8 GEMM on tcgen05 (kind::mxf8f6f4.block_scale; no
+ * reference counterpart: the reference has the formats but no GEMM on
+ * them). C[M][N] (f32 or bf16, row pitch ldc) = sum_k A'[m][k] B'[n][k]
+ * with A' = decode(A) * 2^(sfa - 127) per 32-element K-block of each row,
+ * likewise B'; f32 accumulation. A [M][K] and B [N][K] are e4m3
+ * (ROUGE_B200_FMT_E4M3) or e5m2 codes, K-major, K % 32 == 0, 16-byte
+ * aligned; sfa / sfb are their E8M0 scales in the tensor-core atom layout
+ * made by rouge_b200_mx_scale_atoms from the block quantizer's [rows][K/32]
+ * scales. */
+size_t rouge_b200_mx_scale_atoms_bytes(int rows, int K);
+int rouge_b200_mx_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                              void *stream);
+int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const uint8_t *sfa,
+                       const uint8_t *B, int fmt_b, const uint8_t *sfb, void *C, int ldc,
+                       int out_type, void *stream);
+
 /* Convolution forward with cuDNN's semantics (the operation the reference
  * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU
  * conv): Y = alpha * conv(X, Wt) + beta * Y, cross-correlation, symmetric

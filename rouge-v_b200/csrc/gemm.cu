@@ -45,8 +45,8 @@ struct GemmArgs {
   int num_m, num_n, num_k, num_tiles;
   void *C;
   long long ldc;
-  const float *scales_a;  // int8: per-row or single scale
-  const float *scales_b;  // int8: per-column or single scale
+  const float *scales_a;  // int8: per-row or single scale; MXF8: A's scale atoms (bytes)
+  const float *scales_b;  // int8: per-column or single scale; MXF8: B's scale atoms
   int a_rows, b_cols;
   const float *scale_a;   // e4m3 / f16: per-tensor scale scalars (or null)
   const float *scale_b;
@@ -83,6 +83,9 @@ struct GemmArgs {
   // remaining tiles cut N-wise into `split` parts of BN / split columns
   // (one unit per part), so that the round's units fill more clusters.
   int split_from, split;
+  // Block-scaled kind (MXF8): operand formats (E4M3 0, E5M2 1) and the
+  // number of 128-K blocks per row of the scale-atom arrays.
+  int mx_fmt_a, mx_fmt_b, sf_kblocks;
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
@@ -93,6 +96,9 @@ constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128
 constexpr int kMaxOutMaps = 8;
 struct alignas(64) OutMaps {
   CUtensorMap m[kMaxOutMaps];
+  // Block-scaled kind: scale-factor atoms of A and B (rows of 128 bytes,
+  // four rows = one 512-byte atom of 128 rows x 4 K-blocks).
+  CUtensorMap sfa, sfb;
   int n;
 };
 
@@ -687,8 +693,16 @@ struct Cfg2 {
   static constexpr int HALF_N = BN / 2;  // B rows (K-major) / columns (MN-major) per CTA
   static constexpr int A_BYTES = kBM * kBKBytes;
   static constexpr int B_BYTES = HALF_N * kBKBytes;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int TMEM_COLS = 2 * BN;
+  // Block-scaled kind: per stage the scale atoms of this CTA's 128 A rows
+  // and of all BN B rows (each CTA's TMEM needs the scales of every B row).
+  static constexpr bool MX = KIND == MmaKind::MXF8;
+  static constexpr int SFA_BYTES = MX ? 512 : 0;
+  static constexpr int SFB_BYTES = MX ? (BN / 128) * 512 : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
+  // accumulators (2 x BN columns), then the scale words: SFA (4 columns)
+  // and SFB (4 columns per 128 B rows)
+  static constexpr int SF_COL = 2 * BN;
+  static constexpr int TMEM_COLS = MX ? 512 : 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
   static constexpr int BAR_BYTES = 256;
@@ -708,6 +722,7 @@ struct Cfg2 {
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(!B_MN || B_CHUNKS >= 1, "MN-major B needs whole 128-byte chunks per CTA");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
+  static_assert(!MX || (BN % 128 == 0 && !B_MN && SF_COL + 4 + BN / 32 <= TMEM_COLS), "MX tile");
 };
 
 __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint32_t peer_abort) {
@@ -727,6 +742,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                               ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sB = smem + C::STAGES * C::A_BYTES;
+  uint8_t *sSF = sB + C::STAGES * C::B_BYTES;  // block-scaled kind: [stage][SFA | SFB]
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
   uint64_t *empty = full + C::STAGES;
   uint64_t *tfull = empty + C::STAGES;  // [2]
@@ -757,6 +773,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (args.split > 1) tma_prefetch_desc(&tmB2);
+    if constexpr (C::MX) {
+      tma_prefetch_desc(&om.sfa);
+      tma_prefetch_desc(&om.sfb);
+    }
   }
   if (warp == 2) {
     tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
@@ -783,7 +803,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;  // this CTA's A rows
       const int n0 = nb * BN + part * (BN / parts) + static_cast<int>(rank) * half_w;
       const CUtensorMap *tb = parts > 1 ? &tmB2 : &tmB;
-      const uint32_t tx = 2u * static_cast<uint32_t>(C::A_BYTES + half_w * kBKBytes);
+      const uint32_t tx =
+          2u * static_cast<uint32_t>(C::A_BYTES + half_w * kBKBytes + C::SFA_BYTES + C::SFB_BYTES);
       int cw = 0, ch = 0, cn = 0;
       if constexpr (CONV) conv_box(args, m0, cw, ch, cn);
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
@@ -804,6 +825,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                   static_cast<uint16_t>(kc), static_cast<uint16_t>(kr));
         } else {
           tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, bar, kx, m0);
+        }
+        if constexpr (C::MX) {  // scale atoms: A rows m0.., all BN B rows of the tile
+          uint8_t *sf = sSF + s * (C::SFA_BYTES + C::SFB_BYTES);
+          tma_load_2d_pair(sf, &om.sfa, bar, 0, ((m0 / kBM) * args.sf_kblocks + kb) * 4);
+#pragma unroll
+          for (int j = 0; j < BN / 128; ++j)
+            tma_load_2d_pair(sf + C::SFA_BYTES + j * 512, &om.sfb, bar, 0,
+                             ((nb * BN / 128 + j) * args.sf_kblocks + kb) * 4);
         }
         if constexpr (!B_MN) {
           tma_load_2d_pair(sB + s * C::B_BYTES, tb, bar, kx, n0);
@@ -835,7 +864,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;
     constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : (KIND == MmaKind::TF32 ? 2u : 0u);
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
-    const uint32_t idesc_full = make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
+    const uint32_t idesc_full =
+        C::MX ? make_idesc_mx(static_cast<uint32_t>(args.mx_fmt_a), static_cast<uint32_t>(args.mx_fmt_b),
+                              2 * kBM, BN, 1u, 0u, 0u)
+              : make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
     const uint32_t idesc_part =
         make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN / (args.split > 1 ? args.split : 1));
     const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
@@ -865,13 +897,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_fence_after_sync();
         const uint32_t a0 = smem_u32(sA + s * C::A_BYTES);
         const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
+        if constexpr (C::MX) {
+          // This stage's scale atoms into TMEM (after the previous k-block's
+          // MMAs, which read the same columns: same-thread order), then one
+          // MMA per 32 K reading byte k of every scale word.
+          const uint32_t sf0 = smem_u32(sSF + s * (C::SFA_BYTES + C::SFB_BYTES));
+          const uint32_t t_sfa = tmem_base + static_cast<uint32_t>(C::SF_COL);
+          const uint32_t t_sfb = t_sfa + 4u;
+          tc_cp_32x128b_x4_pair(t_sfa, smem_desc_noswizzle(sf0, 128, 128));
 #pragma unroll
-        for (int k = 0; k < C::BK / C::UMMA_K; ++k) {
-          const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
-          const uint64_t bdesc =
-              B_MN ? smem_desc_sw128(b0 + k * C::UMMA_K * kBKBytes, C::B_CHUNK_BYTES, 1024)
-                   : smem_desc_sw128(b0 + k * 32, 16, 1024);
-          umma_pair<KIND>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int j = 0; j < BN / 128; ++j)
+            tc_cp_32x128b_x4_pair(t_sfb + 4u * j,
+                                  smem_desc_noswizzle(sf0 + C::SFA_BYTES + 512 * j, 128, 128));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t kk = static_cast<uint32_t>(k);
+            umma_mx_pair(d_tmem, smem_desc_sw128(a0 + k * 32, 16, 1024),
+                         smem_desc_sw128(b0 + k * 32, 16, 1024),
+                         idesc | (kk << 29) | (kk << 4), t_sfa | (kk << 30), t_sfb | (kk << 30),
+                         (kb | k) != 0 ? 1u : 0u);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < C::BK / C::UMMA_K; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bdesc =
+                B_MN ? smem_desc_sw128(b0 + k * C::UMMA_K * kBKBytes, C::B_CHUNK_BYTES, 1024)
+                     : smem_desc_sw128(b0 + k * 32, 16, 1024);
+            umma_pair<KIND>(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
         }
         issued = true;
         tc_commit_pair(smem_u32(&empty[s]));
@@ -964,6 +1018,17 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
     if (s != ROUGE_B200_OK) return s;
     tc.n = 1;
   }
+  if constexpr (KIND == MmaKind::MXF8) {
+    // scale atoms as 128-byte rows, 4 rows per atom, no swizzle
+    const uint64_t rows_a = static_cast<uint64_t>((args.M + 127) / 128) * args.sf_kblocks * 4;
+    const uint64_t rows_b = static_cast<uint64_t>((args.N + 127) / 128) * args.sf_kblocks * 4;
+    s = make_tmap_2d(&tc.sfa, args.scales_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, rows_a, 128, 128,
+                     4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (s == ROUGE_B200_OK)
+      s = make_tmap_2d(&tc.sfb, args.scales_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, rows_b, 128, 128,
+                       4, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (s != ROUGE_B200_OK) return s;
+  }
 
   const unsigned long long bit = 1ull << (current_device() & 63);
   const int sms = current_sm_count();
@@ -1034,7 +1099,7 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
 #ifndef RB200_MAX_SPLIT  // largest N-split of the last round (tuning builds)
 #define RB200_MAX_SPLIT 2
 #endif
-    if (!B_MN && rem) {
+    if (!B_MN && rem && KIND != MmaKind::MXF8) {  // (block-scaled: scale atoms span BN)
       for (int f = RB200_MAX_SPLIT; f >= 2; f /= 2) {
         if (rem * f <= clusters) {
           args.split = f;
@@ -1381,11 +1446,56 @@ int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda
   }
 }
 
+// Block-scaled (MXFP8) GEMM on CTA pairs with 256 x 128 tiles:
+// C[M][N] = sum_k (a[m][k] * 2^(sfa - 127)) (b[n][k] * 2^(sfb - 127)),
+// f32 accumulation; A [M][K], B [N][K] e4m3 / e5m2 codes (row pitches lda,
+// ldb bytes), scales in the tcgen05 atom layout (rouge_b200_mx_scale_atoms).
+int launch_gemm_mx(int M, int N, int K, const uint8_t *A, long long lda, int fmt_a,
+                   const uint8_t *sfa, const uint8_t *B, long long ldb, int fmt_b,
+                   const uint8_t *sfb, void *Cp, long long ldc, int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scales_a = reinterpret_cast<const float *>(sfa);
+  g.scales_b = reinterpret_cast<const float *>(sfb);
+  g.mx_fmt_a = fmt_a;
+  g.mx_fmt_b = fmt_b;
+  g.sf_kblocks = (K + 127) / 128;
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.err = device_error_word();
+  g.num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  g.num_n = (N + 127) / 128;
+  g.num_k = (K + 127) / 128;
+  g.num_tiles = g.num_m * g.num_n;
+  if (out_type == ROUGE_B200_OUT_BF16)
+    return launch_gemm_impl<MmaKind::MXF8, 128, false, ROUGE_B200_OUT_BF16, true>(A, lda, B, ldb, g,
+                                                                                  st);
+  return launch_gemm_impl<MmaKind::MXF8, 128, false, ROUGE_B200_OUT_F32, true>(A, lda, B, ldb, g,
+                                                                               st);
+}
+
 }  // namespace rb200
 
 using namespace rb200;
 
 extern "C" {
+
+int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const uint8_t *sfa,
+                       const uint8_t *B, int fmt_b, const uint8_t *sfb, void *C, int ldc,
+                       int out_type, void *stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !sfa || !sfb || !C || ldc < N)
+    return set_status(ROUGE_B200_EINVAL);
+  if ((fmt_a != 0 && fmt_a != 1) || (fmt_b != 0 && fmt_b != 1) ||
+      (out_type != ROUGE_B200_OUT_F32 && out_type != ROUGE_B200_OUT_BF16))
+    return set_status(ROUGE_B200_EINVAL);
+  if (K % 32 || (reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
+      (reinterpret_cast<uintptr_t>(sfa) & 15u) || (reinterpret_cast<uintptr_t>(sfb) & 15u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_gemm_mx(M, N, K, A, K, fmt_a, sfa, B, K, fmt_b, sfb, C, ldc, out_type,
+                        as_stream(stream));
+}
 
 int rouge_b200_set_tile_mode(int mode) {
   if (mode != ROUGE_B200_TILES_AUTO && mode != ROUGE_B200_TILES_SINGLE &&

@@ -143,6 +143,26 @@ __global__ void __launch_bounds__(kMxThreads)
   }
 }
 
+// Scale re-layout for the block-scaled GEMM: src [rows][K/32] (the block
+// quantizer's scales of a row-major [rows][K] matrix) into 512-byte atoms
+// [ceil(rows/128)][ceil(K/128)], atom byte 16*(r%32) + 4*(r/32) + j = the
+// scale of row 128*rb + r, K-block 4*kb + j (the layout tcgen05.cp
+// 32x128b.warpx4 turns into TMEM words: lane r%32, column r/32, byte j).
+// Rows or K-blocks past the matrix get 127 (scale 1: their operand bytes
+// are zero-filled by the GEMM's loads).
+__global__ void mx_scale_atoms_kernel(const uint8_t *__restrict__ src, int rows, int kb32,
+                                      uint8_t *__restrict__ dst, int kb128, size_t atoms) {
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < atoms * 512;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t atom = i >> 9;
+    const int off = static_cast<int>(i & 511);
+    const int rb = static_cast<int>(atom / kb128), kb = static_cast<int>(atom % kb128);
+    const int r = (off >> 4) + 32 * ((off >> 2) & 3), j = off & 3;
+    const int row = rb * 128 + r, col = kb * 4 + j;
+    dst[i] = (row < rows && col < kb32) ? src[static_cast<size_t>(row) * kb32 + col] : 127;
+  }
+}
+
 unsigned grid_for(size_t work_items, int per_block) {
   const size_t need = (work_items + per_block - 1) / per_block;
   const size_t cap = static_cast<size_t>(current_sm_count()) * 8;
@@ -301,6 +321,22 @@ int rouge_b200_nvfp4_quantize(const float *x, size_t n, float global_scale, uint
   if (s != ROUGE_B200_OK) return s;
   if (!(global_scale > 0.0f)) global_scale = 1.0f;
   return launch_nvfp4_quantize(x, n, global_scale, codes, scales, as_stream(stream));
+}
+
+size_t rouge_b200_mx_scale_atoms_bytes(int rows, int K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return static_cast<size_t>((rows + 127) / 128) * ((K + 127) / 128) * 512;
+}
+
+int rouge_b200_mx_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                              void *stream) {
+  if (!scales || !atoms || rows <= 0 || K <= 0 || K % 32) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const size_t n = rouge_b200_mx_scale_atoms_bytes(rows, K) / 512;
+  mx_scale_atoms_kernel<<<grid_for(n * 512, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
+      scales, rows, K / 32, atoms, (K + 127) / 128, n);
+  return cuda_status(cudaGetLastError());
 }
 
 int rouge_b200_mx_dequantize(const uint8_t *codes, const uint8_t *scales, size_t n, int fmt,

@@ -233,7 +233,9 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
 }
 
 // UMMA kinds.
-enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3 };
+// MXF8: kind::mxf8f6f4.block_scale (e4m3 / e5m2 operands, one E8M0 scale
+// per 32 K per row and column, the scales in TMEM).
+enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3, MXF8 = 4 };
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, one instruction, issued by the
 // calling thread. accumulate == 0 overwrites D.
@@ -494,6 +496,55 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
 //   a_fmt/b_fmt: kind::f16: 0 F16, 1 BF16; kind::f8f6f4: 0 E4M3, 1 E5M2;
 //                kind::i8: 0 U8, 1 S8
 //   a_mn/b_mn: 1 = operand is MN-major in shared memory
+// Block-scaled D (+)= (A . sfA)(B . sfB)^T, kind::mxf8f6f4 with E8M0 scales
+// (scale_vec 1X: one scale per 32 K per row of A and of B), CTA pair,
+// issued by the leader. tmem_sfa / tmem_sfb address the scale words in
+// TMEM; bits 31:30 select the byte of each word, the same value as the
+// scale-factor ids in idesc.
+__device__ __forceinline__ void umma_mx_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t tmem_sfa, uint32_t tmem_sfb,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;"
+      "\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+// Copies a 32-row x 16-byte shared-memory matrix (rows 16 bytes apart, no
+// swizzle) into TMEM lanes 0-31 x 4 columns at taddr, replicated into all
+// four lane quarters. CTA pair form (issued by the leader): each CTA copies
+// its own shared memory at the descriptor's address into its own TMEM.
+// Ordered with the tcgen05.mma the same thread issues before and after it.
+__device__ __forceinline__ void tc_cp_32x128b_x4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// Shared-memory matrix descriptor without swizzle (K-major: 8-row x
+// 16-byte core matrices of 128 contiguous bytes, `sbo_bytes` apart along
+// the rows, `lbo_bytes` apart along K).
+__device__ __forceinline__ uint64_t smem_desc_noswizzle(uint32_t saddr, uint32_t lbo_bytes,
+                                                        uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;  // version 1; layout bits [61,64) = 0: no swizzle
+  return d;
+}
+
+// Instruction descriptor of the block-scaled kinds: a_fmt / b_fmt (E4M3 0,
+// E5M2 1, E2M1 5), both operands K-major, sf_fmt 1 = E8M0 (0 = UE4M3),
+// scale-factor ids (the byte of each TMEM scale word) a_sf_id / b_sf_id.
+__host__ __device__ constexpr uint32_t make_idesc_mx(uint32_t a_fmt, uint32_t b_fmt, uint32_t m,
+                                                     uint32_t n, uint32_t sf_fmt, uint32_t a_sf_id,
+                                                     uint32_t b_sf_id) {
+  return (b_sf_id << 4) | (a_fmt << 7) | (b_fmt << 10) | ((n >> 3) << 17) | (sf_fmt << 23) |
+         ((m >> 4) << 24) | (a_sf_id << 29);
+}
+
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt,
                                                   uint32_t a_mn, uint32_t b_mn, uint32_t m,
                                                   uint32_t n) {

@@ -96,6 +96,9 @@ _SIGS = {
     "rouge_b200_mx_quantize": (_I, [_P, _SZ, _I, _P, _P, _P]),
     "rouge_b200_nvfp4_quantize": (_I, [_P, _SZ, C.c_float, _P, _P, _P]),
     "rouge_b200_mx_dequantize": (_I, [_P, _P, _SZ, _I, _P, _P]),
+    "rouge_b200_mx_scale_atoms_bytes": (_SZ, [_I, _I]),
+    "rouge_b200_mx_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
+    "rouge_b200_gemm_mx": (_I, [_I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _P]),
     "rouge_quantize_e5m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e5m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e3m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e3m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e2m3": (C.c_uint8, [C.c_float]), "rouge_dequantize_e2m3": (C.c_float, [C.c_uint8]),
@@ -220,6 +223,25 @@ def nvfp4_quantize(x, global_scale, codes, scales):
 def mx_dequantize(codes, scales, fmt, out):
     _check("rouge_b200_mx_dequantize", lib().rouge_b200_mx_dequantize(
         _dp(codes), _dp(scales), codes.numel(), fmt, _dp(out), _stream()))
+
+
+def mx_scale_atoms(scales, rows, K, atoms):
+    """[rows][K/32] E8M0 scales -> the tensor-core atom layout of gemm_mx."""
+    _check("rouge_b200_mx_scale_atoms", lib().rouge_b200_mx_scale_atoms(
+        _dp(scales), rows, K, _dp(atoms), _stream()))
+
+
+def mx_scale_atoms_bytes(rows, K):
+    return lib().rouge_b200_mx_scale_atoms_bytes(rows, K)
+
+
+def gemm_mx(A, fmt_a, sfa, B, fmt_b, sfb, C, out_type):
+    """C[M][N] = (A x 2^sfa) . (B x 2^sfb)^T, A [M][K], B [N][K] e4m3/e5m2 codes."""
+    M, K = A.shape
+    N = B.shape[0]
+    _check("rouge_b200_gemm_mx", lib().rouge_b200_gemm_mx(
+        M, N, K, _dp(A), fmt_a, _dp(sfa), _dp(B), fmt_b, _dp(sfb), _dp(C), C.shape[1], out_type,
+        _stream()))
 
 
 def convert_f32_to_f16(x, out):
