@@ -399,11 +399,17 @@ __device__ __forceinline__ void bcast_flush(const GemmArgs &args, const uint8_t 
 // [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`.
 // Two 32-column tcgen05.ld loads are kept in flight: chunk c+1 loads while
 // chunk c is converted and stored.
+// Overlapping accumulator buffers (ovl_bar != 0): the warps of column half
+// ovl_half arrive on ovl_bar (a cluster address) once per tile: right after
+// reading chunk ovl_chunk (the chunk shared with the other buffer, which
+// they read first), or at once when the tile does not hold it (ovl_chunk
+// < 0) or it lies past N.
 template <MmaKind KIND, int OUT, int NBUF>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tcol, int m0, int col0,
                                               int width, int quarter, int half, float sab,
                                               uint8_t *stage, int &seq, const OutMaps *om,
-                                              int lane) {
+                                              int lane, uint32_t ovl_bar = 0u, int ovl_half = 0,
+                                              int ovl_chunk = -1) {
   const int row0 = m0 + quarter * 32;
   const int row = row0 + lane;
   const bool row_ok = row < args.M;
@@ -418,10 +424,26 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   const int per_half = width / 64;
   const int c_end = min(nchunks, (half + 1) * per_half);
   const int c_beg = half * per_half;
+  const bool ovl = ovl_bar != 0u && half == ovl_half;
+  const bool ovl_read = ovl && ovl_chunk >= c_beg && ovl_chunk < c_end;
+  auto ovl_done = [&]() {
+    tc_fence_before_sync();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_cluster(ovl_bar);
+  };
+  if (ovl && !ovl_read) ovl_done();  // nothing of the shared chunk is read
   if (c_beg >= c_end) return;
+  // chunk order: the shared chunk first when this warp reads it
+  const int nrot = c_end - c_beg;
+  const int rot = ovl_read ? ovl_chunk - c_beg : 0;
+  auto chunk = [&](int j) {
+    const int k = j + rot;
+    return c_beg + (k >= nrot ? k - nrot : k);
+  };
   uint32_t va[32], vb[32];
-  tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c_beg * 32), va);
+  tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(chunk(0) * 32), va);
   tmem_ld_wait_regs(va);
+  if (ovl_read) ovl_done();
   // staging buffer of this warp's seq-th chunk (the multicast output stages
   // whole lines in the first buffer)
   auto buf = [&]() {
@@ -442,18 +464,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
       bcast_flush<OUT>(args, stage, row0, cc, 0xFFu, lane);
     }
   };
-  for (int c = c_beg; c < c_end; c += 2) {
-    if (c + 1 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 1) * 32), vb);
-    epilogue_chunk<KIND, OUT, NBUF>(args, va, col0 + c * 32, row0, row, row_ok, sa, sa_ok, sab,
-                                    buf(), om, lane);
-    after(c);
-    if (c + 1 < c_end) {
+  // (a rotated order only occurs without multicast output, whose line
+  // flushes assume ascending chunks)
+  for (int j = 0; j < nrot; j += 2) {
+    if (j + 1 < nrot) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(chunk(j + 1) * 32), vb);
+    epilogue_chunk<KIND, OUT, NBUF>(args, va, col0 + chunk(j) * 32, row0, row, row_ok, sa, sa_ok,
+                                    sab, buf(), om, lane);
+    after(chunk(j));
+    if (j + 1 < nrot) {
       tmem_ld_wait_regs(vb);
-      if (c + 2 < c_end) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>((c + 2) * 32), va);
-      epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + (c + 1) * 32, row0, row, row_ok, sa, sa_ok,
-                                      sab, buf(), om, lane);
-      after(c + 1);
-      if (c + 2 < c_end) tmem_ld_wait_regs(va);
+      if (j + 2 < nrot) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(chunk(j + 2) * 32), va);
+      epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + chunk(j + 1) * 32, row0, row, row_ok, sa,
+                                      sa_ok, sab, buf(), om, lane);
+      after(chunk(j + 1));
+      if (j + 2 < nrot) tmem_ld_wait_regs(va);
     }
   }
 }
@@ -698,10 +722,21 @@ struct Cfg2 {
   static constexpr bool MX = KIND == MmaKind::MXF8;
   static constexpr int SFA_BYTES = MX ? 512 : 0;
   static constexpr int SFB_BYTES = MX ? (BN / 128) * 512 : 0;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SFA_BYTES + SFB_BYTES;
-  // accumulators (2 x BN columns), then the scale words: SFA (4 columns)
-  // and SFB (4 columns per 128 B rows)
-  static constexpr int SF_COL = 2 * BN;
+  // per-stage scale region, padded so that stages stay 1024-byte multiples
+  static constexpr int SF_STAGE = MX ? (SFA_BYTES + SFB_BYTES + 1023) / 1024 * 1024 : 0;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE;
+  // TMEM: accumulator buffer 0 at column 0, buffer 1 at ACC1_COL, then
+  // SF_BUFS rotating sets of scale words (SFA: 4 columns, SFB: 4 columns
+  // per 128 B rows). A 256-wide block-scaled tile leaves no room for two
+  // disjoint buffers and the scales: its buffers overlap in 32 columns
+  // (buffer 0's last chunk is buffer 1's first), which each tile's
+  // epilogue drains first and reports on its own barrier.
+  static constexpr int SF_SET = 4 + BN / 32;
+  static constexpr int SF_COL = MX && BN == 256 ? 480 : 2 * BN;
+  static constexpr int SF_BUFS = MX && BN == 256 ? 2 : 4;
+  static constexpr int ACC1_COL = MX && BN == 256 ? SF_COL - BN : BN;
+  static constexpr bool OVERLAP = ACC1_COL < BN;
+  static_assert(!OVERLAP || BN - ACC1_COL == 32, "one shared 32-column chunk");
   static constexpr int TMEM_COLS = MX ? 512 : 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
@@ -719,10 +754,13 @@ struct Cfg2 {
 #endif
   static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+  static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(!B_MN || B_CHUNKS >= 1, "MN-major B needs whole 128-byte chunks per CTA");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
-  static_assert(!MX || (BN % 128 == 0 && !B_MN && SF_COL + 4 + BN / 32 <= TMEM_COLS), "MX tile");
+  static_assert(ACC1_COL + BN <= (MX ? SF_COL : TMEM_COLS), "accumulators below the scales");
+  static_assert(!MX || (BN % 128 == 0 && !B_MN && SF_COL + SF_BUFS * SF_SET <= TMEM_COLS),
+                "MX tile");
 };
 
 __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint32_t peer_abort) {
@@ -748,7 +786,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *tfull = empty + C::STAGES;  // [2]
   uint64_t *tempty = tfull + 2;         // [2]
   uint64_t *mdone = tempty + 2;         // [1]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mdone + 1);
+  uint64_t *ovl = mdone + 1;            // [2] overlapping accumulators: shared chunk drained
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ovl + 2);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -766,6 +805,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 16);
+      mbar_init(&ovl[i], 8);  // the 4 warps of one column half, both CTAs
     }
     mbar_init(mdone, 1);
     *abort = 0;
@@ -827,7 +867,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_load_2d_pair(sA + s * C::A_BYTES, &tmA, bar, kx, m0);
         }
         if constexpr (C::MX) {  // scale atoms: A rows m0.., all BN B rows of the tile
-          uint8_t *sf = sSF + s * (C::SFA_BYTES + C::SFB_BYTES);
+          uint8_t *sf = sSF + s * C::SF_STAGE;
           tma_load_2d_pair(sf, &om.sfa, bar, 0, ((m0 / kBM) * args.sf_kblocks + kb) * 4);
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
@@ -869,7 +909,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                               2 * kBM, BN, 1u, 0u, 0u)
               : make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
     const uint32_t idesc_part =
-        make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN / (args.split > 1 ? args.split : 1));
+        C::MX ? make_idesc_mx(static_cast<uint32_t>(args.mx_fmt_a), static_cast<uint32_t>(args.mx_fmt_b),
+                              2 * kBM, BN / (args.split > 1 ? args.split : 1), 1u, 0u, 0u)
+              : make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM,
+                           BN / (args.split > 1 ? args.split : 1));
     const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
     const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
     int it = 0, local = 0;
@@ -883,9 +926,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         ok = false;
         break;
       }
+      if constexpr (C::OVERLAP) {
+        // the previous tile's epilogue has drained the chunk both buffers share
+        if (local > 0 &&
+            !mbar_wait(&ovl[slot ^ 1], static_cast<uint32_t>((local - 1) >> 1) & 1u, abort)) {
+          report_pair(args.err, abort, peer_abort);
+          ok = false;
+          break;
+        }
+      }
       tc_fence_after_sync();
-      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * BN);
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * C::ACC1_COL);
       const uint32_t idesc = t >= args.split_from ? idesc_part : idesc_full;
+      // block-scaled split unit: its B rows' scale words start 4 columns per
+      // 128 rows into the tile's SFB
+      uint32_t sfb_unit = 0;
+      if constexpr (C::MX) {
+        int mb_, nb_, part_, parts_;
+        unit_coords(t, args, mb_, nb_, part_, parts_);
+        sfb_unit = static_cast<uint32_t>(part_ * (BN / parts_) / 128) * 4u;
+      }
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % C::STAGES;
         const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
@@ -901,8 +961,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // This stage's scale atoms into TMEM (after the previous k-block's
           // MMAs, which read the same columns: same-thread order), then one
           // MMA per 32 K reading byte k of every scale word.
-          const uint32_t sf0 = smem_u32(sSF + s * (C::SFA_BYTES + C::SFB_BYTES));
-          const uint32_t t_sfa = tmem_base + static_cast<uint32_t>(C::SF_COL);
+          const uint32_t sf0 = smem_u32(sSF + s * C::SF_STAGE);
+          const uint32_t t_sfa =
+              tmem_base + static_cast<uint32_t>(C::SF_COL + (it % C::SF_BUFS) * C::SF_SET);
           const uint32_t t_sfb = t_sfa + 4u;
           tc_cp_32x128b_x4_pair(t_sfa, smem_desc_noswizzle(sf0, 128, 128));
 #pragma unroll
@@ -914,8 +975,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint32_t kk = static_cast<uint32_t>(k);
             umma_mx_pair(d_tmem, smem_desc_sw128(a0 + k * 32, 16, 1024),
                          smem_desc_sw128(b0 + k * 32, 16, 1024),
-                         idesc | (kk << 29) | (kk << 4), t_sfa | (kk << 30), t_sfb | (kk << 30),
-                         (kb | k) != 0 ? 1u : 0u);
+                         idesc | (kk << 29) | (kk << 4), t_sfa | (kk << 30),
+                         (t_sfb + sfb_unit) | (kk << 30), (kb | k) != 0 ? 1u : 0u);
           }
         } else {
 #pragma unroll
@@ -946,6 +1007,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 4) >> 2;
     uint8_t *stage = smem + C::STAGES * C::STAGE_BYTES + (warp - 4) * C::EPI_BUFS * kStageBytes;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);  // leader's tempty[0]
+    const uint32_t ovl0 = mapa_shared(smem_u32(ovl), 0);        // leader's ovl[0]
     int local = 0, seq = 0;
     float sab = 1.0f;
     if constexpr (KIND != MmaKind::I8) {
@@ -962,10 +1024,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         break;
       }
       tc_fence_after_sync();
-      epilogue_tile<KIND, OUT, C::EPI_BUFS>(args, tmem_base + static_cast<uint32_t>(slot * BN),
-                                            mb * 2 * kBM + static_cast<int>(rank) * kBM,
-                                            nb * BN + part * (BN / parts), BN / parts, quarter,
-                                            half, sab, stage, seq, &om, lane);
+      epilogue_tile<KIND, OUT, C::EPI_BUFS>(
+          args, tmem_base + static_cast<uint32_t>(slot * C::ACC1_COL),
+          mb * 2 * kBM + static_cast<int>(rank) * kBM, nb * BN + part * (BN / parts), BN / parts,
+          quarter, half, sab, stage, seq, &om, lane,
+          C::OVERLAP ? ovl0 + static_cast<uint32_t>(slot * 8) : 0u,
+          // buffer 0: the shared columns are its chunk ACC1_COL/32 (held
+          // only by full-width tiles); buffer 1: its first chunk
+          slot == 0 ? 1 : 0,
+          slot == 0 ? (BN / parts > C::ACC1_COL ? C::ACC1_COL / 32 : -1) : 0);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
@@ -1099,8 +1166,10 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
 #ifndef RB200_MAX_SPLIT  // largest N-split of the last round (tuning builds)
 #define RB200_MAX_SPLIT 2
 #endif
-    if (!B_MN && rem && KIND != MmaKind::MXF8) {  // (block-scaled: scale atoms span BN)
-      for (int f = RB200_MAX_SPLIT; f >= 2; f /= 2) {
+    // (block-scaled: only halves, whose B rows are one whole scale atom)
+    const int max_split = KIND == MmaKind::MXF8 ? 2 : RB200_MAX_SPLIT;
+    if (!B_MN && rem) {
+      for (int f = max_split; f >= 2; f /= 2) {
         if (rem * f <= clusters) {
           args.split = f;
           break;
@@ -1446,7 +1515,7 @@ int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda
   }
 }
 
-// Block-scaled (MXFP8) GEMM on CTA pairs with 256 x 128 tiles:
+// Block-scaled (MXFP8) GEMM on CTA pairs with 256 x 256 tiles:
 // C[M][N] = sum_k (a[m][k] * 2^(sfa - 127)) (b[n][k] * 2^(sfb - 127)),
 // f32 accumulation; A [M][K], B [N][K] e4m3 / e5m2 codes (row pitches lda,
 // ldb bytes), scales in the tcgen05 atom layout (rouge_b200_mx_scale_atoms).
@@ -1464,13 +1533,13 @@ int launch_gemm_mx(int M, int N, int K, const uint8_t *A, long long lda, int fmt
   g.use_tma_store = vec_ok(Cp, ldc, out_type);
   g.err = device_error_word();
   g.num_m = (M + 2 * kBM - 1) / (2 * kBM);
-  g.num_n = (N + 127) / 128;
+  g.num_n = (N + 255) / 256;
   g.num_k = (K + 127) / 128;
   g.num_tiles = g.num_m * g.num_n;
   if (out_type == ROUGE_B200_OUT_BF16)
-    return launch_gemm_impl<MmaKind::MXF8, 128, false, ROUGE_B200_OUT_BF16, true>(A, lda, B, ldb, g,
+    return launch_gemm_impl<MmaKind::MXF8, 256, false, ROUGE_B200_OUT_BF16, true>(A, lda, B, ldb, g,
                                                                                   st);
-  return launch_gemm_impl<MmaKind::MXF8, 128, false, ROUGE_B200_OUT_F32, true>(A, lda, B, ldb, g,
+  return launch_gemm_impl<MmaKind::MXF8, 256, false, ROUGE_B200_OUT_F32, true>(A, lda, B, ldb, g,
                                                                                st);
 }
 

@@ -57,32 +57,40 @@ __global__ void __launch_bounds__(kMxThreads)
     mx_quant_kernel(const float *__restrict__ x, size_t n, uint8_t *__restrict__ codes,
                     uint8_t *__restrict__ scales, int vec_in, int vec_out) {
   constexpr float kEmax = ID == kE4M3 ? 448.0f : ID == kE5M2 ? 57344.0f : 6.0f;
+  constexpr int kU = 4;  // groups of 4 blocks per warp iteration: kU loads in flight per lane
   const size_t nblk = (n + 31) / 32;
   const int lane = threadIdx.x & 31, sub = lane & 7;
   const size_t nwarps = (static_cast<size_t>(gridDim.x) * blockDim.x) >> 5;
-  for (size_t b0 = ((static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 4;
-       b0 < nblk; b0 += nwarps * 4) {
-    const size_t blk = b0 + (lane >> 3);
-    const size_t e0 = blk * 32 + sub * 4;
-    const float4 v = blk < nblk ? load4(x, e0, n, vec_in) : make_float4(0.f, 0.f, 0.f, 0.f);
-    float a = amax4(v);
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
-    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
-    const uint32_t sc = mx_scale_code(a > 0.0f ? block_pow(a, kEmax) : 0);
-    const float inv = e8m0_inverse(sc);
-    if (blk >= nblk) continue;
-    if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
-    // x86 products: a NaN element keeps its sign (the code is sign|0x7F)
-    const float4 s = make_float4(x86_mul_fast(v.x, inv), x86_mul_fast(v.y, inv),
-                                 x86_mul_fast(v.z, inv), x86_mul_fast(v.w, inv));
-    uint32_t w;
-    if constexpr (ID == kE2M1)
-      w = encode_e2m1(s.x) | (encode_e2m1(s.y) << 8) | (encode_e2m1(s.z) << 16) |
-          (encode_e2m1(s.w) << 24);
-    else
-      w = encode4_f8<ID>(s);
-    store4(codes, e0, n, vec_out, w);
+  for (size_t b0 = ((static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 4 * kU;
+       b0 < nblk; b0 += nwarps * 4 * kU) {
+    float4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const size_t blk = b0 + u * 4 + (lane >> 3);
+      v[u] = blk < nblk ? load4(x, blk * 32 + sub * 4, n, vec_in) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const size_t blk = b0 + u * 4 + (lane >> 3);
+      float a = amax4(v[u]);
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+      const uint32_t sc = mx_scale_code(a > 0.0f ? block_pow(a, kEmax) : 0);
+      const float inv = e8m0_inverse(sc);
+      if (blk >= nblk) continue;
+      if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
+      // x86 products: a NaN element keeps its sign (the code is sign|0x7F)
+      const float4 s = make_float4(x86_mul_fast(v[u].x, inv), x86_mul_fast(v[u].y, inv),
+                                   x86_mul_fast(v[u].z, inv), x86_mul_fast(v[u].w, inv));
+      uint32_t w;
+      if constexpr (ID == kE2M1)
+        w = encode_e2m1(s.x) | (encode_e2m1(s.y) << 8) | (encode_e2m1(s.z) << 16) |
+            (encode_e2m1(s.w) << 24);
+      else
+        w = encode4_f8<ID>(s);
+      store4(codes, blk * 32 + sub * 4, n, vec_out, w);
+    }
   }
 }
 
@@ -176,7 +184,7 @@ bool a4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 int launch_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_t *scales,
                        cudaStream_t st) {
-  const unsigned grid = grid_for((n + 31) / 32, kMxThreads / 8);
+  const unsigned grid = grid_for((n + 31) / 32, kMxThreads / 8 * 4);
   const int vi = a16(x), vo = a4(codes);
   switch (fmt) {
     case kE4M3: mx_quant_kernel<kE4M3><<<grid, kMxThreads, 0, st>>>(x, n, codes, scales, vi, vo); break;

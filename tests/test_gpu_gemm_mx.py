@@ -41,8 +41,10 @@ def test_scale_atom_layout(rb, cuda):
                     assert atom[16 * (r % 32) + 4 * (r // 32) + j] == want
 
 
+# (4096, 4096, 256): 256 tiles on 74 CTA pairs, the last round's 34 tiles cut
+# into 68 half-width units: full tiles and units share one launch
 @pytest.mark.parametrize("M,N,K", [(256, 128, 128), (512, 256, 1024), (300, 200, 96),
-                                   (1000, 384, 544), (2048, 2048, 4096)])
+                                   (1000, 384, 544), (2048, 2048, 4096), (4096, 4096, 256)])
 @pytest.mark.parametrize("fa,fb", [("e4m3", "e4m3"), ("e5m2", "e5m2"), ("e4m3", "e5m2")])
 def test_gemm_mx_against_oracle(rb, orc, cuda, M, N, K, fa, fb):
     import torch
