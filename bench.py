@@ -605,6 +605,52 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
         del As, Bs, Cs, Ct
         shim.cublasDestroy_v2(h)
 
+    # MX formats: MXFP8 block quantization of 8192^2
+    # f32 (e4m3 codes + E8M0 scale per 32) and the block-scaled tcgen05 GEMM
+    # 8192^3 on those codes, checked against the oracle (exact decode, f64
+    # sums) on sampled rows.
+    nm = 8192
+    xa = torch.from_numpy(rb.synth_normal(11, (nm, nm), 0.0, 1.0)).to(dev)
+    xb = torch.from_numpy(rb.synth_normal(12, (nm, nm), 0.0, 1.0)).to(dev)
+    qa = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    qb = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    sa = torch.empty((nm, nm // 32), dtype=torch.uint8, device=dev)
+    sb = torch.empty((nm, nm // 32), dtype=torch.uint8, device=dev)
+    t_q = time_launch(torch, lambda: rb.mx_quantize(xa, rb.FMT_E4M3, qa, sa), flush)
+    rb.mx_quantize(xb, rb.FMT_E4M3, qb, sb)
+    ta = torch.empty(rb.mx_scale_atoms_bytes(nm, nm), dtype=torch.uint8, device=dev)
+    tb = torch.empty_like(ta)
+    t_atoms = time_launch(torch, lambda: rb.mx_scale_atoms(sa, nm, nm, ta), flush)
+    rb.mx_scale_atoms(sb, nm, nm, tb)
+    cm = torch.empty((nm, nm), dtype=torch.bfloat16, device=dev)
+    t_g = time_launch(torch, lambda: rb.gemm_mx(qa, rb.FMT_E4M3, ta, qb, rb.FMT_E4M3, tb, cm,
+                                                rb.OUT_BF16), flush)
+    rb.sync_status()
+    rows = [0, 1, 4095, 8191]
+    xs = xa[rows].cpu().numpy()
+    wq, ws = orc.mx_quantize(xs, "e4m3")
+    codes_ok = bool((qa[rows].cpu().numpy().ravel() == wq).all()
+                    and (sa[rows].cpu().numpy().ravel() == ws).all())
+    A = orc.mx_dequantize(qa[rows].cpu().numpy(), sa[rows].cpu().numpy(), "e4m3").reshape(4, nm)
+    B = orc.mx_dequantize(qb.cpu().numpy(), sb.cpu().numpy(), "e4m3").reshape(nm, nm)
+    want = A.astype(np.float64) @ B.T.astype(np.float64)
+    got = cm[rows].float().cpu().numpy()
+    err = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    fl = 2.0 * nm ** 3
+    qbytes = nm * nm * (4 + 1) + nm * nm // 32
+    out["mxfp8_8192"] = {
+        "quantize_ms": round(t_q, 4), "quantize_gbs": round(qbytes / (t_q * 1e-3) / 1e9, 1),
+        "quantize_hbm_frac": round(qbytes / (t_q * 1e-3) / 1e9 / hbm, 4),
+        "scale_atoms_ms": round(t_atoms, 4),
+        "gemm_ms": round(t_g, 4), "gemm_tflops": round(fl / (t_g * 1e-3) / 1e12, 1),
+        "gemm_frac": round(fl / (t_g * 1e-3) / 1e12 / tc8, 4),
+        "codes_and_scales_bit_exact_sampled_rows": codes_ok, "rel_l2_sampled_rows": err,
+        "kernels": "mx_quant_kernel<e4m3>; gemm_tc2_kernel<MXF8> (kind::mxf8f6f4.block_scale, "
+                   "256x256 CTA-pair tiles, overlapping TMEM accumulators)",
+        "peak": f"gemm vs 2 x {peak_src} bf16; quantize vs {peak_src} HBM "
+                "(5 B/element + 1/32 B scale)"}
+    del xa, xb, qa, qb, sa, sb, ta, tb, cm
+
     # cuDNN-API library: cudnnConvolutionForward at the config-4 shape
     # (N=32, 56x56, 256 -> 256, 3x3 s1 p1), HALF + NHWC (direct: no
     # workspace, alpha / beta in the epilogue, f16 out) and FLOAT + NCHW

@@ -48,12 +48,35 @@ __device__ __forceinline__ float amax4(float4 v) {
   return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 }
 
+// e4m3 / e5m2 codes of x * inv for an MX block (inv = 2^(127 - scale code),
+// so every finite |x * inv| <= emax / 2: the reference's overflow edges are
+// out of reach). The hardware conversion equals the reference except for
+// NaN (sign kept by the reference) and for nonzero magnitudes below half
+// the smallest subnormal, which the hardware rounds to a signed zero and
+// the reference to +0. Both show cheaply per group of four: a NaN makes
+// the sum NaN, a signed zero is a 0x80 byte; such groups take the exact
+// path (x86 products, the reference encoder).
+template <int ID>
+__device__ __forceinline__ uint32_t mx_encode4_f8(float4 x, float inv) {
+  const float sum = (x.x + x.y) + (x.z + x.w);
+  const uint32_t lo = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv))
+                                  : cvt_pair_e5m2(__fmul_rn(x.x, inv), __fmul_rn(x.y, inv));
+  const uint32_t hi = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(x.z, inv), __fmul_rn(x.w, inv))
+                                  : cvt_pair_e5m2(__fmul_rn(x.z, inv), __fmul_rn(x.w, inv));
+  const uint32_t w = lo | (hi << 16);
+  if (sum == sum && __vcmpeq4(w, 0x80808080u) == 0u) return w;
+  return narrow_encode(x86_mul(x.x, inv), ID, false) |
+         (narrow_encode(x86_mul(x.y, inv), ID, false) << 8) |
+         (narrow_encode(x86_mul(x.z, inv), ID, false) << 16) |
+         (narrow_encode(x86_mul(x.w, inv), ID, false) << 24);
+}
+
 // MXFP8 (ID e4m3 / e5m2) and MXFP4 (e2m1): narrow.cpp:200-265. The block
 // maximum ignores NaN (the reference's strict comparison does);
 // scale 2^p with the smallest p >= 0 such that amax <= emax * 2^p, stored
 // as E8M0 code p + 128, elements encoded from x * 2^(127 - code).
 template <int ID>
-__global__ void __launch_bounds__(kMxThreads)
+__global__ void __launch_bounds__(kMxThreads, 8)
     mx_quant_kernel(const float *__restrict__ x, size_t n, uint8_t *__restrict__ codes,
                     uint8_t *__restrict__ scales, int vec_in, int vec_out) {
   constexpr float kEmax = ID == kE4M3 ? 448.0f : ID == kE5M2 ? 57344.0f : 6.0f;
@@ -80,15 +103,14 @@ __global__ void __launch_bounds__(kMxThreads)
       const float inv = e8m0_inverse(sc);
       if (blk >= nblk) continue;
       if (sub == 0) scales[blk] = static_cast<uint8_t>(sc);
-      // x86 products: a NaN element keeps its sign (the code is sign|0x7F)
-      const float4 s = make_float4(x86_mul_fast(v[u].x, inv), x86_mul_fast(v[u].y, inv),
-                                   x86_mul_fast(v[u].z, inv), x86_mul_fast(v[u].w, inv));
       uint32_t w;
-      if constexpr (ID == kE2M1)
-        w = encode_e2m1(s.x) | (encode_e2m1(s.y) << 8) | (encode_e2m1(s.z) << 16) |
-            (encode_e2m1(s.w) << 24);
-      else
-        w = encode4_f8<ID>(s);
+      if constexpr (ID == kE2M1) {
+        // (the sign of a NaN does not matter: e2m1 codes it +MAX)
+        w = encode_e2m1(__fmul_rn(v[u].x, inv)) | (encode_e2m1(__fmul_rn(v[u].y, inv)) << 8) |
+            (encode_e2m1(__fmul_rn(v[u].z, inv)) << 16) | (encode_e2m1(__fmul_rn(v[u].w, inv)) << 24);
+      } else {
+        w = mx_encode4_f8<ID>(v[u], inv);
+      }
       store4(codes, blk * 32 + sub * 4, n, vec_out, w);
     }
   }
