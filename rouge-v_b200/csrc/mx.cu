@@ -116,6 +116,76 @@ __global__ void __launch_bounds__(kMxThreads, 8)
   }
 }
 
+// MXFP8 fast kernel (e4m3 / e5m2, whole blocks, 16-byte aligned x and
+// codes): two lanes per 32-element block, 16 consecutive elements (four
+// float4) per lane, so that the block maximum takes one shuffle and the
+// scale work is shared by 16 elements; the codes leave as one 16-byte
+// store per lane. The hardware codes equal the reference's (see
+// mx_encode4_f8) except for NaN inputs (codes 0x7F / 0xFF, which no finite
+// |x * inv| <= emax / 2 produces) and for 0x80 bytes: those are redone per
+// element (a 0x80 byte stands for -0, -2^-10 in e4m3 or -2^-17 in e5m2,
+// kept by the reference, or a tinier negative value, which it makes +0).
+template <int ID>
+__global__ void __launch_bounds__(kMxThreads, 4)
+    mx_quant_blocks_kernel(const float4 *__restrict__ x, uint32_t nblk, uint4 *__restrict__ codes,
+                           uint8_t *__restrict__ scales) {
+  constexpr float kEmax = ID == kE4M3 ? 448.0f : 57344.0f;
+  constexpr float kTiny = ID == kE4M3 ? 0.0009765625f : 7.62939453125e-06f;  // 2^-10, 2^-17
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t stride = (gridDim.x * blockDim.x) >> 1;  // blocks per grid step
+  for (uint32_t blk = (blockIdx.x * blockDim.x + threadIdx.x) >> 1; ; blk += stride) {
+    // (warp-uniform exit: all lanes of a warp cover 16 consecutive blocks)
+    if (__shfl_sync(0xffffffffu, blk, 0) >= nblk) break;
+    const bool live = blk < nblk;
+    const uint32_t q0 = blk * 8u + (lane & 1u) * 4u;  // first float4 of this lane
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = live ? __ldg(x + q0 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    float a = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a = fmaxf(a, amax4(v[j]));
+    a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+    const uint32_t sc = mx_scale_code(a > kEmax ? block_pow(a, kEmax) : 0);
+    const float inv = e8m0_inverse(sc);
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lo = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv))
+                                      : cvt_pair_e5m2(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv));
+      const uint32_t hi = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv))
+                                      : cvt_pair_e5m2(__fmul_rn(v[j].z, inv), __fmul_rn(v[j].w, inv));
+      w[j] = lo | (hi << 16);
+    }
+    // bytes with (b & 0x7F) == 0x7F (NaN) or b == 0x80
+    uint32_t odd = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t t = w[j] ^ 0x80808080u;
+      odd |= (((w[j] & 0x7F7F7F7Fu) + 0x01010101u) | ((t - 0x01010101u) & ~t)) & 0x80808080u;
+    }
+    if (odd) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t b = (w[j] >> (8 * i)) & 0xFFu;
+          if (b == 0x80u || (b & 0x7Fu) == 0x7Fu) {
+            const float y = x86_mul(e[i], inv);
+            const uint32_t c = (b == 0x80u && y != 0.0f && fabsf(y) < kTiny)
+                                   ? 0u
+                                   : narrow_encode(y, ID, false);
+            w[j] = (w[j] & ~(0xFFu << (8 * i))) | (c << (8 * i));
+          }
+        }
+      }
+    }
+    if (!live) continue;
+    if ((lane & 1u) == 0) scales[blk] = static_cast<uint8_t>(sc);
+    codes[blk * 2u + (lane & 1u)] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // NVFP4: narrow.cpp:270-300. Blocks of 16 e2m1 codes, 4 lanes per block;
 // block maximum of |x| * gs, block scale 2^p coded by the generic e4m3
 // encoder (2^9 and above saturate to 448), elements x * (1 / (scale * gs)).
@@ -206,6 +276,28 @@ bool a4(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 int launch_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_t *scales,
                        cudaStream_t st) {
+  // MXFP8 with aligned operands: whole blocks by the fast kernel, a partial
+  // last block by the general one
+  const size_t full = n / 32;
+  if ((fmt == kE4M3 || fmt == kE5M2) && a16(x) && a16(codes) && full > 0 && full < (1u << 28)) {
+    const size_t want = (full + kMxThreads / 2 - 1) / (kMxThreads / 2);
+    const size_t cap = static_cast<size_t>(current_sm_count()) * 4;  // resident CTAs
+    const unsigned g = static_cast<unsigned>(want < cap ? want : cap);
+    if (fmt == kE4M3)
+      mx_quant_blocks_kernel<kE4M3><<<g, kMxThreads, 0, st>>>(
+          reinterpret_cast<const float4 *>(x), static_cast<uint32_t>(full),
+          reinterpret_cast<uint4 *>(codes), scales);
+    else
+      mx_quant_blocks_kernel<kE5M2><<<g, kMxThreads, 0, st>>>(
+          reinterpret_cast<const float4 *>(x), static_cast<uint32_t>(full),
+          reinterpret_cast<uint4 *>(codes), scales);
+    const int s = cuda_status(cudaGetLastError());
+    if (s != ROUGE_B200_OK || full * 32 == n) return s;
+    x += full * 32;
+    codes += full * 32;
+    scales += full;
+    n -= full * 32;
+  }
   const unsigned grid = grid_for((n + 31) / 32, kMxThreads / 8 * 4);
   const int vi = a16(x), vo = a4(codes);
   switch (fmt) {
