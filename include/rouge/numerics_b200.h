@@ -407,6 +407,21 @@ int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const u
                        const uint8_t *B, int fmt_b, const uint8_t *sfb, void *C, int ldc,
                        int out_type, void *stream);
 
+/* Block-scaled NVFP4 GEMM (kind::mxf4nvf4.block_scale.scale_vec::4X):
+ * C[M][N] = gs_a * gs_b * sum_k (a * sa)(b * sb), a / b the e2m1 codes of
+ * rouge_nvfp4_quantize packed two per byte by rouge_b200_fp4_pack (A
+ * [M][K/2], B [N][K/2] bytes, K % 32 == 0), sa / sb their UE4M3 block
+ * scales (one per 16 K, [rows][K/16]) laid out by
+ * rouge_b200_nvfp4_scale_atoms, gs_a / gs_b device pointers to the global
+ * scales (both null: 1). f32 accumulation; f32 or bf16 output. */
+size_t rouge_b200_nvfp4_scale_atoms_bytes(int rows, int K);
+int rouge_b200_nvfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                                 void *stream);
+int rouge_b200_fp4_pack(const uint8_t *codes, size_t n, uint8_t *packed, void *stream);
+int rouge_b200_gemm_nvfp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa,
+                          const float *gs_a, const uint8_t *B, const uint8_t *sfb,
+                          const float *gs_b, void *C, int ldc, int out_type, void *stream);
+
 /* Convolution forward with cuDNN's semantics (the operation the reference
  * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU
  * conv): Y = alpha * conv(X, Wt) + beta * Y, cross-correlation, symmetric

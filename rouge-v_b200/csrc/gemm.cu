@@ -409,7 +409,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
                                               int width, int quarter, int half, float sab,
                                               uint8_t *stage, int &seq, const OutMaps *om,
                                               int lane, uint32_t ovl_bar = 0u, int ovl_half = 0,
-                                              int ovl_chunk = -1) {
+                                              int ovl_chunk = -1, int ovl_count = 1) {
   const int row0 = m0 + quarter * 32;
   const int row = row0 + lane;
   const bool row_ok = row < args.M;
@@ -425,17 +425,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   const int c_end = min(nchunks, (half + 1) * per_half);
   const int c_beg = half * per_half;
   const bool ovl = ovl_bar != 0u && half == ovl_half;
-  const bool ovl_read = ovl && ovl_chunk >= c_beg && ovl_chunk < c_end;
+  // shared chunks this warp reads (they lead the order; the arrival follows
+  // the last of them)
+  const int ovl_n = (ovl && ovl_chunk >= c_beg && ovl_chunk < c_end)
+                        ? min(ovl_count, c_end - ovl_chunk) : 0;
   auto ovl_done = [&]() {
     tc_fence_before_sync();
     __syncwarp();
     if (lane == 0) mbar_arrive_cluster(ovl_bar);
   };
-  if (ovl && !ovl_read) ovl_done();  // nothing of the shared chunk is read
+  if (ovl && ovl_n == 0) ovl_done();  // nothing of the shared chunks is read
   if (c_beg >= c_end) return;
-  // chunk order: the shared chunk first when this warp reads it
   const int nrot = c_end - c_beg;
-  const int rot = ovl_read ? ovl_chunk - c_beg : 0;
+  const int rot = ovl_n ? ovl_chunk - c_beg : 0;
   auto chunk = [&](int j) {
     const int k = j + rot;
     return c_beg + (k >= nrot ? k - nrot : k);
@@ -443,7 +445,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   uint32_t va[32], vb[32];
   tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(chunk(0) * 32), va);
   tmem_ld_wait_regs(va);
-  if (ovl_read) ovl_done();
+  int loaded = 1;
+  if (ovl_n == 1) ovl_done();
   // staging buffer of this warp's seq-th chunk (the multicast output stages
   // whole lines in the first buffer)
   auto buf = [&]() {
@@ -473,11 +476,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
     after(chunk(j));
     if (j + 1 < nrot) {
       tmem_ld_wait_regs(vb);
+      if (++loaded == ovl_n) ovl_done();
       if (j + 2 < nrot) tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(chunk(j + 2) * 32), va);
       epilogue_chunk<KIND, OUT, NBUF>(args, vb, col0 + chunk(j + 1) * 32, row0, row, row_ok, sa,
                                       sa_ok, sab, buf(), om, lane);
       after(chunk(j + 1));
-      if (j + 2 < nrot) tmem_ld_wait_regs(va);
+      if (j + 2 < nrot) {
+        tmem_ld_wait_regs(va);
+        if (++loaded == ovl_n) ovl_done();
+      }
     }
   }
 }
@@ -719,9 +726,14 @@ struct Cfg2 {
   static constexpr int B_BYTES = HALF_N * kBKBytes;
   // Block-scaled kind: per stage the scale atoms of this CTA's 128 A rows
   // and of all BN B rows (each CTA's TMEM needs the scales of every B row).
-  static constexpr bool MX = KIND == MmaKind::MXF8;
-  static constexpr int SFA_BYTES = MX ? 512 : 0;
-  static constexpr int SFB_BYTES = MX ? (BN / 128) * 512 : 0;
+  // block-scaled kinds: one 512-byte scale atom (128 rows x 4 scales) per
+  // 128 rows per ATOMS_K: MXF8 one per stage (4 K-blocks of 32 = the
+  // stage's 128 K), NVF4 four (one per MMA: 4 blocks of 16 = 64 K)
+  static constexpr bool NV = KIND == MmaKind::NVF4;
+  static constexpr bool MX = KIND == MmaKind::MXF8 || NV;
+  static constexpr int ATOMS_K = NV ? 4 : 1;
+  static constexpr int SFA_BYTES = MX ? ATOMS_K * 512 : 0;
+  static constexpr int SFB_BYTES = MX ? (BN / 128) * ATOMS_K * 512 : 0;
   // per-stage scale region, padded so that stages stay 1024-byte multiples
   static constexpr int SF_STAGE = MX ? (SFA_BYTES + SFB_BYTES + 1023) / 1024 * 1024 : 0;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + SF_STAGE;
@@ -731,12 +743,13 @@ struct Cfg2 {
   // disjoint buffers and the scales: its buffers overlap in 32 columns
   // (buffer 0's last chunk is buffer 1's first), which each tile's
   // epilogue drains first and reports on its own barrier.
-  static constexpr int SF_SET = 4 + BN / 32;
-  static constexpr int SF_COL = MX && BN == 256 ? 480 : 2 * BN;
-  static constexpr int SF_BUFS = MX && BN == 256 ? 2 : 4;
+  static constexpr int SF_SET = ATOMS_K * (4 + BN / 32);  // MXF8 12, NVF4 48 columns (BN 256)
+  static constexpr int SF_COL = MX && BN == 256 ? (NV ? 448 : 480) : 2 * BN;
+  static constexpr int SF_BUFS = MX && BN == 256 ? (NV ? 1 : 2) : (NV ? 1 : 4);
   static constexpr int ACC1_COL = MX && BN == 256 ? SF_COL - BN : BN;
-  static constexpr bool OVERLAP = ACC1_COL < BN;
-  static_assert(!OVERLAP || BN - ACC1_COL == 32, "one shared 32-column chunk");
+  static constexpr int OVL_CHUNKS = (BN - ACC1_COL) / 32;  // chunks both buffers share
+  static constexpr bool OVERLAP = OVL_CHUNKS > 0;
+  static_assert(OVL_CHUNKS <= 2 && (BN - ACC1_COL) % 32 == 0, "shared chunks");
   static constexpr int TMEM_COLS = MX ? 512 : 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
@@ -868,11 +881,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if constexpr (C::MX) {  // scale atoms: A rows m0.., all BN B rows of the tile
           uint8_t *sf = sSF + s * C::SF_STAGE;
-          tma_load_2d_pair(sf, &om.sfa, bar, 0, ((m0 / kBM) * args.sf_kblocks + kb) * 4);
+          constexpr int kRows = 4 * C::ATOMS_K;  // 128-byte rows of this stage's atoms
+          tma_load_2d_pair(sf, &om.sfa, bar, 0, ((m0 / kBM) * args.sf_kblocks + kb) * kRows);
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
-            tma_load_2d_pair(sf + C::SFA_BYTES + j * 512, &om.sfb, bar, 0,
-                             ((nb * BN / 128 + j) * args.sf_kblocks + kb) * 4);
+            tma_load_2d_pair(sf + C::SFA_BYTES + j * C::ATOMS_K * 512, &om.sfb, bar, 0,
+                             ((nb * BN / 128 + j) * args.sf_kblocks + kb) * kRows);
         }
         if constexpr (!B_MN) {
           tma_load_2d_pair(sB + s * C::B_BYTES, tb, bar, kx, n0);
@@ -904,13 +918,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t c_fmt = KIND == MmaKind::I8 ? 2u : 1u;
     constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : (KIND == MmaKind::TF32 ? 2u : 0u);
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
+    // block-scaled: E8M0 scales (format 1) for MXF8, UE4M3 (0) for NVF4
+    constexpr uint32_t sf_fmt = C::NV ? 0u : 1u;
     const uint32_t idesc_full =
         C::MX ? make_idesc_mx(static_cast<uint32_t>(args.mx_fmt_a), static_cast<uint32_t>(args.mx_fmt_b),
-                              2 * kBM, BN, 1u, 0u, 0u)
+                              2 * kBM, BN, sf_fmt, 0u, 0u)
               : make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM, BN);
     const uint32_t idesc_part =
         C::MX ? make_idesc_mx(static_cast<uint32_t>(args.mx_fmt_a), static_cast<uint32_t>(args.mx_fmt_b),
-                              2 * kBM, BN / (args.split > 1 ? args.split : 1), 1u, 0u, 0u)
+                              2 * kBM, BN / (args.split > 1 ? args.split : 1), sf_fmt, 0u, 0u)
               : make_idesc(c_fmt, ab, ab, 0u, B_MN ? 1u : 0u, 2 * kBM,
                            BN / (args.split > 1 ? args.split : 1));
     const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
@@ -959,24 +975,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t b0 = smem_u32(sB + s * C::B_BYTES);
         if constexpr (C::MX) {
           // This stage's scale atoms into TMEM (after the previous k-block's
-          // MMAs, which read the same columns: same-thread order), then one
-          // MMA per 32 K reading byte k of every scale word.
+          // MMAs, which read the same columns: same-thread order). MXF8: one
+          // MMA per 32 K reading byte k of every scale word (SFA at t_sf,
+          // SFB at t_sf + 4); NVF4: one MMA per 64 K reading whole words of
+          // its own atoms (SFA k at t_sf + 4k, SFB k at t_sf + 16 + 8k).
           const uint32_t sf0 = smem_u32(sSF + s * C::SF_STAGE);
-          const uint32_t t_sfa =
+          const uint32_t t_sf =
               tmem_base + static_cast<uint32_t>(C::SF_COL + (it % C::SF_BUFS) * C::SF_SET);
-          const uint32_t t_sfb = t_sfa + 4u;
-          tc_cp_32x128b_x4_pair(t_sfa, smem_desc_noswizzle(sf0, 128, 128));
+          constexpr uint32_t kSfbCol = 4u * C::ATOMS_K;  // SFB after the SFA atoms
+#pragma unroll
+          for (int a = 0; a < C::ATOMS_K; ++a)
+            tc_cp_32x128b_x4_pair(t_sf + 4u * a, smem_desc_noswizzle(sf0 + 512 * a, 128, 128));
 #pragma unroll
           for (int j = 0; j < BN / 128; ++j)
-            tc_cp_32x128b_x4_pair(t_sfb + 4u * j,
-                                  smem_desc_noswizzle(sf0 + C::SFA_BYTES + 512 * j, 128, 128));
+#pragma unroll
+            for (int a = 0; a < C::ATOMS_K; ++a)
+              tc_cp_32x128b_x4_pair(
+                  t_sf + kSfbCol + static_cast<uint32_t>(a * (BN / 32) + 4 * j),
+                  smem_desc_noswizzle(sf0 + C::SFA_BYTES + 512 * (j * C::ATOMS_K + a), 128, 128));
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const uint32_t kk = static_cast<uint32_t>(k);
-            umma_mx_pair(d_tmem, smem_desc_sw128(a0 + k * 32, 16, 1024),
-                         smem_desc_sw128(b0 + k * 32, 16, 1024),
-                         idesc | (kk << 29) | (kk << 4), t_sfa | (kk << 30),
-                         (t_sfb + sfb_unit) | (kk << 30), (kb | k) != 0 ? 1u : 0u);
+            const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
+            const uint64_t bdesc = smem_desc_sw128(b0 + k * 32, 16, 1024);
+            const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+            if constexpr (C::NV)
+              umma_nvf4_pair(d_tmem, adesc, bdesc, idesc, t_sf + 4u * kk,
+                             t_sf + kSfbCol + kk * (BN / 32) + sfb_unit, acc);
+            else
+              umma_mx_pair(d_tmem, adesc, bdesc, idesc | (kk << 29) | (kk << 4), t_sf | (kk << 30),
+                           (t_sf + kSfbCol + sfb_unit) | (kk << 30), acc);
           }
         } else {
 #pragma unroll
@@ -1032,7 +1060,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           // buffer 0: the shared columns are its chunk ACC1_COL/32 (held
           // only by full-width tiles); buffer 1: its first chunk
           slot == 0 ? 1 : 0,
-          slot == 0 ? (BN / parts > C::ACC1_COL ? C::ACC1_COL / 32 : -1) : 0);
+          slot == 0 ? (BN / parts > C::ACC1_COL ? C::ACC1_COL / 32 : -1) : 0, C::OVL_CHUNKS);
       tc_fence_before_sync();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty0 + static_cast<uint32_t>(slot * 8));
@@ -1085,15 +1113,17 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
     if (s != ROUGE_B200_OK) return s;
     tc.n = 1;
   }
-  if constexpr (KIND == MmaKind::MXF8) {
-    // scale atoms as 128-byte rows, 4 rows per atom, no swizzle
-    const uint64_t rows_a = static_cast<uint64_t>((args.M + 127) / 128) * args.sf_kblocks * 4;
-    const uint64_t rows_b = static_cast<uint64_t>((args.N + 127) / 128) * args.sf_kblocks * 4;
+  if constexpr (KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4) {
+    // scale atoms as 128-byte rows, 4 rows per atom, one stage's atoms
+    // (1 for MXF8, 4 for NVF4) per box, no swizzle
+    const uint32_t box = KIND == MmaKind::NVF4 ? 16u : 4u;
+    const uint64_t rows_a = static_cast<uint64_t>((args.M + 127) / 128) * args.sf_kblocks * box;
+    const uint64_t rows_b = static_cast<uint64_t>((args.N + 127) / 128) * args.sf_kblocks * box;
     s = make_tmap_2d(&tc.sfa, args.scales_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, rows_a, 128, 128,
-                     4, CU_TENSOR_MAP_SWIZZLE_NONE);
+                     box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (s == ROUGE_B200_OK)
       s = make_tmap_2d(&tc.sfb, args.scales_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, rows_b, 128, 128,
-                       4, CU_TENSOR_MAP_SWIZZLE_NONE);
+                       box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (s != ROUGE_B200_OK) return s;
   }
 
@@ -1167,7 +1197,7 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
 #define RB200_MAX_SPLIT 2
 #endif
     // (block-scaled: only halves, whose B rows are one whole scale atom)
-    const int max_split = KIND == MmaKind::MXF8 ? 2 : RB200_MAX_SPLIT;
+    const int max_split = KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4 ? 2 : RB200_MAX_SPLIT;
     if (!B_MN && rem) {
       for (int f = max_split; f >= 2; f /= 2) {
         if (rem * f <= clusters) {
@@ -1543,11 +1573,62 @@ int launch_gemm_mx(int M, int N, int K, const uint8_t *A, long long lda, int fmt
                                                                                st);
 }
 
+// Block-scaled NVFP4 GEMM on CTA pairs, 256 x 256 tiles:
+// C[M][N] = gs_a gs_b sum_k (a[m][k] * sa) (b[n][k] * sb), a / b packed
+// e2m1 (two per byte, the lower-index element in the low nibble; row
+// pitches K / 2 bytes), UE4M3 block scales per 16 K in the tcgen05 atom
+// layout (rouge_b200_nvfp4_scale_atoms), gs_a / gs_b device floats or null.
+int launch_gemm_nvf4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa, const float *gs_a,
+                     const uint8_t *B, const uint8_t *sfb, const float *gs_b, void *Cp,
+                     long long ldc, int out_type, cudaStream_t st) {
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scales_a = reinterpret_cast<const float *>(sfa);
+  g.scales_b = reinterpret_cast<const float *>(sfb);
+  g.scale_a = gs_a && gs_b ? gs_a : nullptr;
+  g.scale_b = gs_a && gs_b ? gs_b : nullptr;
+  g.mx_fmt_a = 1;  // E2M1 of kind::mxf4nvf4
+  g.mx_fmt_b = 1;
+  g.sf_kblocks = (K + 255) / 256;
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.err = device_error_word();
+  g.num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  g.num_n = (N + 255) / 256;
+  g.num_k = (K + 255) / 256;
+  g.num_tiles = g.num_m * g.num_n;
+  const uint64_t kbytes = static_cast<uint64_t>(K) / 2;
+  CUtensorMap ta;
+  int s = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, kbytes, M, kbytes, kBKBytes, kBM);
+  if (s != ROUGE_B200_OK) return s;
+  auto make_b = [&](int box_rows, CUtensorMap *tb) {
+    return make_tmap_2d(tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, kbytes, N, kbytes, kBKBytes, box_rows);
+  };
+  if (out_type == ROUGE_B200_OUT_BF16)
+    return launch_tiles<MmaKind::NVF4, 256, false, ROUGE_B200_OUT_BF16, false, true>(ta, make_b, g,
+                                                                                     st);
+  return launch_tiles<MmaKind::NVF4, 256, false, ROUGE_B200_OUT_F32, false, true>(ta, make_b, g, st);
+}
+
 }  // namespace rb200
 
 using namespace rb200;
 
 extern "C" {
+
+int rouge_b200_gemm_nvfp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa,
+                          const float *gs_a, const uint8_t *B, const uint8_t *sfb,
+                          const float *gs_b, void *C, int ldc, int out_type, void *stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !sfa || !sfb || !C || ldc < N ||
+      (out_type != ROUGE_B200_OUT_F32 && out_type != ROUGE_B200_OUT_BF16))
+    return set_status(ROUGE_B200_EINVAL);
+  if (K % 32 || (reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
+      (reinterpret_cast<uintptr_t>(sfa) & 15u) || (reinterpret_cast<uintptr_t>(sfb) & 15u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_gemm_nvf4(M, N, K, A, sfa, gs_a, B, sfb, gs_b, C, ldc, out_type, as_stream(stream));
+}
 
 int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const uint8_t *sfa,
                        const uint8_t *B, int fmt_b, const uint8_t *sfb, void *C, int ldc,

@@ -250,16 +250,31 @@ __global__ void __launch_bounds__(kMxThreads)
 // 32x128b.warpx4 turns into TMEM words: lane r%32, column r/32, byte j).
 // Rows or K-blocks past the matrix get 127 (scale 1: their operand bytes
 // are zero-filled by the GEMM's loads).
-__global__ void mx_scale_atoms_kernel(const uint8_t *__restrict__ src, int rows, int kb32,
-                                      uint8_t *__restrict__ dst, int kb128, size_t atoms) {
+// (generic form: `per_row` scales per row in src, `groups` atoms per 128
+// rows in dst, `pad` for positions past the matrix)
+__global__ void mx_scale_atoms_kernel(const uint8_t *__restrict__ src, int rows, int per_row,
+                                      uint8_t *__restrict__ dst, int groups, size_t atoms,
+                                      uint8_t pad) {
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < atoms * 512;
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t atom = i >> 9;
     const int off = static_cast<int>(i & 511);
-    const int rb = static_cast<int>(atom / kb128), kb = static_cast<int>(atom % kb128);
+    const int rb = static_cast<int>(atom / groups), kb = static_cast<int>(atom % groups);
     const int r = (off >> 4) + 32 * ((off >> 2) & 3), j = off & 3;
     const int row = rb * 128 + r, col = kb * 4 + j;
-    dst[i] = (row < rows && col < kb32) ? src[static_cast<size_t>(row) * kb32 + col] : 127;
+    dst[i] = (row < rows && col < per_row) ? src[static_cast<size_t>(row) * per_row + col] : pad;
+  }
+}
+
+// Two e2m1 codes per byte, the lower-index element in the low nibble
+// (the packed operand layout of the fp4 tensor-core kinds).
+__global__ void fp4_pack_kernel(const uint32_t *__restrict__ codes, size_t nwords,
+                                uint16_t *__restrict__ packed) {
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nwords;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint32_t w = codes[i];
+    packed[i] = static_cast<uint16_t>((w & 0xFu) | ((w >> 4) & 0xF0u) | ((w >> 8) & 0xF00u) |
+                                      ((w >> 12) & 0xF000u));
   }
 }
 
@@ -457,7 +472,35 @@ int rouge_b200_mx_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *a
   if (s != ROUGE_B200_OK) return s;
   const size_t n = rouge_b200_mx_scale_atoms_bytes(rows, K) / 512;
   mx_scale_atoms_kernel<<<grid_for(n * 512, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
-      scales, rows, K / 32, atoms, (K + 127) / 128, n);
+      scales, rows, K / 32, atoms, (K + 127) / 128, n, 127);
+  return cuda_status(cudaGetLastError());
+}
+
+// NVFP4: K / 16 UE4M3 scales per row; four atoms (256 K) per GEMM stage.
+size_t rouge_b200_nvfp4_scale_atoms_bytes(int rows, int K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return static_cast<size_t>((rows + 127) / 128) * ((K + 255) / 256) * 4 * 512;
+}
+
+int rouge_b200_nvfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                                 void *stream) {
+  if (!scales || !atoms || rows <= 0 || K <= 0 || K % 16) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const size_t n = rouge_b200_nvfp4_scale_atoms_bytes(rows, K) / 512;
+  // pad with 0x38 (UE4M3 1.0): the padded K positions of the operands are zero
+  mx_scale_atoms_kernel<<<grid_for(n * 512, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
+      scales, rows, K / 16, atoms, (K + 255) / 256 * 4, n, 0x38);
+  return cuda_status(cudaGetLastError());
+}
+
+int rouge_b200_fp4_pack(const uint8_t *codes, size_t n, uint8_t *packed, void *stream) {
+  if (!codes || !packed || n == 0 || n % 4 || !a4(codes) || (reinterpret_cast<uintptr_t>(packed) & 1u))
+    return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  fp4_pack_kernel<<<grid_for(n / 4, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
+      reinterpret_cast<const uint32_t *>(codes), n / 4, reinterpret_cast<uint16_t *>(packed));
   return cuda_status(cudaGetLastError());
 }
 

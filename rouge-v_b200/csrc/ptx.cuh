@@ -235,7 +235,9 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
 // UMMA kinds.
 // MXF8: kind::mxf8f6f4.block_scale (e4m3 / e5m2 operands, one E8M0 scale
 // per 32 K per row and column, the scales in TMEM).
-enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3, MXF8 = 4 };
+// NVF4: kind::mxf4nvf4.block_scale.scale_vec::4X (packed e2m1 operands,
+// one UE4M3 scale per 16 K per row and column).
+enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3, MXF8 = 4, NVF4 = 5 };
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, one instruction, issued by the
 // calling thread. accumulate == 0 overwrites D.
@@ -507,6 +509,21 @@ __device__ __forceinline__ void umma_mx_pair(uint32_t tmem_d, uint64_t adesc, ui
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;"
+      "\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+// Block-scaled D (+)= (A . sfA)(B . sfB)^T for packed e2m1 operands (K = 64
+// per instruction, 32 bytes of each operand row) with four UE4M3 scales
+// per row per instruction (one per 16 K): the scale word of row r at
+// TMEM lane r % 32, column (tmem_sf + r / 32). CTA pair, leader issues.
+__device__ __forceinline__ void umma_nvf4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t tmem_sfa, uint32_t tmem_sfb,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;"
       "\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
       : "memory");

@@ -99,6 +99,10 @@ _SIGS = {
     "rouge_b200_mx_scale_atoms_bytes": (_SZ, [_I, _I]),
     "rouge_b200_mx_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
     "rouge_b200_gemm_mx": (_I, [_I, _I, _I, _P, _I, _P, _P, _I, _P, _P, _I, _I, _P]),
+    "rouge_b200_nvfp4_scale_atoms_bytes": (_SZ, [_I, _I]),
+    "rouge_b200_nvfp4_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
+    "rouge_b200_fp4_pack": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_gemm_nvfp4": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
     "rouge_quantize_e5m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e5m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e3m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e3m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e2m3": (C.c_uint8, [C.c_float]), "rouge_dequantize_e2m3": (C.c_float, [C.c_uint8]),
@@ -242,6 +246,31 @@ def gemm_mx(A, fmt_a, sfa, B, fmt_b, sfb, C, out_type):
     _check("rouge_b200_gemm_mx", lib().rouge_b200_gemm_mx(
         M, N, K, _dp(A), fmt_a, _dp(sfa), _dp(B), fmt_b, _dp(sfb), _dp(C), C.shape[1], out_type,
         _stream()))
+
+
+def nvfp4_scale_atoms_bytes(rows, K):
+    return lib().rouge_b200_nvfp4_scale_atoms_bytes(rows, K)
+
+
+def nvfp4_scale_atoms(scales, rows, K, atoms):
+    """[rows][K/16] UE4M3 scales -> the tensor-core atom layout of gemm_nvfp4."""
+    _check("rouge_b200_nvfp4_scale_atoms", lib().rouge_b200_nvfp4_scale_atoms(
+        _dp(scales), rows, K, _dp(atoms), _stream()))
+
+
+def fp4_pack(codes, packed):
+    """e2m1 codes (one per byte) -> two per byte, lower index in the low nibble."""
+    _check("rouge_b200_fp4_pack", lib().rouge_b200_fp4_pack(
+        _dp(codes), codes.numel(), _dp(packed), _stream()))
+
+
+def gemm_nvfp4(A, sfa, gs_a, B, sfb, gs_b, C, out_type):
+    """C[M][N] = gs_a gs_b (A x sfa) . (B x sfb)^T, A [M][K/2], B [N][K/2] packed e2m1."""
+    M, K = A.shape[0], 2 * A.shape[1]
+    N = B.shape[0]
+    _check("rouge_b200_gemm_nvfp4", lib().rouge_b200_gemm_nvfp4(
+        M, N, K, _dp(A), _dp(sfa), None if gs_a is None else _dp(gs_a), _dp(B), _dp(sfb),
+        None if gs_b is None else _dp(gs_b), _dp(C), C.shape[1], out_type, _stream()))
 
 
 def convert_f32_to_f16(x, out):

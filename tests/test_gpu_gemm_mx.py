@@ -1,4 +1,5 @@
-"""Block-scaled MXFP8 GEMM (tcgen05 kind::mxf8f6f4.block_scale, CTA pairs)
+"""Block-scaled MXFP8 and NVFP4 GEMMs (tcgen05 kind::mxf8f6f4 / mxf4nvf4
+.block_scale, CTA pairs)
 against the oracle: operands quantized by the MX block quantizer (bit-exact
 with the reference), decoded exactly by the oracle (narrow.cpp:304-331) and
 multiplied in double. The tensor cores multiply exactly and accumulate in
@@ -82,3 +83,56 @@ def test_gemm_mx_bf16_out(rb, orc, cuda):
     want = A @ B.T
     got = C.float().cpu().numpy()
     assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 4e-3
+
+
+def _nvfp4(rb, torch, x, gs, cuda):
+    rows, K = x.shape
+    q = torch.empty((rows, K), dtype=torch.uint8, device=cuda)
+    s = torch.empty((rows, K // 16), dtype=torch.uint8, device=cuda)
+    rb.nvfp4_quantize(x, gs, q, s)
+    packed = torch.empty((rows, K // 2), dtype=torch.uint8, device=cuda)
+    rb.fp4_pack(q, packed)
+    atoms = torch.empty(rb.nvfp4_scale_atoms_bytes(rows, K), dtype=torch.uint8, device=cuda)
+    rb.nvfp4_scale_atoms(s, rows, K, atoms)
+    return q, s, packed, atoms
+
+
+def _nvfp4_decode(orc, q, s, gs, rows, K):
+    """x = e2m1(q) * e4m3(scale) * gs (narrow.cpp:270-300: codes of x / (scale gs))."""
+    v = orc.narrow_decode(q.cpu().numpy().ravel(), "e2m1").astype(np.float64)
+    sc = orc.narrow_decode(s.cpu().numpy().ravel(), "e4m3").astype(np.float64)
+    return (v.reshape(rows, K // 16, 16) * sc.reshape(rows, K // 16, 1)).reshape(rows, K) * gs
+
+
+def test_fp4_pack(rb, cuda):
+    import torch
+    c = torch.randint(0, 16, (4096,), dtype=torch.uint8, device=cuda)
+    p = torch.empty(2048, dtype=torch.uint8, device=cuda)
+    rb.fp4_pack(c, p)
+    ch = c.cpu().numpy()
+    assert (p.cpu().numpy() == (ch[0::2] | (ch[1::2] << 4))).all()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (512, 256, 1024), (300, 200, 96),
+                                   (1000, 384, 544), (2048, 2048, 4096), (4096, 4096, 512)])
+@pytest.mark.parametrize("gsa,gsb", [(1.0, 1.0), (0.37, 4.0)])
+def test_gemm_nvfp4_against_oracle(rb, orc, cuda, M, N, K, gsa, gsb):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(M + 3 * N + K)
+    xa = torch.randn((M, K), device=cuda, generator=g) * torch.exp2(
+        torch.randint(-6, 7, (M, K // 16), device=cuda, generator=g).float()).repeat_interleave(16, 1)
+    xb = torch.randn((N, K), device=cuda, generator=g)
+    qa, sa, pa, ta = _nvfp4(rb, torch, xa, gsa, cuda)
+    qb, sb, pb, tb = _nvfp4(rb, torch, xb, gsb, cuda)
+    ga = torch.tensor([gsa], device=cuda)
+    gb = torch.tensor([gsb], device=cuda)
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    rb.gemm_nvfp4(pa, ta, ga, pb, tb, gb, C, rb.OUT_F32)
+    rb.sync_status()
+    rows = np.unique(np.linspace(0, M - 1, min(M, 64)).astype(int))
+    A = _nvfp4_decode(orc, qa[rows.tolist()], sa[rows.tolist()], gsa, rows.size, K)
+    B = _nvfp4_decode(orc, qb, sb, gsb, N, K)
+    want = A @ B.T
+    got = C.cpu().numpy()[rows].astype(np.float64)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err
