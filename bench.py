@@ -649,7 +649,52 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
                    "256x256 CTA-pair tiles, overlapping TMEM accumulators)",
         "peak": f"gemm vs 2 x {peak_src} bf16; quantize vs {peak_src} HBM "
                 "(5 B/element + 1/32 B scale)"}
-    del xa, xb, qa, qb, sa, sb, ta, tb, cm
+    del qa, qb, sa, sb, ta, tb
+
+    # NVFP4: block quantization (e2m1 + UE4M3 scale per 16, global scale 1),
+    # packing two codes per byte, and the block-scaled fp4 GEMM 8192^3
+    qa = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    qb = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    sa = torch.empty((nm, nm // 16), dtype=torch.uint8, device=dev)
+    sb = torch.empty((nm, nm // 16), dtype=torch.uint8, device=dev)
+    t_q = time_launch(torch, lambda: rb.nvfp4_quantize(xa, 1.0, qa, sa), flush)
+    rb.nvfp4_quantize(xb, 1.0, qb, sb)
+    pa = torch.empty((nm, nm // 2), dtype=torch.uint8, device=dev)
+    pb = torch.empty((nm, nm // 2), dtype=torch.uint8, device=dev)
+    rb.fp4_pack(qa, pa)
+    rb.fp4_pack(qb, pb)
+    ta = torch.empty(rb.nvfp4_scale_atoms_bytes(nm, nm), dtype=torch.uint8, device=dev)
+    tb = torch.empty_like(ta)
+    rb.nvfp4_scale_atoms(sa, nm, nm, ta)
+    rb.nvfp4_scale_atoms(sb, nm, nm, tb)
+    g1 = torch.ones(1, device=dev)
+    t_g = time_launch(torch, lambda: rb.gemm_nvfp4(pa, ta, g1, pb, tb, g1, cm, rb.OUT_BF16), flush)
+    rb.sync_status()
+    wq, ws = orc.nvfp4_quantize(xs, 1.0)
+    codes_ok = bool((qa[rows].cpu().numpy().ravel() == wq).all()
+                    and (sa[rows].cpu().numpy().ravel() == ws).all())
+
+    def dec(q, s_, r):
+        v = orc.narrow_decode(q.ravel(), "e2m1").astype(np.float64).reshape(r, nm // 16, 16)
+        return (v * orc.narrow_decode(s_.ravel(), "e4m3").astype(np.float64).reshape(r, -1, 1)).reshape(r, nm)
+    A = dec(qa[rows].cpu().numpy(), sa[rows].cpu().numpy(), 4)
+    B = dec(qb.cpu().numpy(), sb.cpu().numpy(), nm)
+    want = A @ B.T
+    got = cm[rows].float().cpu().numpy()
+    err = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    qbytes = nm * nm * (4 + 1) + nm * nm // 16
+    tc4 = 4.0 * peaks["bf16_tflops"]
+    out["nvfp4_8192"] = {
+        "quantize_ms": round(t_q, 4), "quantize_gbs": round(qbytes / (t_q * 1e-3) / 1e9, 1),
+        "quantize_hbm_frac": round(qbytes / (t_q * 1e-3) / 1e9 / hbm, 4),
+        "gemm_ms": round(t_g, 4), "gemm_tflops": round(fl / (t_g * 1e-3) / 1e12, 1),
+        "gemm_frac": round(fl / (t_g * 1e-3) / 1e12 / tc4, 4),
+        "codes_and_scales_bit_exact_sampled_rows": codes_ok, "rel_l2_sampled_rows": err,
+        "kernels": "nvfp4_quant_kernel; gemm_tc2_kernel<NVF4> (kind::mxf4nvf4.block_scale."
+                   "scale_vec::4X, 256x256 CTA-pair tiles, packed e2m1)",
+        "peak": f"gemm vs 4 x {peak_src} bf16 (dense fp4 is four times bf16); quantize vs "
+                f"{peak_src} HBM (5 B/element + 1/16 B scale)"}
+    del xa, xb, qa, qb, sa, sb, pa, pb, ta, tb, cm
 
     # cuDNN-API library: cudnnConvolutionForward at the config-4 shape
     # (N=32, 56x56, 256 -> 256, 3x3 s1 p1), HALF + NHWC (direct: no
