@@ -418,9 +418,26 @@ size_t rouge_b200_nvfp4_scale_atoms_bytes(int rows, int K);
 int rouge_b200_nvfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
                                  void *stream);
 int rouge_b200_fp4_pack(const uint8_t *codes, size_t n, uint8_t *packed, void *stream);
+/* rouge_b200_nvfp4_quantize with the codes written packed (n % 16 == 0,
+ * 16-byte aligned x, 8-byte aligned packed[n/2]): the GEMM's operand in one
+ * pass. */
+int rouge_b200_nvfp4_quantize_packed(const float *x, size_t n, float global_scale,
+                                     uint8_t *packed, uint8_t *scales, void *stream);
 int rouge_b200_gemm_nvfp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa,
                           const float *gs_a, const uint8_t *B, const uint8_t *sfb,
                           const float *gs_b, void *C, int ldc, int out_type, void *stream);
+
+/* Block-scaled MXFP4 GEMM (kind::mxf4.block_scale.scale_vec::2X): the e2m1
+ * codes of the MXFP4 quantizer (rouge_b200_mx_quantize, ROUGE_B200_FMT_E2M1)
+ * packed by rouge_b200_fp4_pack, their E8M0 scales (one per 32 K,
+ * [rows][K/32]) laid out by rouge_b200_mxfp4_scale_atoms; otherwise as
+ * rouge_b200_gemm_nvfp4 without global scales. */
+size_t rouge_b200_mxfp4_scale_atoms_bytes(int rows, int K);
+int rouge_b200_mxfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                                 void *stream);
+int rouge_b200_gemm_mxfp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa,
+                          const uint8_t *B, const uint8_t *sfb, void *C, int ldc, int out_type,
+                          void *stream);
 
 /* Convolution forward with cuDNN's semantics (the operation the reference
  * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU

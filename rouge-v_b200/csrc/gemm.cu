@@ -729,9 +729,11 @@ struct Cfg2 {
   // block-scaled kinds: one 512-byte scale atom (128 rows x 4 scales) per
   // 128 rows per ATOMS_K: MXF8 one per stage (4 K-blocks of 32 = the
   // stage's 128 K), NVF4 four (one per MMA: 4 blocks of 16 = 64 K)
+  // (MXF4: two per 128 rows, 8 blocks of 32 = the stage's 256 K)
   static constexpr bool NV = KIND == MmaKind::NVF4;
-  static constexpr bool MX = KIND == MmaKind::MXF8 || NV;
-  static constexpr int ATOMS_K = NV ? 4 : 1;
+  static constexpr bool F4 = KIND == MmaKind::MXF4;
+  static constexpr bool MX = KIND == MmaKind::MXF8 || NV || F4;
+  static constexpr int ATOMS_K = NV ? 4 : (F4 ? 2 : 1);
   static constexpr int SFA_BYTES = MX ? ATOMS_K * 512 : 0;
   static constexpr int SFB_BYTES = MX ? (BN / 128) * ATOMS_K * 512 : 0;
   // per-stage scale region, padded so that stages stay 1024-byte multiples
@@ -743,9 +745,9 @@ struct Cfg2 {
   // disjoint buffers and the scales: its buffers overlap in 32 columns
   // (buffer 0's last chunk is buffer 1's first), which each tile's
   // epilogue drains first and reports on its own barrier.
-  static constexpr int SF_SET = ATOMS_K * (4 + BN / 32);  // MXF8 12, NVF4 48 columns (BN 256)
+  static constexpr int SF_SET = ATOMS_K * (4 + BN / 32);  // MXF8 12, MXF4 24, NVF4 48 (BN 256)
   static constexpr int SF_COL = MX && BN == 256 ? (NV ? 448 : 480) : 2 * BN;
-  static constexpr int SF_BUFS = MX && BN == 256 ? (NV ? 1 : 2) : (NV ? 1 : 4);
+  static constexpr int SF_BUFS = MX && BN == 256 ? (NV || F4 ? 1 : 2) : (NV ? 1 : 4);
   static constexpr int ACC1_COL = MX && BN == 256 ? SF_COL - BN : BN;
   static constexpr int OVL_CHUNKS = (BN - ACC1_COL) / 32;  // chunks both buffers share
   static constexpr bool OVERLAP = OVL_CHUNKS > 0;
@@ -919,7 +921,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr uint32_t ab_fmt = KIND == MmaKind::I8 ? 1u : (KIND == MmaKind::TF32 ? 2u : 0u);
     const uint32_t ab = (KIND == MmaKind::F16 && args.bf16) ? 1u : ab_fmt;
     // block-scaled: E8M0 scales (format 1) for MXF8, UE4M3 (0) for NVF4
-    constexpr uint32_t sf_fmt = C::NV ? 0u : 1u;
+    constexpr uint32_t sf_fmt = C::NV ? 0u : 1u;  // (MXF4: E8M0)
     const uint32_t idesc_full =
         C::MX ? make_idesc_mx(static_cast<uint32_t>(args.mx_fmt_a), static_cast<uint32_t>(args.mx_fmt_b),
                               2 * kBM, BN, sf_fmt, 0u, 0u)
@@ -999,10 +1001,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const uint64_t adesc = smem_desc_sw128(a0 + k * 32, 16, 1024);
             const uint64_t bdesc = smem_desc_sw128(b0 + k * 32, 16, 1024);
             const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
-            if constexpr (C::NV)
+            if constexpr (C::NV) {
               umma_nvf4_pair(d_tmem, adesc, bdesc, idesc, t_sf + 4u * kk,
                              t_sf + kSfbCol + kk * (BN / 32) + sfb_unit, acc);
-            else
+            } else if constexpr (C::F4) {  // atom k / 2, byte pair 2 (k % 2)
+              const uint32_t id = (kk & 1u) * 2u;
+              umma_mxf4_pair(d_tmem, adesc, bdesc, idesc | (id << 29) | (id << 4),
+                             (t_sf + 4u * (kk >> 1)) | (id << 30),
+                             (t_sf + kSfbCol + (kk >> 1) * (BN / 32) + sfb_unit) | (id << 30), acc);
+            } else
               umma_mx_pair(d_tmem, adesc, bdesc, idesc | (kk << 29) | (kk << 4), t_sf | (kk << 30),
                            (t_sf + kSfbCol + sfb_unit) | (kk << 30), acc);
           }
@@ -1113,10 +1120,10 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
     if (s != ROUGE_B200_OK) return s;
     tc.n = 1;
   }
-  if constexpr (KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4) {
+  if constexpr (KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4 || KIND == MmaKind::MXF4) {
     // scale atoms as 128-byte rows, 4 rows per atom, one stage's atoms
-    // (1 for MXF8, 4 for NVF4) per box, no swizzle
-    const uint32_t box = KIND == MmaKind::NVF4 ? 16u : 4u;
+    // (1 for MXF8, 2 for MXF4, 4 for NVF4) per box, no swizzle
+    const uint32_t box = KIND == MmaKind::NVF4 ? 16u : (KIND == MmaKind::MXF4 ? 8u : 4u);
     const uint64_t rows_a = static_cast<uint64_t>((args.M + 127) / 128) * args.sf_kblocks * box;
     const uint64_t rows_b = static_cast<uint64_t>((args.N + 127) / 128) * args.sf_kblocks * box;
     s = make_tmap_2d(&tc.sfa, args.scales_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 128, rows_a, 128, 128,
@@ -1197,7 +1204,8 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
 #define RB200_MAX_SPLIT 2
 #endif
     // (block-scaled: only halves, whose B rows are one whole scale atom)
-    const int max_split = KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4 ? 2 : RB200_MAX_SPLIT;
+    const int max_split =
+        KIND == MmaKind::MXF8 || KIND == MmaKind::NVF4 || KIND == MmaKind::MXF4 ? 2 : RB200_MAX_SPLIT;
     if (!B_MN && rem) {
       for (int f = max_split; f >= 2; f /= 2) {
         if (rem * f <= clusters) {
@@ -1578,9 +1586,10 @@ int launch_gemm_mx(int M, int N, int K, const uint8_t *A, long long lda, int fmt
 // e2m1 (two per byte, the lower-index element in the low nibble; row
 // pitches K / 2 bytes), UE4M3 block scales per 16 K in the tcgen05 atom
 // layout (rouge_b200_nvfp4_scale_atoms), gs_a / gs_b device floats or null.
-int launch_gemm_nvf4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa, const float *gs_a,
-                     const uint8_t *B, const uint8_t *sfb, const float *gs_b, void *Cp,
-                     long long ldc, int out_type, cudaStream_t st) {
+template <MmaKind KIND>
+int launch_gemm_fp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa, const float *gs_a,
+                    const uint8_t *B, const uint8_t *sfb, const float *gs_b, void *Cp,
+                    long long ldc, int out_type, cudaStream_t st) {
   GemmArgs g{};
   g.M = M; g.N = N; g.K = K;
   g.C = Cp; g.ldc = ldc;
@@ -1588,7 +1597,7 @@ int launch_gemm_nvf4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa, 
   g.scales_b = reinterpret_cast<const float *>(sfb);
   g.scale_a = gs_a && gs_b ? gs_a : nullptr;
   g.scale_b = gs_a && gs_b ? gs_b : nullptr;
-  g.mx_fmt_a = 1;  // E2M1 of kind::mxf4nvf4
+  g.mx_fmt_a = 1;  // E2M1 of kind::mxf4nvf4 / kind::mxf4
   g.mx_fmt_b = 1;
   g.sf_kblocks = (K + 255) / 256;
   g.use_tma_store = vec_ok(Cp, ldc, out_type);
@@ -1605,9 +1614,8 @@ int launch_gemm_nvf4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa, 
     return make_tmap_2d(tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, kbytes, N, kbytes, kBKBytes, box_rows);
   };
   if (out_type == ROUGE_B200_OUT_BF16)
-    return launch_tiles<MmaKind::NVF4, 256, false, ROUGE_B200_OUT_BF16, false, true>(ta, make_b, g,
-                                                                                     st);
-  return launch_tiles<MmaKind::NVF4, 256, false, ROUGE_B200_OUT_F32, false, true>(ta, make_b, g, st);
+    return launch_tiles<KIND, 256, false, ROUGE_B200_OUT_BF16, false, true>(ta, make_b, g, st);
+  return launch_tiles<KIND, 256, false, ROUGE_B200_OUT_F32, false, true>(ta, make_b, g, st);
 }
 
 }  // namespace rb200
@@ -1627,7 +1635,23 @@ int rouge_b200_gemm_nvfp4(int M, int N, int K, const uint8_t *A, const uint8_t *
     return set_status(ROUGE_B200_EUNSUPPORTED);
   const int s = device_ready();
   if (s != ROUGE_B200_OK) return s;
-  return launch_gemm_nvf4(M, N, K, A, sfa, gs_a, B, sfb, gs_b, C, ldc, out_type, as_stream(stream));
+  return launch_gemm_fp4<MmaKind::NVF4>(M, N, K, A, sfa, gs_a, B, sfb, gs_b, C, ldc, out_type,
+                                       as_stream(stream));
+}
+
+int rouge_b200_gemm_mxfp4(int M, int N, int K, const uint8_t *A, const uint8_t *sfa,
+                          const uint8_t *B, const uint8_t *sfb, void *C, int ldc, int out_type,
+                          void *stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !sfa || !sfb || !C || ldc < N ||
+      (out_type != ROUGE_B200_OUT_F32 && out_type != ROUGE_B200_OUT_BF16))
+    return set_status(ROUGE_B200_EINVAL);
+  if (K % 32 || (reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(B) & 15u) ||
+      (reinterpret_cast<uintptr_t>(sfa) & 15u) || (reinterpret_cast<uintptr_t>(sfb) & 15u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_gemm_fp4<MmaKind::MXF4>(M, N, K, A, sfa, nullptr, B, sfb, nullptr, C, ldc, out_type,
+                                        as_stream(stream));
 }
 
 int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const uint8_t *sfa,

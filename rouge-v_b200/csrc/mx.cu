@@ -219,6 +219,85 @@ __global__ void __launch_bounds__(kMxThreads)
   }
 }
 
+// Four e2m1 codes (RNE, satfinite) from the hardware conversion, one per
+// nibble, x0 in the low nibble.
+__device__ __forceinline__ uint32_t cvt4_e2m1(float x0, float x1, float x2, float x3) {
+  uint16_t r;
+  asm("{\n\t.reg .b8 t0, t1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t1, %4, %3;\n\t"
+      "mov.b16 %0, {t0, t1};\n\t}"
+      : "=h"(r)
+      : "f"(x0), "f"(x1), "f"(x2), "f"(x3));
+  return r;
+}
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// e2m1 input fix: the reference encodes magnitudes in (0, 0.25) as +0, the
+// hardware as a signed zero; zeroing the negative ones first makes them
+// agree (-0.25 and -0 keep their sign in both).
+__device__ __forceinline__ float e2m1_pre(float y) { return (y > -0.25f && y < 0.0f) ? 0.0f : y; }
+
+// NVFP4 fast kernel (16-byte aligned x, whole blocks): one lane per
+// 16-element block (four float4), no shuffles. The block maximum uses a
+// NaN-propagating max: a block holding a NaN takes the exact per-element
+// encoder instead. max(|x| * gs) == max|x| * gs (rounding is monotonic).
+// PACKED: codes leave two per byte (8 bytes per block) for the fp4 GEMM,
+// otherwise one per byte (the reference's layout, 16 bytes per block).
+template <bool PACKED>
+__global__ void __launch_bounds__(kMxThreads)
+    nvfp4_quant_blocks_kernel(const float4 *__restrict__ x, uint32_t nblk, float gs,
+                              uint8_t *__restrict__ codes, uint8_t *__restrict__ scales) {
+  for (uint32_t blk = blockIdx.x * blockDim.x + threadIdx.x; blk < nblk;
+       blk += gridDim.x * blockDim.x) {
+    float4 v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __ldg(x + blk * 4u + j);
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      m = max_nan(m, max_nan(max_nan(fabsf(v[j].x), fabsf(v[j].y)),
+                             max_nan(fabsf(v[j].z), fabsf(v[j].w))));
+    const bool has_nan = m != m;
+    if (has_nan) {  // the reference's maximum skips NaN
+      m = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) m = fmaxf(m, amax4(v[j]));
+    }
+    const float amax = __fmul_rn(m, gs);
+    const int p = amax > 448.0f ? block_pow(amax, 448.0f) : 0;
+    const uint32_t sc = p <= 8 ? static_cast<uint32_t>(p + 7) << 3 : 0x7Eu;  // e4m3 of 2^p
+    const float inv = __fdiv_rn(1.0f, __fmul_rn(narrow_decode(sc, kE4M3), gs));
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float y0 = __fmul_rn(v[j].x, inv), y1 = __fmul_rn(v[j].y, inv);
+      const float y2 = __fmul_rn(v[j].z, inv), y3 = __fmul_rn(v[j].w, inv);
+      if (has_nan)
+        w[j] = encode_e2m1(y0) | (encode_e2m1(y1) << 4) | (encode_e2m1(y2) << 8) |
+               (encode_e2m1(y3) << 12);
+      else
+        w[j] = cvt4_e2m1(e2m1_pre(y0), e2m1_pre(y1), e2m1_pre(y2), e2m1_pre(y3));
+    }
+    scales[blk] = static_cast<uint8_t>(sc);
+    if constexpr (PACKED) {
+      reinterpret_cast<uint2 *>(codes)[blk] = make_uint2(w[0] | (w[1] << 16), w[2] | (w[3] << 16));
+    } else {
+      uint32_t b[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        b[j] = (w[j] & 0xFu) | ((w[j] & 0xF0u) << 4) | ((w[j] & 0xF00u) << 8) |
+               ((w[j] & 0xF000u) << 12);
+      reinterpret_cast<uint4 *>(codes)[blk] = make_uint4(b[0], b[1], b[2], b[3]);
+    }
+  }
+}
+
 // narrow.cpp:304-331: out = decode(code) * 2^(scale - 127), the product with
 // x86's NaN rules (a NaN code keeps its sign and payload).
 template <int ID>
@@ -325,6 +404,22 @@ int launch_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_
 
 int launch_nvfp4_quantize(const float *x, size_t n, float gs, uint8_t *codes, uint8_t *scales,
                           cudaStream_t st) {
+  // whole blocks of aligned operands by the fast kernel, a partial last
+  // block by the general one
+  const size_t full = n / 16;
+  if (a16(x) && a16(codes) && full > 0 && full < (1u << 28)) {
+    const size_t want = (full + kMxThreads - 1) / kMxThreads;
+    const size_t cap = static_cast<size_t>(current_sm_count()) * 8;
+    nvfp4_quant_blocks_kernel<false><<<static_cast<unsigned>(want < cap ? want : cap), kMxThreads,
+                                       0, st>>>(reinterpret_cast<const float4 *>(x),
+                                                static_cast<uint32_t>(full), gs, codes, scales);
+    const int s = cuda_status(cudaGetLastError());
+    if (s != ROUGE_B200_OK || full * 16 == n) return s;
+    x += full * 16;
+    codes += full * 16;
+    scales += full;
+    n -= full * 16;
+  }
   const unsigned grid = grid_for((n + 15) / 16, kMxThreads / 4);
   nvfp4_quant_kernel<<<grid, kMxThreads, 0, st>>>(x, n, gs, codes, scales, a16(x), a4(codes));
   return cuda_status(cudaGetLastError());
@@ -494,6 +589,24 @@ int rouge_b200_nvfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t
   return cuda_status(cudaGetLastError());
 }
 
+// MXFP4 operands of the fp4 GEMM: K / 32 E8M0 scales per row, two atoms
+// per 256 K.
+size_t rouge_b200_mxfp4_scale_atoms_bytes(int rows, int K) {
+  if (rows <= 0 || K <= 0) return 0;
+  return static_cast<size_t>((rows + 127) / 128) * ((K + 255) / 256) * 2 * 512;
+}
+
+int rouge_b200_mxfp4_scale_atoms(const uint8_t *scales, int rows, int K, uint8_t *atoms,
+                                 void *stream) {
+  if (!scales || !atoms || rows <= 0 || K <= 0 || K % 32) return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  const size_t n = rouge_b200_mxfp4_scale_atoms_bytes(rows, K) / 512;
+  mx_scale_atoms_kernel<<<grid_for(n * 512, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
+      scales, rows, K / 32, atoms, (K + 255) / 256 * 2, n, 127);
+  return cuda_status(cudaGetLastError());
+}
+
 int rouge_b200_fp4_pack(const uint8_t *codes, size_t n, uint8_t *packed, void *stream) {
   if (!codes || !packed || n == 0 || n % 4 || !a4(codes) || (reinterpret_cast<uintptr_t>(packed) & 1u))
     return set_status(ROUGE_B200_EINVAL);
@@ -501,6 +614,24 @@ int rouge_b200_fp4_pack(const uint8_t *codes, size_t n, uint8_t *packed, void *s
   if (s != ROUGE_B200_OK) return s;
   fp4_pack_kernel<<<grid_for(n / 4, kMxThreads), kMxThreads, 0, as_stream(stream)>>>(
       reinterpret_cast<const uint32_t *>(codes), n / 4, reinterpret_cast<uint16_t *>(packed));
+  return cuda_status(cudaGetLastError());
+}
+
+int rouge_b200_nvfp4_quantize_packed(const float *x, size_t n, float global_scale,
+                                     uint8_t *packed, uint8_t *scales, void *stream) {
+  if (!x || !packed || !scales || n == 0 || n % 16 || (n / 16) >= (1u << 28) ||
+      (reinterpret_cast<uintptr_t>(x) & 15u) || (reinterpret_cast<uintptr_t>(packed) & 7u))
+    return set_status(ROUGE_B200_EINVAL);
+  const int s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  if (!(global_scale > 0.0f)) global_scale = 1.0f;
+  const size_t full = n / 16;
+  const size_t want = (full + kMxThreads - 1) / kMxThreads;
+  const size_t cap = static_cast<size_t>(current_sm_count()) * 8;
+  nvfp4_quant_blocks_kernel<true><<<static_cast<unsigned>(want < cap ? want : cap), kMxThreads, 0,
+                                    as_stream(stream)>>>(reinterpret_cast<const float4 *>(x),
+                                                         static_cast<uint32_t>(full), global_scale,
+                                                         packed, scales);
   return cuda_status(cudaGetLastError());
 }
 

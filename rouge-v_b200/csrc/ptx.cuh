@@ -237,7 +237,9 @@ __device__ __forceinline__ void tc_commit(uint64_t *bar) {
 // per 32 K per row and column, the scales in TMEM).
 // NVF4: kind::mxf4nvf4.block_scale.scale_vec::4X (packed e2m1 operands,
 // one UE4M3 scale per 16 K per row and column).
-enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3, MXF8 = 4, NVF4 = 5 };
+// MXF4: kind::mxf4.block_scale.scale_vec::2X (packed e2m1, one E8M0 scale
+// per 32 K).
+enum class MmaKind : int { I8 = 0, F8F6F4 = 1, F16 = 2, TF32 = 3, MXF8 = 4, NVF4 = 5, MXF4 = 6 };
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T, one instruction, issued by the
 // calling thread. accumulate == 0 overwrites D.
@@ -524,6 +526,20 @@ __device__ __forceinline__ void umma_nvf4_pair(uint32_t tmem_d, uint64_t adesc, 
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X [%0], %1, %2, %3, [%5], [%6], p;"
+      "\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
+      : "memory");
+}
+
+// The same for MXFP4: two E8M0 scales per row per instruction (one per 32
+// K), the byte pair of each scale word selected by the scale-factor ids
+// (0 or 2) in idesc and bits 31:30 of the scale addresses.
+__device__ __forceinline__ void umma_mxf4_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t tmem_sfa, uint32_t tmem_sfb,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;"
       "\n\t}\n" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tmem_sfa), "r"(tmem_sfb)
       : "memory");

@@ -102,7 +102,11 @@ _SIGS = {
     "rouge_b200_nvfp4_scale_atoms_bytes": (_SZ, [_I, _I]),
     "rouge_b200_nvfp4_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
     "rouge_b200_fp4_pack": (_I, [_P, _SZ, _P, _P]),
+    "rouge_b200_nvfp4_quantize_packed": (_I, [_P, _SZ, C.c_float, _P, _P, _P]),
     "rouge_b200_gemm_nvfp4": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "rouge_b200_mxfp4_scale_atoms_bytes": (_SZ, [_I, _I]),
+    "rouge_b200_mxfp4_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
+    "rouge_b200_gemm_mxfp4": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
     "rouge_quantize_e5m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e5m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e3m2": (C.c_uint8, [C.c_float]), "rouge_dequantize_e3m2": (C.c_float, [C.c_uint8]),
     "rouge_quantize_e2m3": (C.c_uint8, [C.c_float]), "rouge_dequantize_e2m3": (C.c_float, [C.c_uint8]),
@@ -258,6 +262,11 @@ def nvfp4_scale_atoms(scales, rows, K, atoms):
         _dp(scales), rows, K, _dp(atoms), _stream()))
 
 
+def nvfp4_quantize_packed(x, global_scale, packed, scales):
+    _check("rouge_b200_nvfp4_quantize_packed", lib().rouge_b200_nvfp4_quantize_packed(
+        _dp(x), x.numel(), global_scale, _dp(packed), _dp(scales), _stream()))
+
+
 def fp4_pack(codes, packed):
     """e2m1 codes (one per byte) -> two per byte, lower index in the low nibble."""
     _check("rouge_b200_fp4_pack", lib().rouge_b200_fp4_pack(
@@ -271,6 +280,23 @@ def gemm_nvfp4(A, sfa, gs_a, B, sfb, gs_b, C, out_type):
     _check("rouge_b200_gemm_nvfp4", lib().rouge_b200_gemm_nvfp4(
         M, N, K, _dp(A), _dp(sfa), None if gs_a is None else _dp(gs_a), _dp(B), _dp(sfb),
         None if gs_b is None else _dp(gs_b), _dp(C), C.shape[1], out_type, _stream()))
+
+
+def mxfp4_scale_atoms_bytes(rows, K):
+    return lib().rouge_b200_mxfp4_scale_atoms_bytes(rows, K)
+
+
+def mxfp4_scale_atoms(scales, rows, K, atoms):
+    _check("rouge_b200_mxfp4_scale_atoms", lib().rouge_b200_mxfp4_scale_atoms(
+        _dp(scales), rows, K, _dp(atoms), _stream()))
+
+
+def gemm_mxfp4(A, sfa, B, sfb, C, out_type):
+    """C[M][N] = (A x 2^sfa) . (B x 2^sfb)^T, A [M][K/2], B [N][K/2] packed e2m1."""
+    M, K = A.shape[0], 2 * A.shape[1]
+    N = B.shape[0]
+    _check("rouge_b200_gemm_mxfp4", lib().rouge_b200_gemm_mxfp4(
+        M, N, K, _dp(A), _dp(sfa), _dp(B), _dp(sfb), _dp(C), C.shape[1], out_type, _stream()))
 
 
 def convert_f32_to_f16(x, out):

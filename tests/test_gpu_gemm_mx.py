@@ -136,3 +136,35 @@ def test_gemm_nvfp4_against_oracle(rb, orc, cuda, M, N, K, gsa, gsb):
     got = C.cpu().numpy()[rows].astype(np.float64)
     err = np.linalg.norm(got - want) / np.linalg.norm(want)
     assert err <= 1e-5, err
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 256), (512, 256, 1024), (300, 200, 96),
+                                   (1000, 384, 544), (4096, 4096, 512)])
+def test_gemm_mxfp4_against_oracle(rb, orc, cuda, M, N, K):
+    import torch
+    g = torch.Generator(device=cuda).manual_seed(M + 5 * N + K)
+    xa = torch.randn((M, K), device=cuda, generator=g) * torch.exp2(
+        torch.randint(-6, 7, (M, K // 32), device=cuda, generator=g).float()).repeat_interleave(32, 1)
+    xb = torch.randn((N, K), device=cuda, generator=g)
+    out = []
+    for x, rows in ((xa, M), (xb, N)):
+        q = torch.empty((rows, K), dtype=torch.uint8, device=cuda)
+        s = torch.empty((rows, K // 32), dtype=torch.uint8, device=cuda)
+        rb.mx_quantize(x, rb.FMT_E2M1, q, s)
+        p = torch.empty((rows, K // 2), dtype=torch.uint8, device=cuda)
+        rb.fp4_pack(q, p)
+        t = torch.empty(rb.mxfp4_scale_atoms_bytes(rows, K), dtype=torch.uint8, device=cuda)
+        rb.mxfp4_scale_atoms(s, rows, K, t)
+        out.append((q, s, p, t))
+    (qa, sa, pa, ta), (qb, sb, pb, tb) = out
+    C = torch.full((M, N), float("nan"), dtype=torch.float32, device=cuda)
+    rb.gemm_mxfp4(pa, ta, pb, tb, C, rb.OUT_F32)
+    rb.sync_status()
+    rows = np.unique(np.linspace(0, M - 1, min(M, 64)).astype(int))
+    A = orc.mx_dequantize(qa[rows.tolist()].cpu().numpy(), sa[rows.tolist()].cpu().numpy(),
+                          "e2m1").reshape(rows.size, K).astype(np.float64)
+    B = orc.mx_dequantize(qb.cpu().numpy(), sb.cpu().numpy(), "e2m1").reshape(N, K).astype(np.float64)
+    want = A @ B.T
+    got = C.cpu().numpy()[rows].astype(np.float64)
+    err = np.linalg.norm(got - want) / np.linalg.norm(want)
+    assert err <= 1e-5, err

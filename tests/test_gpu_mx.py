@@ -129,3 +129,17 @@ def test_host_drop_ins_match_reference(rb, ref, cuda):
     assert L.rouge_mx_quantize_f32(P(x), 0, 1, P(q), P(s)) == 0
     assert L.rouge_nvfp4_quantize_f32(None, 64, 1.0, P(q), P(s)) == 0
     assert (q == 7).all() and (s == 7).all()
+
+
+@pytest.mark.parametrize("gs", [1.0, 0.37, -2.0])
+def test_nvfp4_packed_equals_codes_packed(rb, orc, cuda, gs):
+    import torch
+    n = 1 << 20
+    x = _data(np.random.default_rng(5), n)
+    xd = torch.from_numpy(x).to(cuda)
+    p = torch.empty(n // 2, dtype=torch.uint8, device=cuda)
+    s = torch.empty(n // 16, dtype=torch.uint8, device=cuda)
+    rb.nvfp4_quantize_packed(xd, gs, p, s)
+    wq, ws = orc.nvfp4_quantize(x, gs)
+    _eq(s.cpu().numpy(), ws)
+    _eq(p.cpu().numpy(), (wq[0::2] | (wq[1::2] << 4)).astype(np.uint8))
