@@ -439,6 +439,52 @@ int rouge_b200_gemm_mxfp4(int M, int N, int K, const uint8_t *A, const uint8_t *
                           const uint8_t *B, const uint8_t *sfb, void *C, int ldc, int out_type,
                           void *stream);
 
+/* ------------------------------------------------------------------------ */
+/* Attention and the transformer block (the GEMM's in-library consumers)     */
+/* ------------------------------------------------------------------------ */
+/* Replace numerics.h:125-137,173-183 (attention.cpp:27-88,
+ * attention_gqa.cpp:52-269, transformer.cpp:33-161), host pointers,
+ * synchronous, same layouts: Q [Hq][S][Dh], K / V [Hkv][Skv][Dh] (f32 or
+ * e4m3 codes with per-head scales), O [Hq][S][Dh]; scale <= 0 means
+ * 1/sqrt(Dh); causal masks t > s + kv_off, window > 0 masks
+ * t < s + kv_off - window + 1; fully masked rows give 0. Scores and the
+ * weighted sums run on the tf32 tensor cores with split operands
+ * (f32-accurate); softmax per row on the device. */
+void rouge_attention_f32(int S, int Skv, int D, const float *Q, const float *K, const float *V,
+                         float *O, float scale, int causal, int kv_off);
+void rouge_attention_gqa(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q, const float *K,
+                         const float *V, float *O, float scale, int causal, int window,
+                         int kv_off);
+void rouge_attention_gqa_fp8kv(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q,
+                               const uint8_t *Kq, const uint8_t *Vq, const float *scales_k,
+                               const float *scales_v, float *O, float scale, int causal,
+                               int window, int kv_off);
+void rouge_rmsnorm(const float *x, int n, const float *w, float eps, float *out);
+void rouge_rope(float *x, int heads, int head_dim, int pos, float theta);
+void rouge_swiglu(const float *gate, const float *up, int n, float *out);
+void rouge_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, const float *x,
+                             const float *wrms1, const float *wq, const float *wk, const float *wv,
+                             const float *wo, const float *wrms2, const float *wgate,
+                             const float *wup, const float *wdown, int Dff, float rope_theta,
+                             float rms_eps, float *out);
+
+/* Device-pointer forms (asynchronous on `stream`; workspace 256-byte
+ * aligned, at least the *_workspace bytes, else ROUGE_B200_ETOOBIG).
+ * Attention: f32 K / V, or (Kq != NULL) e4m3 K / V with device scales. */
+size_t rouge_b200_attention_workspace(int S, int Skv, int Dh, int Hq, int Hkv, int fp8_kv);
+int rouge_b200_attention_gqa(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q,
+                             const float *K, const float *V, const uint8_t *Kq, const uint8_t *Vq,
+                             const float *scales_k, const float *scales_v, float *O, float scale,
+                             int causal, int window, int kv_off, void *workspace,
+                             size_t workspace_bytes, void *stream);
+size_t rouge_b200_transformer_block_workspace(int S, int D, int Hq, int Hkv, int Dq, int Dff);
+int rouge_b200_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, const float *x,
+                                 const float *wrms1, const float *wq, const float *wk,
+                                 const float *wv, const float *wo, const float *wrms2,
+                                 const float *wgate, const float *wup, const float *wdown, int Dff,
+                                 float rope_theta, float rms_eps, float *out, void *workspace,
+                                 size_t workspace_bytes, void *stream);
+
 /* Convolution forward with cuDNN's semantics (the operation the reference
  * runs in cudnnConvolutionForward, cudnn_shim.cpp:188-232, on its CPU
  * conv): Y = alpha * conv(X, Wt) + beta * Y, cross-correlation, symmetric

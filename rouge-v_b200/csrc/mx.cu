@@ -116,7 +116,31 @@ __global__ void __launch_bounds__(kMxThreads, 8)
   }
 }
 
-// MXFP8 fast kernel (e4m3 / e5m2, whole blocks, 16-byte aligned x and
+// Four e2m1 codes (RNE, satfinite) from the hardware conversion, one per
+// nibble, x0 in the low nibble.
+__device__ __forceinline__ uint32_t cvt4_e2m1(float x0, float x1, float x2, float x3) {
+  uint16_t r;
+  asm("{\n\t.reg .b8 t0, t1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t1, %4, %3;\n\t"
+      "mov.b16 %0, {t0, t1};\n\t}"
+      : "=h"(r)
+      : "f"(x0), "f"(x1), "f"(x2), "f"(x3));
+  return r;
+}
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// e2m1 input fix: the reference encodes magnitudes in (0, 0.25) as +0, the
+// hardware as a signed zero; zeroing the negative ones first makes them
+// agree (-0.25 and -0 keep their sign in both).
+__device__ __forceinline__ float e2m1_pre(float y) { return (y > -0.25f && y < 0.0f) ? 0.0f : y; }
+
+// MXFP8 / MXFP4 fast kernel (e4m3 / e5m2 / e2m1, whole blocks, 16-byte aligned x and
 // codes): two lanes per 32-element block, 16 consecutive elements (four
 // float4) per lane, so that the block maximum takes one shuffle and the
 // scale work is shared by 16 elements; the codes leave as one 16-byte
@@ -125,11 +149,14 @@ __global__ void __launch_bounds__(kMxThreads, 8)
 // |x * inv| <= emax / 2 produces) and for 0x80 bytes: those are redone per
 // element (a 0x80 byte stands for -0, -2^-10 in e4m3 or -2^-17 in e5m2,
 // kept by the reference, or a tinier negative value, which it makes +0).
+// (MXFP4: e2m1 codes from the hardware conversion of values whose
+// (-0.25, 0) part is zeroed first; a block holding a NaN, found by a
+// NaN-propagating maximum, takes the exact threshold encoder.)
 template <int ID>
 __global__ void __launch_bounds__(kMxThreads, 4)
     mx_quant_blocks_kernel(const float4 *__restrict__ x, uint32_t nblk, uint4 *__restrict__ codes,
                            uint8_t *__restrict__ scales) {
-  constexpr float kEmax = ID == kE4M3 ? 448.0f : 57344.0f;
+  constexpr float kEmax = ID == kE4M3 ? 448.0f : (ID == kE5M2 ? 57344.0f : 6.0f);
   constexpr float kTiny = ID == kE4M3 ? 0.0009765625f : 7.62939453125e-06f;  // 2^-10, 2^-17
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t stride = (gridDim.x * blockDim.x) >> 1;  // blocks per grid step
@@ -148,6 +175,32 @@ __global__ void __launch_bounds__(kMxThreads, 4)
     const uint32_t sc = mx_scale_code(a > kEmax ? block_pow(a, kEmax) : 0);
     const float inv = e8m0_inverse(sc);
     uint32_t w[4];
+    if constexpr (ID == kE2M1) {
+      float mn = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        mn = max_nan(mn, max_nan(max_nan(fabsf(v[j].x), fabsf(v[j].y)),
+                                 max_nan(fabsf(v[j].z), fabsf(v[j].w))));
+      const bool nan = mn != mn;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float y0 = __fmul_rn(v[j].x, inv), y1 = __fmul_rn(v[j].y, inv);
+        const float y2 = __fmul_rn(v[j].z, inv), y3 = __fmul_rn(v[j].w, inv);
+        uint32_t c;
+        if (nan) {
+          c = encode_e2m1(y0) | (encode_e2m1(y1) << 8) | (encode_e2m1(y2) << 16) |
+              (encode_e2m1(y3) << 24);
+        } else {
+          const uint32_t h = cvt4_e2m1(e2m1_pre(y0), e2m1_pre(y1), e2m1_pre(y2), e2m1_pre(y3));
+          c = (h & 0xFu) | ((h & 0xF0u) << 4) | ((h & 0xF00u) << 8) | ((h & 0xF000u) << 12);
+        }
+        w[j] = c;
+      }
+      if (!live) continue;
+      if ((lane & 1u) == 0) scales[blk] = static_cast<uint8_t>(sc);
+      codes[blk * 2u + (lane & 1u)] = make_uint4(w[0], w[1], w[2], w[3]);
+      continue;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t lo = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv))
@@ -218,30 +271,6 @@ __global__ void __launch_bounds__(kMxThreads)
     store4(codes, e0, n, vec_out, w);
   }
 }
-
-// Four e2m1 codes (RNE, satfinite) from the hardware conversion, one per
-// nibble, x0 in the low nibble.
-__device__ __forceinline__ uint32_t cvt4_e2m1(float x0, float x1, float x2, float x3) {
-  uint16_t r;
-  asm("{\n\t.reg .b8 t0, t1;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 t0, %2, %1;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 t1, %4, %3;\n\t"
-      "mov.b16 %0, {t0, t1};\n\t}"
-      : "=h"(r)
-      : "f"(x0), "f"(x1), "f"(x2), "f"(x3));
-  return r;
-}
-
-__device__ __forceinline__ float max_nan(float a, float b) {
-  float r;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
-// e2m1 input fix: the reference encodes magnitudes in (0, 0.25) as +0, the
-// hardware as a signed zero; zeroing the negative ones first makes them
-// agree (-0.25 and -0 keep their sign in both).
-__device__ __forceinline__ float e2m1_pre(float y) { return (y > -0.25f && y < 0.0f) ? 0.0f : y; }
 
 // NVFP4 fast kernel (16-byte aligned x, whole blocks): one lane per
 // 16-element block (four float4), no shuffles. The block maximum uses a
@@ -373,18 +402,19 @@ int launch_mx_quantize(const float *x, size_t n, int fmt, uint8_t *codes, uint8_
   // MXFP8 with aligned operands: whole blocks by the fast kernel, a partial
   // last block by the general one
   const size_t full = n / 32;
-  if ((fmt == kE4M3 || fmt == kE5M2) && a16(x) && a16(codes) && full > 0 && full < (1u << 28)) {
+  if (a16(x) && a16(codes) && full > 0 && full < (1u << 28)) {
     const size_t want = (full + kMxThreads / 2 - 1) / (kMxThreads / 2);
     const size_t cap = static_cast<size_t>(current_sm_count()) * 4;  // resident CTAs
     const unsigned g = static_cast<unsigned>(want < cap ? want : cap);
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    uint4 *c4 = reinterpret_cast<uint4 *>(codes);
+    const uint32_t nb = static_cast<uint32_t>(full);
     if (fmt == kE4M3)
-      mx_quant_blocks_kernel<kE4M3><<<g, kMxThreads, 0, st>>>(
-          reinterpret_cast<const float4 *>(x), static_cast<uint32_t>(full),
-          reinterpret_cast<uint4 *>(codes), scales);
+      mx_quant_blocks_kernel<kE4M3><<<g, kMxThreads, 0, st>>>(x4, nb, c4, scales);
+    else if (fmt == kE5M2)
+      mx_quant_blocks_kernel<kE5M2><<<g, kMxThreads, 0, st>>>(x4, nb, c4, scales);
     else
-      mx_quant_blocks_kernel<kE5M2><<<g, kMxThreads, 0, st>>>(
-          reinterpret_cast<const float4 *>(x), static_cast<uint32_t>(full),
-          reinterpret_cast<uint4 *>(codes), scales);
+      mx_quant_blocks_kernel<kE2M1><<<g, kMxThreads, 0, st>>>(x4, nb, c4, scales);
     const int s = cuda_status(cudaGetLastError());
     if (s != ROUGE_B200_OK || full * 32 == n) return s;
     x += full * 32;
