@@ -196,11 +196,7 @@ __global__ void __launch_bounds__(kMxThreads, 4)
         }
         w[j] = c;
       }
-      if (!live) continue;
-      if ((lane & 1u) == 0) scales[blk] = static_cast<uint8_t>(sc);
-      codes[blk * 2u + (lane & 1u)] = make_uint4(w[0], w[1], w[2], w[3]);
-      continue;
-    }
+    } else {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t lo = ID == kE4M3 ? cvt_pair_e4m3(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv))
@@ -233,6 +229,7 @@ __global__ void __launch_bounds__(kMxThreads, 4)
         }
       }
     }
+    }  // (e4m3 / e5m2)
     if (!live) continue;
     if ((lane & 1u) == 0) scales[blk] = static_cast<uint8_t>(sc);
     codes[blk * 2u + (lane & 1u)] = make_uint4(w[0], w[1], w[2], w[3]);
