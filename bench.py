@@ -696,6 +696,63 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
                 f"{peak_src} HBM (5 B/element + 1/16 B scale)"}
     del xa, xb, qa, qb, sa, sb, pa, pb, ta, tb, cm
 
+    # Rank-4 consumers at the reference benchmark's shapes (bench_ai.cpp:73-126):
+    # causal GQA attention S=512, Dh=64, Hq=8, Hkv=2, and the transformer block
+    # S=256, D=512, Hq=8, Hkv=2, Dq=64, Dff=1376; device time of the device
+    # entries (inputs resident) beside one call of the reference's CPU code.
+    S_, Dh_, Hq_, Hkv_ = 512, 64, 8, 2
+    Qa = torch.randn((Hq_, S_, Dh_), device=dev)
+    Ka = torch.randn((Hkv_, S_, Dh_), device=dev)
+    Va = torch.randn((Hkv_, S_, Dh_), device=dev)
+    Oa = torch.empty_like(Qa)
+    wsa = torch.empty(rb.attention_workspace(S_, S_, Dh_, Hq_, Hkv_), dtype=torch.uint8, device=dev)
+    t_att = time_launch(torch, lambda: rb.attention_gqa(Qa, Ka, Va, Oa, workspace=wsa), flush)
+    Sx, Dx, Dqx, Dffx = 256, 512, 64, 1376
+    g_ = torch.Generator(device=dev).manual_seed(9)
+    mk = lambda *sh: torch.randn(sh, device=dev, generator=g_) * 0.05  # noqa: E731
+    xb_ = torch.randn((Sx, Dx), device=dev, generator=g_)
+    w1_ = torch.ones(Dx, device=dev)
+    wts = [mk(Dx, Hq_ * Dqx), mk(Dx, Hkv_ * Dqx), mk(Dx, Hkv_ * Dqx), mk(Hq_ * Dqx, Dx)]
+    mlp = [mk(Dx, Dffx), mk(Dx, Dffx), mk(Dffx, Dx)]
+    ob_ = torch.empty_like(xb_)
+    wsb = torch.empty(rb.transformer_block_workspace(Sx, Dx, Hq_, Hkv_, Dqx, Dffx), dtype=torch.uint8,
+                      device=dev)
+    t_blk = time_launch(torch, lambda: rb.transformer_block(xb_, w1_, *wts, w1_, *mlp, Hq_, Hkv_, Dqx,
+                                                            ob_, workspace=wsb), flush)
+    rb.sync_status()
+    ops_att = 2.0 * S_ * S_ * Dh_ * Hq_
+    ops_blk = (2.0 * Sx * Dx * (Hq_ * Dqx + 2 * Hkv_ * Dqx + Dx) + 2.0 * Sx * Dx * 3 * Dffx
+               + 2.0 * Sx * Sx * Dqx * Hq_)
+    cons = {"attention_gqa_ms": round(t_att, 4),
+            "attention_gqa_gflops": round(ops_att / (t_att * 1e-3) / 1e9, 1),
+            "transformer_block_ms": round(t_blk, 4),
+            "transformer_block_gflops": round(ops_blk / (t_blk * 1e-3) / 1e9, 1),
+            "flops_counted_as": "bench_ai.cpp:88,118-120 (the reference benchmark's own counts)"}
+    refp = os.path.join(ROOT, "oracle", "_ref", "librouge_ref_shims.so")
+    if os.path.exists(refp):
+        import ctypes as C_
+        R = C_.CDLL(refp)
+        P_ = C_.c_void_p
+        R.rouge_attention_gqa.argtypes = [C_.c_int] * 5 + [P_] * 4 + [C_.c_float] + [C_.c_int] * 3
+        q_, k_, v_ = (t.cpu().numpy() for t in (Qa, Ka, Va))
+        o_ = np.empty_like(q_)
+        t0 = time.perf_counter()
+        R.rouge_attention_gqa(S_, S_, Dh_, Hq_, Hkv_, *(P_(a.ctypes.data) for a in (q_, k_, v_, o_)),
+                              0.0, 1, 0, 0)
+        cons["reference_cpu_attention_gqa_ms"] = round((time.perf_counter() - t0) * 1e3, 2)
+        cons["attention_max_abs_diff_vs_reference"] = float(np.abs(o_ - Oa.cpu().numpy()).max())
+        R.rouge_transformer_block.argtypes = [C_.c_int] * 6 + [P_] * 10 + [C_.c_int, C_.c_float,
+                                                                          C_.c_float, P_]
+        host = [t.cpu().numpy() for t in [xb_, w1_] + wts + [w1_] + mlp]
+        ro = np.empty((Sx, Dx), np.float32)
+        t0 = time.perf_counter()
+        R.rouge_transformer_block(Sx, Dx, Hq_, Hkv_, Dqx, Dqx, *(P_(a.ctypes.data) for a in host),
+                                  Dffx, 10000.0, 1e-5, P_(ro.ctypes.data))
+        cons["reference_cpu_transformer_block_ms"] = round((time.perf_counter() - t0) * 1e3, 2)
+        cons["block_max_abs_diff_vs_reference"] = float(np.abs(ro - ob_.cpu().numpy()).max())
+    out["consumers"] = cons
+    del Qa, Ka, Va, Oa, wsa, xb_, wts, mlp, ob_, wsb
+
     # cuDNN-API library: cudnnConvolutionForward at the config-4 shape
     # (N=32, 56x56, 256 -> 256, 3x3 s1 p1), HALF + NHWC (direct: no
     # workspace, alpha / beta in the epilogue, f16 out) and FLOAT + NCHW

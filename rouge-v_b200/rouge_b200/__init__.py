@@ -104,6 +104,12 @@ _SIGS = {
     "rouge_b200_fp4_pack": (_I, [_P, _SZ, _P, _P]),
     "rouge_b200_nvfp4_quantize_packed": (_I, [_P, _SZ, C.c_float, _P, _P, _P]),
     "rouge_b200_gemm_nvfp4": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P]),
+    "rouge_b200_attention_workspace": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "rouge_b200_attention_gqa": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P,
+                                      C.c_float, _I, _I, _I, _P, _SZ, _P]),
+    "rouge_b200_transformer_block_workspace": (_SZ, [_I, _I, _I, _I, _I, _I]),
+    "rouge_b200_transformer_block": (_I, [_I] * 6 + [_P] * 10 + [_I, C.c_float, C.c_float, _P, _P,
+                                                                  _SZ, _P]),
     "rouge_b200_mxfp4_scale_atoms_bytes": (_SZ, [_I, _I]),
     "rouge_b200_mxfp4_scale_atoms": (_I, [_P, _I, _I, _P, _P]),
     "rouge_b200_gemm_mxfp4": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _I, _I, _P]),
@@ -297,6 +303,45 @@ def gemm_mxfp4(A, sfa, B, sfb, C, out_type):
     N = B.shape[0]
     _check("rouge_b200_gemm_mxfp4", lib().rouge_b200_gemm_mxfp4(
         M, N, K, _dp(A), _dp(sfa), _dp(B), _dp(sfb), _dp(C), C.shape[1], out_type, _stream()))
+
+
+def attention_gqa(Q, K, V, O, scale=0.0, causal=1, window=0, kv_off=0, Kq=None, Vq=None,
+                  scales_k=None, scales_v=None, workspace=None):
+    """O[Hq][S][Dh] from Q[Hq][S][Dh] and K/V[Hkv][Skv][Dh] (f32, or e4m3 Kq/Vq with
+    per-head scales); workspace: a uint8 tensor of attention_workspace() bytes."""
+    Hq, S, Dh = Q.shape
+    src = K if Kq is None else Kq
+    Hkv, Skv = src.shape[0], src.shape[1]
+    if workspace is None:
+        import torch
+        workspace = torch.empty(attention_workspace(S, Skv, Dh, Hq, Hkv, Kq is not None),
+                                dtype=torch.uint8, device=Q.device)
+    d = lambda t: None if t is None else _dp(t)  # noqa: E731
+    _check("rouge_b200_attention_gqa", lib().rouge_b200_attention_gqa(
+        S, Skv, Dh, Hq, Hkv, _dp(Q), d(K), d(V), d(Kq), d(Vq), d(scales_k), d(scales_v), _dp(O),
+        scale, causal, window, kv_off, _dp(workspace), workspace.numel(), _stream()))
+
+
+def attention_workspace(S, Skv, Dh, Hq, Hkv, fp8_kv=False):
+    return lib().rouge_b200_attention_workspace(S, Skv, Dh, Hq, Hkv, int(bool(fp8_kv)))
+
+
+def transformer_block_workspace(S, D, Hq, Hkv, Dq, Dff):
+    return lib().rouge_b200_transformer_block_workspace(S, D, Hq, Hkv, Dq, Dff)
+
+
+def transformer_block(x, wrms1, wq, wk, wv, wo, wrms2, wgate, wup, wdown, Hq, Hkv, Dq, out,
+                      rope_theta=10000.0, rms_eps=1e-5, workspace=None):
+    S, D = x.shape
+    Dff = wgate.shape[1]
+    if workspace is None:
+        import torch
+        workspace = torch.empty(transformer_block_workspace(S, D, Hq, Hkv, Dq, Dff),
+                                dtype=torch.uint8, device=x.device)
+    _check("rouge_b200_transformer_block", lib().rouge_b200_transformer_block(
+        S, D, Hq, Hkv, Dq, Dq, _dp(x), _dp(wrms1), _dp(wq), _dp(wk), _dp(wv), _dp(wo), _dp(wrms2),
+        _dp(wgate), _dp(wup), _dp(wdown), Dff, rope_theta, rms_eps, _dp(out), _dp(workspace),
+        workspace.numel(), _stream()))
 
 
 def convert_f32_to_f16(x, out):
