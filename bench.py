@@ -753,6 +753,10 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
     out["consumers"] = cons
     del Qa, Ka, Va, Oa, wsa, xb_, wts, mlp, ob_, wsb
 
+    # The reference's own CPU code for the rows past the hot path, timed on
+    # bounded samples on this host (one call each), beside the numbers above
+    out["reference_cpu_samples"] = reference_cpu_samples()
+
     # cuDNN-API library: cudnnConvolutionForward at the config-4 shape
     # (N=32, 56x56, 256 -> 256, 3x3 s1 p1), HALF + NHWC (direct: no
     # workspace, alpha / beta in the epilogue, f16 out) and FLOAT + NCHW
@@ -821,6 +825,71 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
             del xt, wt, yt, wsb, want
         dnn.cudnnDestroy(hd)
     return out
+
+
+def reference_cpu_samples():
+    """One call of the reference library's cuBLAS shim SGEMM, cuDNN shim
+    convolution, MX / NVFP4 quantizers and dequantize-then-GEMM on bounded
+    samples (oracle/_ref, compiled from the reference's sources)."""
+    import ctypes as C_
+    refp = os.path.join(ROOT, "oracle", "_ref", "librouge_ref_shims.so")
+    if not os.path.exists(refp):
+        return {"unavailable": "oracle/_ref/librouge_ref_shims.so not built"}
+    R = C_.CDLL(refp)
+    P_, I_, F_ = C_.c_void_p, C_.c_int, C_.c_float
+    ptr = lambda a: P_(a.ctypes.data)  # noqa: E731
+    res = {"cores": os.cpu_count()}
+    rng = np.random.default_rng(0)
+
+    def timed(fn):
+        t0 = time.perf_counter()
+        fn()
+        return time.perf_counter() - t0
+
+    # cublasSgemm_v2 (cublas_shim.cpp:199-211) at 1024^3
+    n = 1024
+    a = rng.standard_normal((n, n)).astype(np.float32)
+    b = rng.standard_normal((n, n)).astype(np.float32)
+    c = np.zeros((n, n), np.float32)
+    h = P_()
+    R.cublasCreate_v2(C_.byref(h))
+    one, zero = F_(1.0), F_(0.0)
+    R.cublasSgemm_v2.argtypes = [P_, I_, I_, I_, I_, I_, P_, P_, I_, P_, I_, P_, P_, I_]
+    t = timed(lambda: R.cublasSgemm_v2(h, 0, 0, n, n, n, C_.byref(one), ptr(a), n, ptr(b), n,
+                                       C_.byref(zero), ptr(c), n))
+    R.cublasDestroy_v2(h)
+    res["cublas_sgemm_1024_gflops"] = round(2.0 * n ** 3 / t / 1e9, 2)
+    # cudnnConvolutionForward FLOAT NCHW (cudnn_shim.cpp:188-232): the
+    # config-4 convolution on 2 of its 32 images
+    N, Ci, H, W, Co = 2, 256, 56, 56, 256
+    x = rng.uniform(-1, 1, (N, Ci, H, W)).astype(np.float32)
+    w = rng.uniform(-1, 1, (Co, Ci, 3, 3)).astype(np.float32) * 0.03
+    y = np.zeros((N, Co, H, W), np.float32)
+    R.rouge_conv2d_f32.argtypes = [I_] * 9 + [P_] * 5
+    t = timed(lambda: R.rouge_conv2d_f32(N, Ci, H, W, Co, 3, 3, 1, 1, ptr(x), ptr(w), None, ptr(y),
+                                         None))
+    res["conv2d_f32_2x256x56x56_gflops"] = round(2.0 * N * H * W * Co * 9 * Ci / t / 1e9, 2)
+    # MX / NVFP4 quantizers (narrow.cpp:200-300) on 16 M elements
+    m = 16 << 20
+    xs = rng.standard_normal(m).astype(np.float32)
+    q = np.empty(m, np.uint8)
+    sc = np.empty(m // 16, np.uint8)
+    R.rouge_mx_quantize_f32.argtypes = [P_, I_, I_, P_, P_]
+    R.rouge_nvfp4_quantize_f32.argtypes = [P_, I_, F_, P_, P_]
+    t = timed(lambda: R.rouge_mx_quantize_f32(ptr(xs), m, 1, ptr(q), ptr(sc)))
+    res["mxfp8_quantize_16M_gbs"] = round(m * 5 / t / 1e9, 3)
+    t = timed(lambda: R.rouge_nvfp4_quantize_f32(ptr(xs), m, F_(1.0), ptr(q), ptr(sc)))
+    res["nvfp4_quantize_16M_gbs"] = round(m * 5 / t / 1e9, 3)
+    # the reference's route to a GEMM on MX data: dequantize, then its f32
+    # GEMM (rouge_mx_dequantize_f32 + rouge_gemm_f32) at 1024^3
+    R.rouge_mx_quantize_f32(ptr(a), n * n, 1, ptr(q), ptr(sc))
+    R.rouge_mx_dequantize_f32.argtypes = [P_, P_, I_, I_, P_]
+    R.rouge_gemm_f32.argtypes = [I_, I_, I_, P_, P_, P_, P_]
+    deq = np.empty(n * n, np.float32)
+    t = timed(lambda: (R.rouge_mx_dequantize_f32(ptr(q), ptr(sc), n * n, 1, ptr(deq)),
+                       R.rouge_gemm_f32(n, n, n, ptr(deq), ptr(b), ptr(c), None)))
+    res["mx_dequantize_plus_gemm_f32_1024_gflops"] = round(2.0 * n ** 3 / t / 1e9, 2)
+    return res
 
 
 def check_parity(rb, X, qx, sx, qw, sw, C):
