@@ -111,6 +111,14 @@ int rouge_b200_set_tile_mode(int mode);
  * Returns ROUGE_B200_OK or the failure (e.g. ROUGE_B200_ETIMEOUT). */
 int rouge_b200_sync_status(void *stream);
 
+/* Failure-detection check of the bounded device waits: launches one CTA on
+ * `stream` that waits on an mbarrier nothing arrives at, bounded by
+ * limit_ns (1e6..2e9 ns, else ROUGE_B200_EINVAL). The launch ends by itself
+ * after about limit_ns; the next rouge_b200_sync_status(stream) returns
+ * ROUGE_B200_ETIMEOUT and clears it, and the context stays usable.
+ * Returns the launch status. */
+int rouge_b200_check_wait_limit(unsigned long long limit_ns, void *stream);
+
 /* Layout of the B operand of a GEMM. */
 #define ROUGE_B200_B_KN 0 /* B[K][N] row-major (the reference's layout)  */
 #define ROUGE_B200_B_NK 1 /* B[N][K] row-major (column-major B, K-major) */

@@ -61,18 +61,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false if
-// *abort became non-zero or the time limit passed.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          const volatile int *abort) {
+// *abort became non-zero or limit_ns passed.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity,
+                                              const volatile int *abort, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+      if (global_timer_ns() - t0 > limit_ns) return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          const volatile int *abort) {
+  return mbar_wait_for(bar, parity, abort, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------- TMA

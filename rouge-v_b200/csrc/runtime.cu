@@ -3,6 +3,8 @@
 
 #include <cudaTypedefs.h>
 
+#include "ptx.cuh"
+
 #include <array>
 #include <atomic>
 
@@ -237,6 +239,33 @@ int ensure_workspace(HostCallContext *ctx, size_t bytes) {
   return ROUGE_B200_OK;
 }
 
+// The wait-limit check: warp 0 waits with `limit_ns` on an mbarrier that
+// nothing arrives at; when the limit passes it raises the block's abort flag
+// and records ROUGE_B200_ETIMEOUT in the error word, exactly as a GEMM warp
+// whose TMA or MMA partner never signals does. Warps 1-3 wait on the same
+// barrier with the kernels' own limit and leave on the abort flag, so the
+// launch ends after about limit_ns, not after kWaitLimitNs.
+__global__ void __launch_bounds__(128) wait_limit_kernel(int *err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  volatile int *abort = &abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    *abort = 0;
+    mbar_init_fence();
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  if (warp == 0) {
+    if (!mbar_wait_for(&bar, 0, abort, limit_ns) && threadIdx.x == 0) {
+      *abort = 1;
+      atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
+    }
+  } else if (!mbar_wait(&bar, 0, abort) && (threadIdx.x & 31) == 0 && !*abort) {
+    atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
+  }
+}
+
 }  // namespace rb200
 
 extern "C" {
@@ -290,6 +319,21 @@ int rouge_b200_sync_status(void *stream) {
   int st = rb200::device_ready();
   if (st != ROUGE_B200_OK) return st;
   return rb200::take_device_error(rb200::as_stream(stream));
+}
+
+
+/* Runs one CTA whose wait can never complete, bounded by limit_ns (1 ms to
+ * 2 s), on `stream`: the launch ends by itself and the next
+ * rouge_b200_sync_status on that stream returns ROUGE_B200_ETIMEOUT, after
+ * which the context is still usable. Returns the launch status. */
+int rouge_b200_check_wait_limit(unsigned long long limit_ns, void *stream) {
+  int st = rb200::device_ready();
+  if (st != ROUGE_B200_OK) return st;
+  if (limit_ns < 1000000ull || limit_ns > 2000000000ull) return rb200::set_status(ROUGE_B200_EINVAL);
+  int *err = rb200::device_error_word();
+  if (!err) return rb200::set_status(ROUGE_B200_ENOMEM);
+  rb200::wait_limit_kernel<<<1, 128, 0, rb200::as_stream(stream)>>>(err, limit_ns);
+  return rb200::cuda_status(cudaGetLastError());
 }
 
 }  // extern "C"

@@ -65,6 +65,7 @@ _SIGS = {
     "rouge_gemm_isa_variant": (C.c_char_p, []),
     "rouge_b200_device_ok": (_I, []),
     "rouge_b200_sync_status": (_I, [_P]),
+    "rouge_b200_check_wait_limit": (_I, [C.c_ulonglong, _P]),
     "rouge_b200_set_sm_budget": (_I, [_I]),
     "rouge_b200_set_tile_mode": (_I, [_I]),
     "rouge_quantize_e4m3": (C.c_uint8, [_F]),
@@ -408,6 +409,15 @@ def conv2d_nhwc_f16(X, Wt, bias, Y, stride, pad, is_bf16=False):
 
 def sync_status():
     _check("rouge_b200_sync_status", lib().rouge_b200_sync_status(_stream()))
+
+
+def check_wait_limit(limit_ns):
+    """Launches the never-completing bounded wait (limit_ns) on the current
+    stream and returns the status rouge_b200_sync_status then reports
+    (ROUGE_B200_ETIMEOUT when the limit works)."""
+    L = lib()
+    _check("rouge_b200_check_wait_limit", L.rouge_b200_check_wait_limit(int(limit_ns), _stream()))
+    return L.rouge_b200_sync_status(_stream())
 
 
 class tile_mode:

@@ -98,3 +98,65 @@ def test_sharded_gather_gloo(world, M, N, K, R):
     results = dict(q.get(timeout=5) for _ in range(world))
     assert all(p.exitcode == 0 for p in procs)
     assert all(results[r] for r in range(world)), results
+
+
+def _failing_rank(rank, world, port, q):
+    """Rank 1's local GEMM fails the way a device entry reports a bounded
+    wait that ran out (the binding raises); rank 1 leaves without joining
+    the band's all-gather. Rank 0 must get an error from that collective
+    within the process group's short timeout instead of waiting for good."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    M, N, K, R = 256, 64, 32, 128
+
+    def gemm(a, sa, w, sw, out):
+        if rank == 1:
+            raise RuntimeError("rouge_b200_gemm_i8: device-side wait timed out (-5)")
+        out.zero_()
+
+    sh = ShardedW8A8(M, N, K, rank, world, "cpu", R=R, local_gemm=gemm, unshard=_cpu_unshard)
+    a = torch.zeros((M, K), dtype=torch.int8)
+    sa = torch.ones(M)
+    w = torch.zeros((sh.ns, K), dtype=torch.int8)
+    sw = torch.ones(sh.ns)
+    t0 = time.monotonic()
+    try:
+        sh(a, sa, w, sw)
+        q.put((rank, "completed", time.monotonic() - t0))
+    except RuntimeError as e:
+        q.put((rank, "timed out" if "timed out" in str(e) else "error", time.monotonic() - t0))
+        if rank == 1:
+            raise
+    finally:
+        if rank == 0:
+            try:
+                dist.destroy_process_group()
+            except Exception:  # the peer is gone; nothing left to tear down
+                pass
+
+
+def test_rank_failure_ends_peer_collective_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank waited past every timeout"
+    res = {}
+    while not q.empty():
+        r, what, dt = q.get(timeout=5)
+        res[r] = (what, dt)
+    assert res[1][0] == "timed out"              # the failing call raised on rank 1
+    assert procs[1].exitcode != 0                # and the rank left
+    assert res[0][0] != "completed"              # rank 0's all-gather ended with an error
+    assert res[0][1] < 60.0, res
