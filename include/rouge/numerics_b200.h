@@ -289,6 +289,25 @@ int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
                        const float *scales_b, int b_cols, void *C, int ldc,
                        int out_type, void *stream);
 
+/* The W8A8 linear step -- rouge_quantize_i8_channel of the activations
+ * followed by rouge_gemm_i8 with per-row and per-column scales
+ * (quant_int8.cpp:72-90, 189-211) -- as one device call:
+ *   Aq[M][K], sa[M] = rouge_b200_quantize_i8_rows(X[M][K])
+ *   C = rouge_b200_gemm_i8(Aq, Wq, ROUGE_B200_B_NK, sa, 1, sw, 1, out_type)
+ * with identical results. Wq[N][K] holds the weights' int8 codes (one row
+ * per output channel), sw[N] their scales. When K <= 4096 and the problem
+ * takes CTA-pair tiles the quantization runs inside the GEMM launch (the
+ * first round of tiles starts as soon as its rows are coded; the other
+ * rows are coded while the tiles run); otherwise two launches.
+ * `workspace`: rouge_b200_w8a8_workspace_bytes(M) bytes of device memory,
+ * 4-byte aligned, zeroed before its first use; every call leaves it zeroed.
+ * Calls that may run at the same time need separate workspaces.
+ * Alignment: X 16 bytes, K % 16 == 0, plus those of rouge_b200_gemm_i8. */
+size_t rouge_b200_w8a8_workspace_bytes(int M);
+int rouge_b200_w8a8_linear(int M, int N, int K, const float *X, const int8_t *Wq,
+                           const float *sw, int8_t *Aq, float *sa, void *C, int ldc,
+                           int out_type, void *workspace, void *stream);
+
 /* Column-major BLAS GEMM (the semantics of cublasSgemm / cublasGemmEx; the
  * reference implements them on its CPU GEMM, cublas_shim.cpp:36-65,199-211):
  *   C (m x n, column-major, ldc) = alpha * op(A) * op(B) + beta * C

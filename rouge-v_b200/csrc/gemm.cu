@@ -30,6 +30,7 @@
 #include "formats.cuh"
 #include "x86fp.cuh"
 #include "ptx.cuh"
+#include "i8code.cuh"
 #include "runtime.cuh"
 
 namespace rb200 {
@@ -86,6 +87,23 @@ struct GemmArgs {
   // Block-scaled kind (MXF8): operand formats (E4M3 0, E5M2 1) and the
   // number of 128-K blocks per row of the scale-atom arrays.
   int mx_fmt_a, mx_fmt_b, sf_kblocks;
+  // Fused per-row quantization of A (the W8A8 linear step, CTA-pair int8
+  // kernel only): the launch itself turns the f32 rows fq_x[M][K] into A's
+  // codes fq_codes[M][K] and scales fq_scales[M] (= scales_a). fq_cnt[b]
+  // counts the finished rows of 128-row block b, fq_cnt[nblk] the finished
+  // CTAs and fq_cnt[nblk + 1] the rows handed out (nblk = ceil(M/128)); the
+  // last CTA zeroes them all. Rows below fq_rows0 (those of the first round
+  // of tiles) are quantized by every warp before the tiles start, the
+  // others, in order, by warps 2-3 and by idle epilogue warps while the
+  // tiles run.
+  const float *fq_x;
+  int8_t *fq_codes;
+  float *fq_scales;
+  unsigned *fq_cnt;
+  int fq_rows0;
+  // units walk N first (m-block = tile / num_n), so that the first round
+  // needs few blocks of A rows
+  int n_fast;
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
@@ -143,7 +161,12 @@ __device__ __forceinline__ void unit_coords(int u, const GemmArgs &args, int &mb
     t = args.split_from + (u - args.split_from) / parts;
     part = (u - args.split_from) - (t - args.split_from) * parts;
   }
-  tile_coords(t, args.num_m, args.num_n, mb, nb);
+  if (args.n_fast) {
+    mb = t / args.num_n;
+    nb = t - mb * args.num_n;
+  } else {
+    tile_coords(t, args.num_m, args.num_n, mb, nb);
+  }
 }
 
 __device__ __forceinline__ void report(int *err, volatile int *abort, int code) {
@@ -415,7 +438,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   const bool row_ok = row < args.M;
   float sa = 1.0f;
   if constexpr (KIND == MmaKind::I8) {
-    if (OUT != ROUGE_B200_OUT_I32 && row_ok) sa = __ldg(args.scales_a + (args.a_rows ? row : 0));
+    // (scales written by this launch itself are read through L2)
+    if (OUT != ROUGE_B200_OUT_I32 && row_ok)
+      sa = args.fq_cnt ? __ldcg(args.scales_a + row) : __ldg(args.scales_a + (args.a_rows ? row : 0));
   }
   const bool sa_ok = fabsf(sa) < 7.9e28f;  // finite and below 2^96
   const uint32_t tbase = tcol + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -716,7 +741,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //   empty[s]  each CTA: the leader's MMA commit arrives on both
 //   tfull[2]  each CTA: the leader's commit after a tile's last k-block
 //   tempty[2] leader only: 16 arrivals, one per epilogue warp of each CTA
-template <MmaKind KIND, int BN, bool B_MN>
+template <MmaKind KIND, int BN, bool B_MN, bool FQ = false>
 struct Cfg2 {
   static constexpr int ESIZE = KIND == MmaKind::TF32 ? 4 : (KIND == MmaKind::F16 ? 2 : 1);
   static constexpr int BK = kBKBytes / ESIZE;
@@ -755,21 +780,29 @@ struct Cfg2 {
   static constexpr int TMEM_COLS = MX ? 512 : 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
-  static constexpr int BAR_BYTES = 256;
+  // fused quantization: two 16 KB row slots (warps 2-3) and 12 more
+  // mbarriers (one per warp's row slot)
+  static constexpr int QSLOT = 16384;
+  static constexpr int QSLOT_BYTES = FQ ? 2 * QSLOT : 0;
+  static constexpr int BAR_BYTES = FQ ? 512 : 256;
 #ifndef RB200_PAIR_EPI_BUFS  // staging buffers per epilogue warp (tuning builds)
 #define RB200_PAIR_EPI_BUFS 1
 #endif
   static constexpr int EPI_BUFS = RB200_PAIR_EPI_BUFS;
   static constexpr int EPI_BYTES = 8 * EPI_BUFS * kStageBytes;
-  static constexpr int STAGE_ROOM = (232448 - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES;
+  static constexpr int STAGE_ROOM =
+      (232448 - 1024 - EPI_BYTES - QSLOT_BYTES - BAR_BYTES) / STAGE_BYTES;
 #ifdef RB200_PAIR_STAGES  // stage-count override for tuning builds
   static constexpr int STAGES = RB200_PAIR_STAGES;
 #else
   static constexpr int STAGES = STAGE_ROOM > 8 ? 8 : STAGE_ROOM;
 #endif
-  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES + EPI_BYTES + QSLOT_BYTES;
+  static constexpr int SMEM = 1024 + BAR_OFF + BAR_BYTES;
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
+  // the prologue's 12 row slots: 10 in stage memory, the 2 quantizer slots
+  static_assert(!FQ || (KIND == MmaKind::I8 && STAGES * STAGE_BYTES >= 10 * QSLOT), "FQ");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(!B_MN || B_CHUNKS >= 1, "MN-major B needs whole 128-byte chunks per CTA");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
@@ -778,25 +811,160 @@ struct Cfg2 {
                 "MX tile");
 };
 
+// Scale and codes of one row held in registers (v[j] = float4 j * 32 +
+// lane of the row; nvec float4 in all) as quant_int8.cpp:72-90 computes
+// them: scale and reciprocal in double, branch-free single-precision codes,
+// words near a rounding tie re-encoded in double afterwards from a second
+// read of their inputs (xr). Then one count on the row's 128-row block
+// (release: the codes and scale are visible to whoever sees the count).
+template <int VPL>
+__device__ __forceinline__ void fq_encode_row(const GemmArgs &args, int r, const float4 (&v)[VPL],
+                                              int nvec, int lane) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j)
+    amax = max3(amax, max3(fabsf(v[j].x), fabsf(v[j].y), fabsf(v[j].z)), fabsf(v[j].w));
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const double a = static_cast<double>(amax);
+  const float sc = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
+  const double inv = __ddiv_rn(1.0, static_cast<double>(sc));
+  const float inv_f = __double2float_rn(inv);
+  const bool exact_row = isinf(inv_f);
+  if (lane == 0) args.fq_scales[r] = sc;
+  uint32_t *orow = reinterpret_cast<uint32_t *>(args.fq_codes + static_cast<size_t>(r) * args.K);
+  uint32_t redo = 0;
+#pragma unroll
+  for (int j = 0; j < VPL; ++j) {
+    const int i = j * 32 + lane;
+    bool tie;
+    const uint32_t w = encode4_i8_fast(v[j], inv_f, tie);
+    tie |= exact_row;
+    if (i < nvec && !tie) orow[i] = w;
+    redo |= (tie && i < nvec) ? (1u << j) : 0u;
+  }
+  const float4 *xr = reinterpret_cast<const float4 *>(args.fq_x + static_cast<size_t>(r) * args.K);
+  while (redo) {
+    const int j = __ffs(redo) - 1;
+    redo &= redo - 1;
+    orow[j * 32 + lane] = encode4_i8_exact(__ldg(xr + j * 32 + lane), inv);
+  }
+  // codes and scale before the count, also for the TMA loads that read them
+  fence_async_global();
+  __syncwarp();
+  if (lane == 0) red_release_add(args.fq_cnt + (r >> 7), 1u);
+}
+
+// Rows [0, fq_rows0) of the fused quantizer (GemmArgs::fq_x), before the
+// tiles start: every warp of the grid takes rows with the stride of the
+// grid's warps (12 per CTA) through its 16 KB shared-memory slot -- bulk
+// copy, registers (32 float4 per lane: rows up to 4096 elements), the next
+// row's copy into the slot, then fq_encode_row. A copy that does not land
+// in time reports ROUGE_B200_ETIMEOUT and ends the warp's rows (the block
+// counts then stay short and the tiles that need them time out as well).
+__device__ __forceinline__ void fq_rows_first(const GemmArgs &args, uint8_t *slot, uint64_t *bar,
+                                              int warp, int lane) {
+  constexpr int kVpl = 32;
+  const int end = args.fq_rows0;
+  const int gw = static_cast<int>(gridDim.x) * 12;
+  int r = static_cast<int>(blockIdx.x) * 12 + warp;
+  const uint32_t row_bytes = static_cast<uint32_t>(args.K) * 4u;
+  const int nvec = args.K >> 2;
+  bool in_flight = r < end;
+  if (lane == 0 && in_flight) {
+    mbar_arrive_expect_tx(bar, row_bytes);
+    bulk_load(slot, args.fq_x + static_cast<size_t>(r) * args.K, row_bytes, bar);
+  }
+  const volatile int never = 0;
+  uint32_t phase = 0;
+  while (r < end) {
+    const bool got = mbar_wait(bar, phase, &never);
+    if (!__all_sync(0xffffffffu, got)) {
+      if (lane == 0 && args.err) atomicCAS(args.err, 0, ROUGE_B200_ETIMEOUT);
+      break;
+    }
+    phase ^= 1u;
+    in_flight = false;
+    const float4 *row = reinterpret_cast<const float4 *>(slot);
+    float4 v[kVpl];
+#pragma unroll
+    for (int j = 0; j < kVpl; ++j) {
+      const int i = j * 32 + lane;
+      v[j] = i < nvec ? row[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // the slot is in registers: it takes the warp's next row
+    fence_async_smem();
+    __syncwarp();
+    const int rn = r + gw;
+    if (lane == 0 && rn < end) {
+      mbar_arrive_expect_tx(bar, row_bytes);
+      bulk_load(slot, args.fq_x + static_cast<size_t>(rn) * args.K, row_bytes, bar);
+      in_flight = true;
+    }
+    fq_encode_row(args, r, v, nvec, lane);
+    r = rn;
+  }
+  if (in_flight && lane == 0) mbar_wait(bar, phase, &never);  // let the last copy land
+  // L2 prefetch of the first rows the running tiles' quantizer will claim
+  const int pf = args.fq_rows0 + static_cast<int>(blockIdx.x) * 12 + warp;
+  if (lane == 0 && pf < args.M && pf < args.fq_rows0 + 512)
+    bulk_prefetch_l2(args.fq_x + static_cast<size_t>(pf) * args.K, row_bytes);
+}
+
+// Rows [fq_rows0, M) of the fused quantizer are handed out in order from
+// a counter (fq_cnt[nblk + 1]) while the tiles run, to warps 2-3 and to the
+// epilogue warps while their next accumulator is not ready. Returns the
+// claimed row (>= M: none left) and starts an L2 prefetch of the row
+// kFqAhead places further on, which the warps claim a few microseconds
+// later; the first kFqAhead rows are prefetched by fq_rows_first.
+constexpr int kFqAhead = 512;
+
+__device__ __forceinline__ int fq_claim(const GemmArgs &args, int lane) {
+  const int nblk = (args.M + kBM - 1) / kBM;
+  int r = 0;
+  if (lane == 0) {
+    r = args.fq_rows0 + static_cast<int>(atomicAdd(args.fq_cnt + nblk + 1, 1u));
+    if (r + kFqAhead < args.M)
+      bulk_prefetch_l2(args.fq_x + static_cast<size_t>(r + kFqAhead) * args.K,
+                       static_cast<uint32_t>(args.K) * 4u);
+  }
+  return __shfl_sync(0xffffffffu, r, 0);
+}
+
+// One claimed row, loaded straight into registers (streaming loads: no
+// shared memory and no TMA queue, which the tiles' loads keep busy).
+__device__ __forceinline__ void fq_row_direct(const GemmArgs &args, int r, int lane) {
+  constexpr int kVpl = 32;
+  const int nvec = args.K >> 2;
+  const float4 *xr = reinterpret_cast<const float4 *>(args.fq_x + static_cast<size_t>(r) * args.K);
+  float4 v[kVpl];
+#pragma unroll
+  for (int j = 0; j < kVpl; ++j) {
+    const int i = j * 32 + lane;
+    v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  fq_encode_row(args, r, v, nvec, lane);
+}
+
 __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint32_t peer_abort) {
   *abort = 1;
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(peer_abort), "r"(1u) : "memory");
   if (err) atomicCAS(err, 0, ROUGE_B200_ETIMEOUT);
 }
 
-template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false>
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV = false, bool FQ = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ OutMaps om,
                     const GemmArgs args) {
-  using C = Cfg2<KIND, BN, B_MN>;
+  using C = Cfg2<KIND, BN, B_MN, FQ>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sB = smem + C::STAGES * C::A_BYTES;
   uint8_t *sSF = sB + C::STAGES * C::B_BYTES;  // block-scaled kind: [stage][SFA | SFB]
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   uint64_t *empty = full + C::STAGES;
   uint64_t *tfull = empty + C::STAGES;  // [2]
   uint64_t *tempty = tfull + 2;         // [2]
@@ -804,6 +972,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *ovl = mdone + 1;            // [2] overlapping accumulators: shared chunk drained
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ovl + 2);
   volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  uint64_t *qbar = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF + 256);  // [12] fused quantizer
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -823,6 +992,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&ovl[i], 8);  // the 4 warps of one column half, both CTAs
     }
     mbar_init(mdone, 1);
+    if constexpr (FQ)
+      for (int w = 0; w < 12; ++w) mbar_init(&qbar[w], 1);
     *abort = 0;
     mbar_init_fence();
     tma_prefetch_desc(&tmA);
@@ -846,6 +1017,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // only after this point.
   grid_dependency_wait();
 
+  if constexpr (FQ) {
+    // ------------------------------------------------------------ fused quantizer
+    // Every warp quantizes its rows of the first round's A blocks through a
+    // row slot of stage memory (warps 2-3: their own slots); the 10 warps
+    // that own stage memory then meet on named barrier 1 before the first
+    // TMA load into it. Warps 2-3 go on with the remaining rows meanwhile.
+    const bool qwarp = warp == 2 || warp == 3;
+    uint8_t *slot = qwarp ? smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES + (warp - 2) * C::QSLOT
+                          : smem + (warp < 2 ? warp : warp - 2) * C::QSLOT;
+    fq_rows_first(args, slot, &qbar[warp], warp, lane);
+    if (qwarp) {
+      for (int r = fq_claim(args, lane); r < args.M; r = fq_claim(args, lane)) fq_row_direct(args, r, lane);
+    } else {
+      asm volatile("bar.sync 1, 320;" ::: "memory");
+    }
+  }
+
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     const uint32_t full0 = mapa_shared(smem_u32(full), 0);  // leader's full[0]
@@ -862,6 +1050,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           2u * static_cast<uint32_t>(C::A_BYTES + half_w * kBKBytes + C::SFA_BYTES + C::SFB_BYTES);
       int cw = 0, ch = 0, cn = 0;
       if constexpr (CONV) conv_box(args, m0, cw, ch, cn);
+      if constexpr (FQ) {  // this CTA's 128 A rows quantized (codes for the TMA loads)
+        if (m0 < args.M) {
+          if (!wait_count(args.fq_cnt + (m0 / kBM), static_cast<unsigned>(min(kBM, args.M - m0)),
+                          abort)) {
+            report_pair(args.err, abort, peer_abort);
+            ok = false;
+            break;
+          }
+          fence_async_global();
+        }
+      }
       for (int kb = 0; kb < args.num_k; ++kb, ++it) {
         const int s = it % C::STAGES;
         const uint32_t round = static_cast<uint32_t>(it / C::STAGES);
@@ -1049,16 +1248,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (args.scale_a && args.scale_b) sab = x86_mul(__ldg(args.scale_a), __ldg(args.scale_b));
       if (args.blas) sab = args.alpha;
     }
+    bool fq_more = FQ;  // rows of A left to claim
     for (int t = cluster; t < args.num_tiles; t += nclusters, ++local) {
       int mb, nb, part, parts;
       unit_coords(t, args, mb, nb, part, parts);
       const int slot = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if constexpr (FQ) {
+        // code rows of A while this tile's accumulator is not ready (a row
+        // takes a few microseconds; the other accumulator buffer keeps the
+        // MMA busy meanwhile)
+        while (fq_more && !__any_sync(0xffffffffu, mbar_test_wait(&tfull[slot], use & 1u))) {
+          const int r = fq_claim(args, lane);
+          if (r >= args.M) {
+            fq_more = false;
+            break;
+          }
+          fq_row_direct(args, r, lane);
+        }
+      }
       if (!mbar_wait(&tfull[slot], use & 1u, abort)) {
         report_pair(args.err, abort, peer_abort);
         break;
       }
       tc_fence_after_sync();
+      if constexpr (FQ) {  // the rows' scales (complete: the tile's codes were)
+        const int m0 = mb * 2 * kBM + static_cast<int>(rank) * kBM;
+        if (m0 < args.M &&
+            !wait_count(args.fq_cnt + (m0 / kBM), static_cast<unsigned>(min(kBM, args.M - m0)), abort)) {
+          report_pair(args.err, abort, peer_abort);
+          break;
+        }
+      }
       epilogue_tile<KIND, OUT, C::EPI_BUFS>(
           args, tmem_base + static_cast<uint32_t>(slot * C::ACC1_COL),
           mb * 2 * kBM + static_cast<int>(rank) * kBM, nb * BN + part * (BN / parts), BN / parts,
@@ -1084,12 +1305,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after_sync();
     tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
   }
+  if constexpr (FQ) {
+    // The last CTA to finish zeroes the block counts for the next launch
+    // (every other CTA is past its last use of them).
+    if (threadIdx.x == 0) {
+      const int nblk = (args.M + kBM - 1) / kBM;
+      if (atom_add_acq_rel(args.fq_cnt + nblk, 1u) == gridDim.x - 1u) {
+        for (int b = 0; b <= nblk + 1; ++b) args.fq_cnt[b] = 0u;
+      }
+    }
+  }
 }
 
 // Builds the output map and launches one GEMM / convolution.
 // make_b(box_rows, map) encodes the B operand's tensor map with boxes of
 // `box_rows` rows (K-major B) and returns a status.
-template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR, class MakeB>
+template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR, bool FQ = false, class MakeB>
 int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_t st) {
   int s = ROUGE_B200_OK;
   CUtensorMap tb;
@@ -1160,8 +1391,8 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
     cfg.numAttrs = 1;
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, args));
   } else {
-    using C = Cfg2<KIND, BN, B_MN>;
-    auto kern = gemm_tc2_kernel<KIND, BN, B_MN, OUT, CONV>;
+    using C = Cfg2<KIND, BN, B_MN, FQ>;
+    auto kern = gemm_tc2_kernel<KIND, BN, B_MN, OUT, CONV, FQ>;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -1222,6 +1453,18 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
       if (s != ROUGE_B200_OK) return s;
     }
     if (clusters > args.num_tiles) clusters = args.num_tiles;
+    if constexpr (FQ) {
+      // rows of the A blocks the first RB200_FQ_ROUNDS rounds of units need
+      // (units walk N first, so a round's last unit has its largest m-block)
+#ifndef RB200_FQ_ROUNDS  // rounds quantized before the tiles start (tuning builds)
+#define RB200_FQ_ROUNDS 1
+#endif
+      const int u = (args.num_tiles < RB200_FQ_ROUNDS * clusters ? args.num_tiles
+                                                                  : RB200_FQ_ROUNDS * clusters) - 1;
+      const int t = u >= args.split_from ? args.split_from + (u - args.split_from) / args.split : u;
+      const long long rows = static_cast<long long>(t / args.num_n + 1) * 2 * kBM;
+      args.fq_rows0 = rows < args.M ? static_cast<int>(rows) : args.M;
+    }
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, tc, args));
   }
@@ -1462,6 +1705,58 @@ int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const in
   return launch_kind<MmaKind::I8>(A, lda, B, ldb, b_layout, g, out_type, st);
 }
 
+int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8_t *out,
+                         cudaStream_t st);
+
+// The W8A8 linear step: per-row quantization of X (codes Aq, scales sa)
+// and C = dequant(Aq . Wq^T). One launch of the CTA-pair int8 kernel with
+// the quantizer fused (see GemmArgs::fq_x) when K <= 4096 (a row fits a
+// 16 KB slot) and the problem takes CTA-pair tiles; otherwise the row
+// quantizer, then the GEMM.
+int launch_w8a8_linear(int M, int N, int K, const float *X, const int8_t *Wq, const float *sw,
+                       int8_t *Aq, float *sa, void *Cp, long long ldc, int out_type, unsigned *ws,
+                       cudaStream_t st) {
+  const bool fuse = K <= 4096 && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && use_pair_tiles(M, N);
+  if (!fuse) {
+    int s = launch_quant_i8_rows(X, M, K, sa, Aq, st);
+    if (s != ROUGE_B200_OK) return s;
+    return launch_gemm_i8(M, N, K, Aq, K, Wq, K, ROUGE_B200_B_NK, sa, 1, sw, 1, Cp, ldc, out_type,
+                          st);
+  }
+  GemmArgs g{};
+  g.M = M; g.N = N; g.K = K;
+  g.C = Cp; g.ldc = ldc;
+  g.scales_a = sa; g.scales_b = sw; g.a_rows = 1; g.b_cols = 1;
+  g.use_tma_store = vec_ok(Cp, ldc, out_type);
+  g.vec16 = (reinterpret_cast<uintptr_t>(sw) & 15u) == 0;
+  g.err = device_error_word();
+  g.fq_x = X;
+  g.fq_codes = Aq;
+  g.fq_scales = sa;
+  g.fq_cnt = ws;
+  g.n_fast = 1;
+  g.num_m = (M + 2 * kBM - 1) / (2 * kBM);
+  g.num_n = (N + 255) / 256;
+  g.num_k = (K + kBKBytes - 1) / kBKBytes;
+  g.num_tiles = g.num_m * g.num_n;
+  CUtensorMap ta;
+  int s = make_tmap_2d(&ta, Aq, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, static_cast<uint64_t>(K),
+                       kBKBytes, kBM);
+  if (s != ROUGE_B200_OK) return s;
+  auto make_b = [&](int box_rows, CUtensorMap *tb) {
+    return make_tmap_2d(tb, Wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, static_cast<uint64_t>(K),
+                        kBKBytes, box_rows);
+  };
+  switch (out_type) {
+    case ROUGE_B200_OUT_F32:
+      return launch_tiles<MmaKind::I8, 256, false, ROUGE_B200_OUT_F32, false, true, true>(ta, make_b, g, st);
+    case ROUGE_B200_OUT_BF16:
+      return launch_tiles<MmaKind::I8, 256, false, ROUGE_B200_OUT_BF16, false, true, true>(ta, make_b, g, st);
+    default:
+      return launch_tiles<MmaKind::I8, 256, false, ROUGE_B200_OUT_I32, false, true, true>(ta, make_b, g, st);
+  }
+}
+
 // As launch_gemm_i8, with the device word that receives a timeout status
 // supplied by the caller.
 int launch_gemm_i8_with_err(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
@@ -1689,6 +1984,24 @@ int rouge_b200_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, in
   const long long ldb = b_layout == ROUGE_B200_B_KN ? N : K;
   return launch_gemm_i8(M, N, K, A, K, B, ldb, b_layout, scales_a, a_rows, scales_b, b_cols, C,
                         ldc, out_type, as_stream(stream));
+}
+
+size_t rouge_b200_w8a8_workspace_bytes(int M) {
+  return M > 0 ? (static_cast<size_t>(M + 127) / 128 + 2) * sizeof(unsigned) : 0;
+}
+
+int rouge_b200_w8a8_linear(int M, int N, int K, const float *X, const int8_t *Wq, const float *sw,
+                           int8_t *Aq, float *sa, void *C, int ldc, int out_type, void *workspace,
+                           void *stream) {
+  if (!X || !sw || !sa || !workspace) return set_status(ROUGE_B200_EINVAL);
+  int s = check_common(M, N, K, Aq, Wq, C, ldc, ROUGE_B200_B_NK, out_type, 1);
+  if (s != ROUGE_B200_OK) return set_status(s);
+  if ((K & 3) || (reinterpret_cast<uintptr_t>(X) & 15u) || (reinterpret_cast<uintptr_t>(workspace) & 3u))
+    return set_status(ROUGE_B200_EUNSUPPORTED);
+  s = device_ready();
+  if (s != ROUGE_B200_OK) return s;
+  return launch_w8a8_linear(M, N, K, X, Wq, sw, Aq, sa, C, ldc, out_type,
+                            static_cast<unsigned *>(workspace), as_stream(stream));
 }
 
 int rouge_b200_gemm_i8_bcast(int M, int N, int K, const int8_t *A, const int8_t *B, int b_layout,

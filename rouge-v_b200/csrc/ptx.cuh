@@ -60,6 +60,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test: has the phase with the given parity completed?
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete. Returns false if
 // *abort became non-zero or limit_ns passed.
 __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity,
@@ -184,6 +197,50 @@ __device__ __forceinline__ void multimem_st_v4(uint64_t addr, uint4 v) {
   asm volatile("multimem.st.weak.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(v.x),
                "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
+}
+
+// ------------------------------------ counters between CTAs of one grid
+//
+// A CTA that wrote data with ordinary (generic-proxy) stores publishes it
+// with fence_async_global + red_release_add; a CTA that reads it with TMA
+// (async proxy) waits with wait_count, whose acquire is followed by
+// fence_async_global before the loads are issued.
+
+__device__ __forceinline__ void fence_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v)
+               : "memory");
+  return old;
+}
+
+// Waits until *p >= need. Returns false if *abort became non-zero or the
+// time limit passed.
+__device__ __forceinline__ bool wait_count(const unsigned *p, unsigned need,
+                                           const volatile int *abort) {
+  if (ld_acquire(p) >= need) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(100);
+    if (ld_acquire(p) >= need) return true;
+    if ((i & 15u) == 0) {
+      if (*abort) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
 }
 
 // ------------------------------------------- programmatic dependent launch

@@ -66,6 +66,8 @@ _SIGS = {
     "rouge_b200_device_ok": (_I, []),
     "rouge_b200_sync_status": (_I, [_P]),
     "rouge_b200_check_wait_limit": (_I, [C.c_ulonglong, _P]),
+    "rouge_b200_w8a8_workspace_bytes": (_SZ, [_I]),
+    "rouge_b200_w8a8_linear": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "rouge_b200_set_sm_budget": (_I, [_I]),
     "rouge_b200_set_tile_mode": (_I, [_I]),
     "rouge_quantize_e4m3": (C.c_uint8, [_F]),
@@ -380,6 +382,24 @@ def gemm_i8_bcast(A, B, b_layout, out_type, scales_a, a_rows, scales_b, b_cols, 
         M, N, K, _dp(A), _dp(B), b_layout, _dp(scales_a), a_rows, _dp(scales_b), b_cols,
         C.c_void_p(mc_ptr) if mc_ptr else None, peers, 0 if mc_ptr else len(peer_ptrs), ldc,
         col_off, out_type, _stream()))
+
+
+def w8a8_workspace(M, device):
+    """Zeroed workspace of rouge_b200_w8a8_linear for M rows (every call
+    leaves it zeroed)."""
+    import torch
+    n = lib().rouge_b200_w8a8_workspace_bytes(M)
+    return torch.zeros((n + 3) // 4, dtype=torch.int32, device=device)
+
+
+def w8a8_linear(X, Wq, sw, Aq, sa, C_, out_type, ws):
+    """Aq, sa = per-row int8 quantization of X[M][K]; C = dequant(Aq . Wq^T)
+    with Wq[N][K] codes and sw[N] scales (one fused launch when it applies)."""
+    M, K = X.shape
+    N = Wq.shape[0]
+    _check("rouge_b200_w8a8_linear", lib().rouge_b200_w8a8_linear(
+        M, N, K, _dp(X), _dp(Wq), _dp(sw), _dp(Aq), _dp(sa), _dp(C_), C_.stride(0), out_type,
+        _dp(ws), _stream()))
 
 
 def gemm_e4m3(A, B, b_layout, C_, out_type, scale_a=None, scale_b=None):
