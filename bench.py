@@ -107,6 +107,9 @@ class ClockSampler:
 
 M = N = K = 4096
 SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
+# DRAM bytes (read + write) of one fused launch: dram__bytes_read.sum +
+# dram__bytes_write.sum of an ncu --set full capture of this workload
+FUSED_TRAFFIC = 118.9e6
 
 
 def make_inputs(rb):
@@ -153,10 +156,15 @@ def run_ours(args, rank, world, local_rank):
     for j in range(SETS):
         sets.append({"x": Xh.to(dev), "qx": torch.empty((M, K), dtype=torch.int8, device=dev),
                      "sx": torch.empty(M, dtype=torch.float32, device=dev),
-                     "qw": qw0.clone(), "c": torch.empty((M, N), dtype=torch.float32, device=dev)})
+                     "qw": qw0.clone(), "c": torch.empty((M, N), dtype=torch.float32, device=dev),
+                     "ws": rb.w8a8_workspace(M, dev)})
     del qw0
     busy = torch.zeros(512 << 20, dtype=torch.uint8, device=dev)
     flush = busy
+
+    def step(s):
+        # one launch: the per-row quantizer fused into the CTA-pair GEMM
+        rb.w8a8_linear(s["x"], s["qw"], sw, s["qx"], s["sx"], s["c"], rb.OUT_F32, s["ws"])
 
     def quant(s):
         rb.quantize_i8_rows(s["x"], s["sx"], s["qx"])
@@ -171,8 +179,7 @@ def run_ours(args, rank, world, local_rank):
         busy.view(torch.int32).sum()
 
     for i in range(args.warmup):
-        quant(sets[i % SETS])
-        gemm(sets[i % SETS])
+        step(sets[i % SETS])
     rb.sync_status()
 
     dist = None
@@ -189,8 +196,7 @@ def run_ours(args, rank, world, local_rank):
     keep_busy()
     e0.record()
     for i in range(args.steps):
-        quant(sets[i % SETS])
-        gemm(sets[i % SETS])
+        step(sets[i % SETS])
     e1.record()
     torch.cuda.synchronize()
     if dist:
@@ -199,8 +205,12 @@ def run_ours(args, rank, world, local_rank):
     rb.sync_status()
     t_step = e0.elapsed_time(e1) / args.steps
 
-    # Per-kernel breakdown (a second run of K steps with an event between
-    # every two kernels): the quantizer's and the GEMM's own device times.
+    # The same step as two launches (quantizer, then GEMM; a second run of K
+    # steps with an event between every two kernels): each kernel's own
+    # device time, and the GEMM's roofline on its own.
+    for i in range(3):
+        quant(sets[i % SETS])
+        gemm(sets[i % SETS])
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * args.steps + 1)]
     keep_busy()
     evs[0].record()
@@ -217,7 +227,10 @@ def run_ours(args, rank, world, local_rank):
         t = torch.tensor([t_step, t_gemm, t_quant], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         t_step, t_gemm, t_quant = t.tolist()
-    last = sets[(args.steps - 1) % SETS]
+    # parity on the fused launch's own outputs
+    last = sets[0]
+    step(last)
+    rb.sync_status()
     qx, sx, qw, C = last["qx"], last["sx"], last["qw"], last["c"]
 
     ops = 2.0 * M * N * K
@@ -254,22 +267,30 @@ def run_ours(args, rank, world, local_rank):
                          "quantized W and C (160 MB per step, 640 MB in all); K steps launched "
                          "back to back between one pair of CUDA events",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc2_kernel<I8> (2-CTA pairs, 256x256 tiles)",
-                     "achieved": round(gemm_tops, 2), "peak": round(int8_peak, 1), "unit": "TOP/s",
-                     "frac": round(gemm_tops / int8_peak, 4),
+        # the step is one launch: its average duration is ms_per_step
+        "roofline": {"bound": "tensor",
+                     "kernel": "gemm_tc2_kernel<I8, fused row quantizer> (2-CTA pairs, 256x256 "
+                               "tiles; one launch per step)",
+                     "achieved": round(value / world, 2), "peak": round(int8_peak, 1),
+                     "unit": "TOP/s", "frac": round(value / world / int8_peak, 4),
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch,
-                     # ncu capture summarised in profiles/gemm_tc2_i8_w8a8_4096.md
-                     "traffic": 56.28e6, "traffic_unit": "bytes per launch (ncu)",
+                     # ncu capture summarised in profiles/
+                     "traffic": FUSED_TRAFFIC, "traffic_unit": "bytes per launch (ncu)",
                      "peak_source": f"2 x {peak_src} dense bf16 ({peaks['bf16_tflops']} TF/s); "
                                     "int8 dense rate is twice bf16 on B200",
-                     "frac_of_datasheet_4500": round(gemm_tops / 4500.0, 4)},
-        "kernels": {"gemm_ms": round(t_gemm, 5), "gemm_tops": round(gemm_tops, 2),
+                     "frac_of_datasheet_4500": round(value / world / 4500.0, 4)},
+        # the same step as two launches (rouge_b200_quantize_i8_rows, then
+        # rouge_b200_gemm_i8): each kernel's own time and roofline
+        "kernels": {"two_launch_ms": round(t_gemm + t_quant, 5),
+                    "gemm_ms": round(t_gemm, 5), "gemm_tops": round(gemm_tops, 2),
+                    "gemm_frac": round(gemm_tops / int8_peak, 4),
+                    "gemm_traffic": 56.28e6,
                     "quant_ms": round(t_quant, 5), "quant_gbs": round(quant_gbs, 1),
                     "quant_hbm_frac": round(quant_gbs / peaks["hbm_gbs"], 4)},
         "parity": parity,
         "e2e": e2e,
         "clocks": clk,
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": args.steps,
     }
     if rank == 0 and world == 1 and not args.profile:
         line["cpu_baseline"] = cpu_baseline(X, W)
