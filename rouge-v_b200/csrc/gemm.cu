@@ -583,6 +583,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // is programmatically serialised; its outputs (A, the scales) are read
   // only after this point.
   grid_dependency_wait();
+  // The next programmatically serialised launch may start its own set-up
+  // on SMs this grid leaves (its CTAs then wait for this grid to complete).
+  grid_launch_dependents();
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -1016,6 +1019,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // is programmatically serialised; its outputs (A, the scales) are read
   // only after this point.
   grid_dependency_wait();
+  // The next programmatically serialised launch may start its own set-up
+  // on SMs this grid leaves (its CTAs then wait for this grid to complete).
+  grid_launch_dependents();
 
   if constexpr (FQ) {
     // ------------------------------------------------------------ fused quantizer
