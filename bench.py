@@ -715,6 +715,46 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
                    "scale_vec::4X, 256x256 CTA-pair tiles, packed e2m1)",
         "peak": f"gemm vs 4 x {peak_src} bf16 (dense fp4 is four times bf16); quantize vs "
                 f"{peak_src} HBM (5 B/element + 1/16 B scale)"}
+    del qa, qb, sa, sb, pa, pb, ta, tb
+
+    # MXFP4: MX block quantization to e2m1 (E8M0 scale per 32), packing, and
+    # the block-scaled fp4 GEMM 8192^3 (kind::mxf4.block_scale)
+    qa = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    qb = torch.empty((nm, nm), dtype=torch.uint8, device=dev)
+    sa = torch.empty((nm, nm // 32), dtype=torch.uint8, device=dev)
+    sb = torch.empty((nm, nm // 32), dtype=torch.uint8, device=dev)
+    t_q = time_launch(torch, lambda: rb.mx_quantize(xa, rb.FMT_E2M1, qa, sa), flush)
+    rb.mx_quantize(xb, rb.FMT_E2M1, qb, sb)
+    pa = torch.empty((nm, nm // 2), dtype=torch.uint8, device=dev)
+    pb = torch.empty((nm, nm // 2), dtype=torch.uint8, device=dev)
+    rb.fp4_pack(qa, pa)
+    rb.fp4_pack(qb, pb)
+    ta = torch.empty(rb.mxfp4_scale_atoms_bytes(nm, nm), dtype=torch.uint8, device=dev)
+    tb = torch.empty_like(ta)
+    rb.mxfp4_scale_atoms(sa, nm, nm, ta)
+    rb.mxfp4_scale_atoms(sb, nm, nm, tb)
+    t_g = time_launch(torch, lambda: rb.gemm_mxfp4(pa, ta, pb, tb, cm, rb.OUT_BF16), flush)
+    rb.sync_status()
+    wq, ws = orc.mx_quantize(xs, "e2m1")
+    codes_ok = bool((qa[rows].cpu().numpy().ravel() == wq).all()
+                    and (sa[rows].cpu().numpy().ravel() == ws).all())
+    A = orc.mx_dequantize(qa[rows].cpu().numpy(), sa[rows].cpu().numpy(), "e2m1").reshape(
+        4, nm).astype(np.float64)
+    B = orc.mx_dequantize(qb.cpu().numpy(), sb.cpu().numpy(), "e2m1").reshape(nm, nm).astype(np.float64)
+    want = A @ B.T
+    got = cm[rows].float().cpu().numpy()
+    err = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    qbytes = nm * nm * (4 + 1) + nm * nm // 32
+    out["mxfp4_8192"] = {
+        "quantize_ms": round(t_q, 4), "quantize_gbs": round(qbytes / (t_q * 1e-3) / 1e9, 1),
+        "quantize_hbm_frac": round(qbytes / (t_q * 1e-3) / 1e9 / hbm, 4),
+        "gemm_ms": round(t_g, 4), "gemm_tflops": round(fl / (t_g * 1e-3) / 1e12, 1),
+        "gemm_frac": round(fl / (t_g * 1e-3) / 1e12 / tc4, 4),
+        "codes_and_scales_bit_exact_sampled_rows": codes_ok, "rel_l2_sampled_rows": err,
+        "kernels": "mx_quant_blocks_kernel<e2m1>; gemm_tc2_kernel<MXF4> (kind::mxf4.block_scale."
+                   "scale_vec::2X, 256x256 CTA-pair tiles, packed e2m1)",
+        "peak": f"gemm vs 4 x {peak_src} bf16 (dense fp4 is four times bf16); quantize vs "
+                f"{peak_src} HBM (5 B/element + 1/32 B scale)"}
     del xa, xb, qa, qb, sa, sb, pa, pb, ta, tb, cm
 
     # Rank-4 consumers at the reference benchmark's shapes (bench_ai.cpp:73-126):
