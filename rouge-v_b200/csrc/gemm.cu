@@ -1468,7 +1468,7 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
       const int u = (args.num_tiles < RB200_FQ_ROUNDS * clusters ? args.num_tiles
                                                                   : RB200_FQ_ROUNDS * clusters) - 1;
       const int t = u >= args.split_from ? args.split_from + (u - args.split_from) / args.split : u;
-      const long long rows = static_cast<long long>(t / args.num_n + 1) * 2 * kBM;
+      const long long rows = RB200_FQ_ROUNDS > 0 ? static_cast<long long>(t / args.num_n + 1) * 2 * kBM : 0;
       args.fq_rows0 = rows < args.M ? static_cast<int>(rows) : args.M;
     }
     cfg.gridDim = dim3(2 * clusters, 1, 1);
