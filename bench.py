@@ -524,9 +524,13 @@ def other_configs(rb, torch, dev, peaks, peak_src, flush):
     want = orc.gemm_f32(orc.f16_decode(a), orc.f16_decode(b), True)
     err = float(np.linalg.norm(c1.cpu().numpy() - want) / np.linalg.norm(want))
     fl = 2.0 * n1 ** 3
+    # torch's cuBLAS on the same operands, timed the same way (context only)
+    ah16, bh16 = ad.view(torch.float16), bd.view(torch.float16)
+    t_torch = time_launch(torch, lambda: torch.matmul(ah16, bh16.t()), flush)
     out["config1_f16_gemm_512"] = {
         "ms": round(t, 5), "tflops": round(fl / (t * 1e-3) / 1e12, 2),
         "frac_of_bf16_peak": round(fl / (t * 1e-3) / 1e12 / tc16, 4), "rel_l2_vs_oracle": err,
+        "torch_matmul_ms": round(t_torch, 5),
         "note": "16 output tiles for 148 SMs: latency-bound by construction"}
 
     # config 3: fp8 e4m3 path, A, B [8192][8192] f32 ~ N(0,1); B in the
