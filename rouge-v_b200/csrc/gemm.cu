@@ -934,19 +934,67 @@ __device__ __forceinline__ int fq_claim(const GemmArgs &args, int lane) {
   return __shfl_sync(0xffffffffu, r, 0);
 }
 
-// One claimed row, loaded straight into registers (streaming loads: no
-// shared memory and no TMA queue, which the tiles' loads keep busy).
+// One claimed row, loaded straight into registers (no shared memory and
+// no TMA queue, which the tiles' loads keep busy) in two passes of half a
+// row per lane each: the maximum (loads kept in L2), then the codes from a
+// second read of the row. Half the registers of a whole row in flight,
+// which the epilogue warps that run this between tiles need.
 __device__ __forceinline__ void fq_row_direct(const GemmArgs &args, int r, int lane) {
-  constexpr int kVpl = 32;
+  constexpr int kHalf = 16;  // float4 per lane per pass: rows up to 4096 elements
   const int nvec = args.K >> 2;
   const float4 *xr = reinterpret_cast<const float4 *>(args.fq_x + static_cast<size_t>(r) * args.K);
-  float4 v[kVpl];
+  float amax = 0.0f;
 #pragma unroll
-  for (int j = 0; j < kVpl; ++j) {
-    const int i = j * 32 + lane;
-    v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int h = 0; h < 2; ++h) {
+    float4 v[kHalf];
+#pragma unroll
+    for (int j = 0; j < kHalf; ++j) {
+      const int i = (h * kHalf + j) * 32 + lane;
+      v[j] = i < nvec ? __ldcg(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int j = 0; j < kHalf; ++j)
+      amax = max3(amax, max3(fabsf(v[j].x), fabsf(v[j].y), fabsf(v[j].z)), fabsf(v[j].w));
   }
-  fq_encode_row(args, r, v, nvec, lane);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  // quant_int8.cpp:82-84: scale and reciprocal in double
+  const double a = static_cast<double>(amax);
+  const float sc = a > 0.0 ? __double2float_rn(__ddiv_rn(a, 127.0)) : 1.0f;
+  const double inv = __ddiv_rn(1.0, static_cast<double>(sc));
+  const float inv_f = __double2float_rn(inv);
+  const bool exact_row = isinf(inv_f);
+  if (lane == 0) args.fq_scales[r] = sc;
+  uint32_t *orow = reinterpret_cast<uint32_t *>(args.fq_codes + static_cast<size_t>(r) * args.K);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float4 v[kHalf];
+#pragma unroll
+    for (int j = 0; j < kHalf; ++j) {
+      const int i = (h * kHalf + j) * 32 + lane;
+      v[j] = i < nvec ? __ldcs(xr + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    uint32_t redo = 0;
+#pragma unroll
+    for (int j = 0; j < kHalf; ++j) {
+      const int i = (h * kHalf + j) * 32 + lane;
+      bool tie;
+      const uint32_t w = encode4_i8_fast(v[j], inv_f, tie);
+      tie |= exact_row;
+      if (i < nvec && !tie) orow[i] = w;
+      redo |= (tie && i < nvec) ? (1u << j) : 0u;
+    }
+    while (redo) {
+      const int j = __ffs(redo) - 1;
+      redo &= redo - 1;
+      const int i = (h * kHalf + j) * 32 + lane;
+      orow[i] = encode4_i8_exact(__ldg(xr + i), inv);
+    }
+  }
+  // codes and scale before the count, also for the TMA loads that read them
+  fence_async_global();
+  __syncwarp();
+  if (lane == 0) red_release_add(args.fq_cnt + (r >> 7), 1u);
 }
 
 __device__ __forceinline__ void report_pair(int *err, volatile int *abort, uint32_t peer_abort) {
@@ -1026,17 +1074,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if constexpr (FQ) {
     // ------------------------------------------------------------ fused quantizer
     // Every warp quantizes its rows of the first round's A blocks through a
-    // row slot of stage memory (warps 2-3: their own slots); the 10 warps
-    // that own stage memory then meet on named barrier 1 before the first
-    // TMA load into it. Warps 2-3 go on with the remaining rows meanwhile.
+    // row slot of stage memory (warps 2-3: their own slots); the producer
+    // waits on named barrier 1 until the other nine warps that own stage
+    // memory have arrived on it, before its first TMA load into it. Warps
+    // 2-3 go on with the remaining rows meanwhile.
     const bool qwarp = warp == 2 || warp == 3;
     uint8_t *slot = qwarp ? smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES + (warp - 2) * C::QSLOT
                           : smem + (warp < 2 ? warp : warp - 2) * C::QSLOT;
     fq_rows_first(args, slot, &qbar[warp], warp, lane);
     if (qwarp) {
       for (int r = fq_claim(args, lane); r < args.M; r = fq_claim(args, lane)) fq_row_direct(args, r, lane);
+    } else if (warp == 0) {
+      asm volatile("bar.sync 1, 320;" ::: "memory");  // the producer: every stage slot is free
     } else {
-      asm volatile("bar.sync 1, 320;" ::: "memory");
+      asm volatile("bar.arrive 1, 320;" ::: "memory");
     }
   }
 
