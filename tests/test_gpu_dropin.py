@@ -115,16 +115,19 @@ def test_quantize_i8_channel_banded(rb, orc, cuda, rows, cols):
     assert (s.view(np.uint32) == os_.view(np.uint32)).all()
 
 
-@pytest.mark.parametrize("M,N,K,a_rows", [(1000, 2048, 1024, 1), (1100, 2000, 1000, 0)])
-def test_gemm_i8_banded(rb, orc, cuda, M, N, K, a_rows):
+# Ragged last bands, per-row and single scales on either side; the last
+# case is below the banding threshold.
+@pytest.mark.parametrize("M,N,K,a_rows,b_cols", [(1000, 2048, 1024, 1, 1), (1100, 2000, 1000, 0, 1),
+                                                 (1300, 1700, 528, 1, 0), (700, 600, 256, 1, 1)])
+def test_gemm_i8_banded(rb, orc, cuda, M, N, K, a_rows, b_cols):
     rng = np.random.default_rng(M + N + K)
     A = rng.integers(-127, 128, (M, K), dtype=np.int8)
     B = rng.integers(-127, 128, (K, N), dtype=np.int8)   # [K][N], as rouge_gemm_i8 takes it
     sa = rng.uniform(1e-3, 2e-2, M if a_rows else 1).astype(np.float32)
-    sb = rng.uniform(1e-3, 2e-2, N).astype(np.float32)
-    C = rb.host_gemm_i8(A, B, sa, a_rows, sb, 1)
+    sb = rng.uniform(1e-3, 2e-2, N if b_cols else 1).astype(np.float32)
+    C = rb.host_gemm_i8(A, B, sa, a_rows, sb, b_cols)
     rows = _band_rows(M, 256)
-    _, oc = orc.gemm_i8(A, B, False, sa, a_rows, sb, 1, rows=rows)
+    _, oc = orc.gemm_i8(A, B, False, sa, a_rows, sb, b_cols, rows=rows)
     assert (C[rows].view(np.uint32) == oc.view(np.uint32)).all()
 
 
