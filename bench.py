@@ -109,7 +109,7 @@ M = N = K = 4096
 SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
 # DRAM bytes (read + write) of one fused launch: dram__bytes_read.sum +
 # dram__bytes_write.sum of an ncu --set full capture of this workload
-FUSED_TRAFFIC = 118.9e6
+FUSED_TRAFFIC = 116.7e6
 
 
 def make_inputs(rb):
