@@ -66,6 +66,21 @@ def test_invalid_arguments_are_refused(rb):
     assert (out == 7).all()
 
 
+def test_fused_step_host_checks(rb):
+    L = rb.lib()
+    # one count per 128-row block, a finished-CTA count and the row counter
+    assert L.rouge_b200_w8a8_workspace_bytes(4096) == (32 + 2) * 4
+    assert L.rouge_b200_w8a8_workspace_bytes(1000) == (8 + 2) * 4
+    assert L.rouge_b200_w8a8_workspace_bytes(0) == 0
+    # refused before any device work: no workspace / no input
+    assert L.rouge_b200_w8a8_linear(256, 256, 64, None, None, None, None, None, None, 256, 0,
+                                    None, None) == rb.EINVAL
+    # the wait-limit check refuses limits outside 1 ms .. 2 s (or reports no device)
+    st = L.rouge_b200_check_wait_limit(10, None)
+    assert st in (rb.EINVAL, rb.ENODEV)
+    L.rouge_b200_clear_error()
+
+
 def test_tile_mode_switch(rb):
     L = rb.lib()
     assert L.rouge_b200_set_tile_mode(7) == rb.EINVAL          # unknown: nothing changed
