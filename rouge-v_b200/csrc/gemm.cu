@@ -814,6 +814,10 @@ struct Cfg2 {
                 "MX tile");
 };
 
+// Rows of the fused quantizer claimed while the tiles run get an L2
+// prefetch this many rows ahead of the row claimed.
+constexpr int kFqAhead = 512;
+
 // Scale and codes of one row held in registers (v[j] = float4 j * 32 +
 // lane of the row; nvec float4 in all) as quant_int8.cpp:72-90 computes
 // them: scale and reciprocal in double, branch-free single-precision codes,
@@ -910,7 +914,7 @@ __device__ __forceinline__ void fq_rows_first(const GemmArgs &args, uint8_t *slo
   if (in_flight && lane == 0) mbar_wait(bar, phase, &never);  // let the last copy land
   // L2 prefetch of the first rows the running tiles' quantizer will claim
   const int pf = args.fq_rows0 + static_cast<int>(blockIdx.x) * 12 + warp;
-  if (lane == 0 && pf < args.M && pf < args.fq_rows0 + 512)
+  if (lane == 0 && pf < args.M && pf < args.fq_rows0 + kFqAhead)
     bulk_prefetch_l2(args.fq_x + static_cast<size_t>(pf) * args.K, row_bytes);
 }
 
@@ -920,8 +924,6 @@ __device__ __forceinline__ void fq_rows_first(const GemmArgs &args, uint8_t *slo
 // claimed row (>= M: none left) and starts an L2 prefetch of the row
 // kFqAhead places further on, which the warps claim a few microseconds
 // later; the first kFqAhead rows are prefetched by fq_rows_first.
-constexpr int kFqAhead = 512;
-
 __device__ __forceinline__ int fq_claim(const GemmArgs &args, int lane) {
   const int nblk = (args.M + kBM - 1) / kBM;
   int r = 0;
