@@ -1076,6 +1076,41 @@ def run_reference(args, rank, world):
     }
 
 
+# ------------------------------------------------------------------ ncu drivers
+
+def profile_kernel(name):
+    """Runs one kernel of another configuration three times on cuda:0 and
+    exits (the short command lines the ncu captures of those kernels use):
+      conv4  rouge_b200_conv2d_nhwc_f16 on the config-4 shape
+      mxfp8  MXFP8 quantization of a 4096^2 operand and gemm_mx 4096^3."""
+    import torch
+    import rouge_b200 as rb
+    dev = torch.device("cuda", 0)
+    if name == "conv4":
+        n, h, w, ci, co = 32, 56, 56, 256, 256
+        x = torch.randn((n, h, w, ci), device=dev).half()
+        wt = (torch.randn((co, 3, 3, ci), device=dev) * 0.03).half()
+        b = torch.zeros(co, device=dev)
+        y = torch.empty((n, h, w, co), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            rb.conv2d_nhwc_f16(x.view(torch.int16), wt.view(torch.int16), b, y, 1, 1)
+    else:
+        n = 4096
+        x = torch.randn((n, n), device=dev)
+        q = torch.empty((n, n), dtype=torch.uint8, device=dev)
+        sc = torch.empty((n, n // 32), dtype=torch.uint8, device=dev)
+        for _ in range(3):
+            rb.mx_quantize(x, rb.FMT_E4M3, q, sc)
+        at = torch.empty(rb.mx_scale_atoms_bytes(n, n), dtype=torch.uint8, device=dev)
+        rb.mx_scale_atoms(sc, n, n, at)
+        c = torch.empty((n, n), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            rb.gemm_mx(q, rb.FMT_E4M3, at, q, rb.FMT_E4M3, at, c, rb.OUT_F32)
+    torch.cuda.synchronize()
+    rb.sync_status()
+    print(json.dumps({"profile_kernel": name, "status": "ok"}), flush=True)
+
+
 # ------------------------------------------------------------------ main
 
 def main():
@@ -1086,7 +1121,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--profile", action="store_true",
                     help="time the kernels only (no e2e / parity / CPU baseline), for ncu")
+    ap.add_argument("--profile-kernel", default=None, choices=["conv4", "mxfp8"],
+                    help="run only this kernel three times and exit (ncu captures)")
     args = ap.parse_args()
+    if args.profile_kernel:
+        profile_kernel(args.profile_kernel)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
