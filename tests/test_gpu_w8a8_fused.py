@@ -69,7 +69,8 @@ def _weights(rb, torch, rng, N, K, cuda):
 
 @pytest.mark.parametrize("M,N,K,pair", [(4096, 4096, 4096, False), (1000, 1000, 1024, True),
                                         (384, 512, 48, True), (260, 256, 4096, True),
-                                        (128, 4096, 256, True)])
+                                        (128, 4096, 256, True), (1, 272, 16, True),
+                                        (129, 300, 2064, True), (8192, 2048, 1024, False)])
 def test_fused_equals_two_calls(rb, orc, cuda, M, N, K, pair):
     import torch
     rng = np.random.default_rng(M * 7 + N + K)
@@ -86,6 +87,7 @@ def test_fused_equals_two_calls(rb, orc, cuda, M, N, K, pair):
             assert int(ws.abs().sum()) == 0          # the workspace is left zeroed
     # sampled rows against the oracle itself
     rows = np.unique(np.r_[0:6, rng.integers(0, M, 10)])
+    rows = rows[rows < M]
     x = xd.cpu().numpy()
     oq, os_ = orc.quantize_i8_rows(x[rows])
     aq, sa, c = got[0], got[1], None
