@@ -283,7 +283,16 @@ int attention_device(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q, co
       softmax_split_kernel<<<grid_of(static_cast<size_t>(m) * 32), kThreads, 0, st>>>(
           Sc, a.Kp, m, sb, s0, Skv, a.Kp, causal, window, kv_off, Pp);
       s = cuda_status(cudaGetLastError());
-      for (int g = 0; s == ROUGE_B200_OK && g < a.group; ++g) {
+      if (sb == S) {
+        // the whole sequence in one block: the group's heads are consecutive
+        // [S][Dh] blocks of O, so their P.V products are one GEMM of
+        // group * S rows
+        s = launch_gemm_blas(3, m, Dh, 3 * a.Kp, Pp, 3 * a.Kp,
+                             Vt + static_cast<size_t>(hk) * Dh * 3 * a.Kp, 3 * a.Kp,
+                             ROUGE_B200_B_NK, 1.0f, 0.0f,
+                             O + static_cast<size_t>(hk) * a.group * S * Dh, Dh, st);
+      }
+      for (int g = 0; s == ROUGE_B200_OK && sb != S && g < a.group; ++g) {
         const int hq = hk * a.group + g;
         s = launch_gemm_blas(3, sb, Dh, 3 * a.Kp, Pp + static_cast<size_t>(g) * sb * 3 * a.Kp,
                              3 * a.Kp, Vt + static_cast<size_t>(hk) * Dh * 3 * a.Kp, 3 * a.Kp,
