@@ -42,6 +42,9 @@ namespace rb200 {
 int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
                      long long ldb, int b_layout, float alpha, float beta, float *Cp,
                      long long ldc, cudaStream_t st);
+int launch_gemm_blas_batched(int kind, int M, int N, int K, const void *A, long long lda,
+                             const void *B, long long ldb, float alpha, float beta, float *Cp,
+                             long long ldc, int batch, cudaStream_t st);
 
 namespace {
 
@@ -212,6 +215,9 @@ struct Arena {
 
 struct AttnPlan {
   int Dp, Kp, group, sb;
+  // all K/V head groups at once: the sequence is one block and a group's
+  // rows (group * S) a multiple of 256, so each GEMM is one batched launch
+  bool all_groups;
   size_t bytes;
 };
 
@@ -224,7 +230,9 @@ AttnPlan attn_plan(int S, int Skv, int Dh, int Hq, int Hkv, bool fp8) {
   size_t sb = kScoreBudget / (per_row * a.group);
   if (sb < 16) sb = 16;
   a.sb = static_cast<int>(sb < static_cast<size_t>(S) ? sb : S);
-  const size_t rows = static_cast<size_t>(a.group) * a.sb;
+  a.all_groups = a.sb == S && (static_cast<size_t>(a.group) * S) % 256 == 0 && Hkv > 1 &&
+                 static_cast<size_t>(Hkv) * a.group * S * per_row <= kScoreBudget;
+  const size_t rows = static_cast<size_t>(a.group) * a.sb * (a.all_groups ? Hkv : 1);
   a.bytes = rup(static_cast<size_t>(Hkv) * Skv * 3 * a.Dp * 4, 256) +        // K'
             rup(static_cast<size_t>(Hkv) * Dh * 3 * a.Kp * 4, 256) +         // V'^T
             rup(rows * 3 * a.Dp * 4, 256) + rup(rows * a.Kp * 4, 256) +     // Q', S
@@ -243,7 +251,7 @@ int attention_device(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q, co
   const AttnPlan a = attn_plan(S, Skv, Dh, Hq, Hkv, fp8);
   if (ws_bytes < a.bytes) return set_status(ROUGE_B200_ETOOBIG);
   Arena ar(ws, ws_bytes);
-  const size_t rows = static_cast<size_t>(a.group) * a.sb;
+  const size_t rows = static_cast<size_t>(a.group) * a.sb * (a.all_groups ? Hkv : 1);
   uint32_t *Kp_ = ar.take<uint32_t>(static_cast<size_t>(Hkv) * Skv * 3 * a.Dp);
   uint32_t *Vt = ar.take<uint32_t>(static_cast<size_t>(Hkv) * Dh * 3 * a.Kp);
   uint32_t *Qp = ar.take<uint32_t>(rows * 3 * a.Dp);
@@ -267,6 +275,28 @@ int attention_device(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q, co
   if (s == ROUGE_B200_OK)
     s = pack_launch<uint32_t>(V, static_cast<long long>(Skv) * Dh, 1, Dh, Dh, Skv, a.Kp, 2, Vt,
                               static_cast<long long>(Dh) * 3 * a.Kp, 3 * a.Kp, Hkv, st);
+  if (a.all_groups) {
+    // Every head at once: Q' of all Hq heads ([hk][g][s] rows), the scores
+    // of every group as one batched GEMM (item hk: its group's rows times
+    // K' of head hk), one softmax pass, and P.V batched the same way; O's
+    // [Hq][S][Dh] rows are the same [hk][g][s] order.
+    const int m = a.group * S;
+    if (s == ROUGE_B200_OK)
+      s = pack_launch<uint32_t>(Q, static_cast<long long>(S) * Dh, Dh, 1, S, Dh, a.Dp, 1, Qp,
+                                static_cast<long long>(S) * 3 * a.Dp, 3 * a.Dp, Hq, st);
+    if (s == ROUGE_B200_OK)
+      s = launch_gemm_blas_batched(3, m, Skv, 3 * a.Dp, Qp, 3 * a.Dp, Kp_, 3 * a.Dp, scale, 0.0f,
+                                   Sc, a.Kp, Hkv, st);
+    if (s == ROUGE_B200_OK) {
+      softmax_split_kernel<<<grid_of(static_cast<size_t>(m) * Hkv * 32), kThreads, 0, st>>>(
+          Sc, a.Kp, m * Hkv, S, 0, Skv, a.Kp, causal, window, kv_off, Pp);
+      s = cuda_status(cudaGetLastError());
+    }
+    if (s == ROUGE_B200_OK)
+      s = launch_gemm_blas_batched(3, m, Dh, 3 * a.Kp, Pp, 3 * a.Kp, Vt, 3 * a.Kp, 1.0f, 0.0f, O,
+                                   Dh, Hkv, st);
+    return s == ROUGE_B200_OK ? s : set_status(s);
+  }
   for (int hk = 0; s == ROUGE_B200_OK && hk < Hkv; ++hk) {
     for (int s0 = 0; s == ROUGE_B200_OK && s0 < S; s0 += a.sb) {
       const int sb = S - s0 < a.sb ? S - s0 : a.sb;

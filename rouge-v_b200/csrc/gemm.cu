@@ -104,6 +104,11 @@ struct GemmArgs {
   // units walk N first (m-block = tile / num_n), so that the first round
   // needs few blocks of A rows
   int n_fast;
+  // Batched GEMM with K-major B (item_m > 0): M / item_m items stacked by
+  // rows; item i multiplies A rows [i*item_m, +item_m) by B rows
+  // [i*N, +N) into C rows [i*item_m, +item_m). item_m is a multiple of
+  // 256, so no tile spans two items.
+  int item_m;
 };
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
@@ -615,7 +620,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tma_load_2d(sA + s * C::A_BYTES, &tmA, &full[s], kx, mb * kBM);
         }
         if constexpr (!B_MN) {
-          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kx, nb * BN);
+          tma_load_2d(sB + s * C::B_BYTES, &tmB, &full[s], kx,
+                      nb * BN + (args.item_m ? (mb * kBM / args.item_m) * args.N : 0));
         } else {
 #pragma unroll
           for (int j = 0; j < C::B_CHUNKS; ++j)
@@ -1149,7 +1155,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              ((nb * BN / 128 + j) * args.sf_kblocks + kb) * kRows);
         }
         if constexpr (!B_MN) {
-          tma_load_2d_pair(sB + s * C::B_BYTES, tb, bar, kx, n0);
+          tma_load_2d_pair(sB + s * C::B_BYTES, tb, bar, kx,
+                           n0 + (args.item_m ? (m0 / args.item_m) * args.N : 0));
         } else {  // (no split units with MN-major B)
 #pragma unroll
           for (int j = 0; j < C::B_CHUNKS; ++j)
@@ -1541,9 +1548,10 @@ int launch_gemm_impl(const void *A, long long lda, const void *B, long long ldb,
                        kBM);
   if (s != ROUGE_B200_OK) return s;
   auto make_b = [&](int box_rows, CUtensorMap *tb) {
-    if (!B_MN)  // K-major: boxes of box_rows rows of B
-      return make_tmap_2d(tb, B, dt, args.K, args.N, static_cast<uint64_t>(ldb) * C::ESIZE, C::BK,
-                          box_rows);
+    if (!B_MN)  // K-major: boxes of box_rows rows of B (every item's rows when batched)
+      return make_tmap_2d(tb, B, dt, args.K,
+                          static_cast<uint64_t>(args.N) * (args.item_m ? args.M / args.item_m : 1),
+                          static_cast<uint64_t>(ldb) * C::ESIZE, C::BK, box_rows);
     return make_tmap_2d(tb, B, dt, args.N, args.K, static_cast<uint64_t>(ldb) * C::ESIZE,
                         kBKBytes / C::ESIZE, C::BK);
   };
@@ -1905,6 +1913,28 @@ int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda
     default:
       return set_status(ROUGE_B200_EINVAL);
   }
+}
+
+// launch_gemm_blas over `batch` items stacked by rows (K-major B only):
+// item i computes C[i*M + m][n] = alpha * sum_k A[i*M + m][k] B[i*N + n][k]
+// (+ beta * C). M must be a multiple of 256 when batch > 1.
+int launch_gemm_blas_batched(int kind, int M, int N, int K, const void *A, long long lda,
+                             const void *B, long long ldb, float alpha, float beta, float *Cp,
+                             long long ldc, int batch, cudaStream_t st) {
+  if (batch <= 1)
+    return launch_gemm_blas(kind, M, N, K, A, lda, B, ldb, ROUGE_B200_B_NK, alpha, beta, Cp, ldc,
+                            st);
+  if (M % 256 != 0 || kind != 3) return set_status(ROUGE_B200_EUNSUPPORTED);
+  GemmArgs g{};
+  g.M = M * batch; g.N = N; g.K = K;
+  g.item_m = M;
+  g.C = Cp; g.ldc = ldc;
+  g.blas = 1;
+  g.alpha = alpha;
+  g.beta = beta;
+  g.use_tma_store = vec_ok(Cp, ldc, ROUGE_B200_OUT_F32);
+  g.err = device_error_word();
+  return launch_kind<MmaKind::TF32>(A, lda, B, ldb, ROUGE_B200_B_NK, g, ROUGE_B200_OUT_F32, st);
 }
 
 // Block-scaled (MXFP8) GEMM on CTA pairs with 256 x 256 tiles:
