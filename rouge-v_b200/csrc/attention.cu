@@ -139,8 +139,8 @@ __device__ __forceinline__ void rope_pair(float &x0, float &x1, int i, int n, in
 }
 
 // flat [S][H * Dq] -> [H][S][Dq], RoPE at position s when rope != 0.
-__global__ void relayout_rope_kernel(const float *__restrict__ flat, int S, int H, int Dq, int rope,
-                                     float theta, float *__restrict__ out) {
+__global__ void relayout_rope_kernel(const float *__restrict__ flat, long long ld, int S, int H,
+                                     int Dq, int rope, float theta, float *__restrict__ out) {
   const int half = Dq / 2;
   if (half == 0) rope = 0;  // (no pair to rotate: a plain relayout)
   const size_t pairs = static_cast<size_t>(S) * H * (rope ? half : Dq);
@@ -150,7 +150,7 @@ __global__ void relayout_rope_kernel(const float *__restrict__ flat, int S, int 
       const int j = static_cast<int>(i % half);
       const size_t hs = i / half;
       const int h = static_cast<int>(hs % H), s = static_cast<int>(hs / H);
-      const float *src = flat + (static_cast<size_t>(s) * H + h) * Dq;
+      const float *src = flat + static_cast<size_t>(s) * ld + static_cast<size_t>(h) * Dq;
       float x0 = src[j], x1 = src[j + half];
       rope_pair(x0, x1, j, Dq, s, theta);
       float *dst = out + (static_cast<size_t>(h) * S + s) * Dq;
@@ -161,7 +161,8 @@ __global__ void relayout_rope_kernel(const float *__restrict__ flat, int S, int 
       const int d = static_cast<int>(i % Dq);
       const size_t hs = i / Dq;
       const int h = static_cast<int>(hs % H), s = static_cast<int>(hs / H);
-      out[(static_cast<size_t>(h) * S + s) * Dq + d] = flat[(static_cast<size_t>(s) * H + h) * Dq + d];
+      out[(static_cast<size_t>(h) * S + s) * Dq + d] =
+          flat[static_cast<size_t>(s) * ld + static_cast<size_t>(h) * Dq + d];
     }
   }
 }
@@ -185,6 +186,19 @@ __global__ void swiglu_kernel(float *__restrict__ gate, const float *__restrict_
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const float g = gate[i];
     gate[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), up[i]);
+  }
+}
+
+// SwiGLU on the side-by-side gate | up projections gu[S][2*Dff]: the gate
+// half of each row becomes silu(gate) * up, as swiglu_kernel computes it.
+__global__ void swiglu_rows_kernel(float *__restrict__ gu, int S, int Dff) {
+  const size_t n = static_cast<size_t>(S) * Dff;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / Dff, j = i - r * Dff;
+    float *row = gu + r * 2 * Dff;
+    const float g = row[j];
+    row[j] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), row[Dff + j]);
   }
 }
 
@@ -337,9 +351,31 @@ int attention_device(int S, int Skv, int Dh, int Hq, int Hkv, const float *Q, co
 // Row-major C[M][N] (pitch ldc) = A[M][K] . W[K][N] + beta * C, f32 through
 // the column-major 3xTF32 GEMM (C^T = W^T A^T with no transposes).
 int rowmajor_gemm(int M, int N, int K, const float *A, const float *W, float beta, float *C,
-                  void *ws, size_t ws_bytes, cudaStream_t st) {
-  return rouge_b200_gemm_colmajor(0, 0, N, M, K, ROUGE_B200_T_F32, 1.0f, W, N, A, K, beta, C,
-                                  ROUGE_B200_T_F32, N, ws, ws_bytes, st);
+                  void *ws, size_t ws_bytes, cudaStream_t st, int lda = 0) {
+  return rouge_b200_gemm_colmajor(0, 0, N, M, K, ROUGE_B200_T_F32, 1.0f, W, N, A, lda ? lda : K,
+                                  beta, C, ROUGE_B200_T_F32, N, ws, ws_bytes, st);
+}
+
+// Row-major C[M][sum Nw] = A[M][K] . [W_0 | W_1 | ...] for weights W_j
+// [K][Nw_j] (the reference's [in][out]) placed side by side: A packed once,
+// each weight packed into its rows of one B' operand, one GEMM -- the
+// operands and workspace layout of rowmajor_gemm's (A' then B').
+int rowmajor_gemm_cat(int M, int K, const float *A, int nw, const float *const *W, const int *Nw,
+                      float *C, void *ws, size_t ws_bytes, cudaStream_t st) {
+  const int Kp = static_cast<int>(rup(K, 32));
+  int Nt = 0;
+  for (int j = 0; j < nw; ++j) Nt += Nw[j];
+  const size_t a_bytes = rup(static_cast<size_t>(M) * 3 * Kp * 4, 256);
+  if (ws_bytes < a_bytes + static_cast<size_t>(Nt) * 3 * Kp * 4) return set_status(ROUGE_B200_ETOOBIG);
+  uint32_t *Ap = static_cast<uint32_t *>(ws);
+  uint32_t *Bp = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) + a_bytes);
+  int s = pack_launch<uint32_t>(A, 0, K, 1, M, K, Kp, 1, Ap, 0, 3 * Kp, 1, st);
+  for (int j = 0, off = 0; s == ROUGE_B200_OK && j < nw; off += Nw[j], ++j)
+    s = pack_launch<uint32_t>(W[j], 0, 1, Nw[j], Nw[j], K, Kp, 2,
+                              Bp + static_cast<size_t>(off) * 3 * Kp, 0, 3 * Kp, 1, st);
+  if (s != ROUGE_B200_OK) return s;
+  return launch_gemm_blas(3, M, Nt, 3 * Kp, Ap, 3 * Kp, Bp, 3 * Kp, ROUGE_B200_B_NK, 1.0f, 0.0f,
+                          C, Nt, st);
 }
 
 }  // namespace
@@ -516,8 +552,8 @@ size_t rouge_b200_transformer_block_workspace(int S, int D, int Hq, int Hkv, int
   const size_t skv = rup(static_cast<size_t>(S) * Hkv * Dq * 4, 256);
   const size_t sf = rup(static_cast<size_t>(S) * Dff * 4, 256);
   size_t g = 0;
-  const int shapes[6][3] = {{Hq * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
-                            {Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
+  const int shapes[6][3] = {{(Hq + 2 * Hkv) * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
+                            {2 * Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
   for (auto &sh : shapes) {
     const size_t w = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, sh[0], sh[1], sh[2]);
     if (w > g) g = w;
@@ -544,14 +580,15 @@ int rouge_b200_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, 
   const size_t nsd = static_cast<size_t>(S) * D, nq = static_cast<size_t>(S) * Hq * Dq;
   const size_t nkv = static_cast<size_t>(S) * Hkv * Dq, nf = static_cast<size_t>(S) * Dff;
   float *norm = ar.take<float>(nsd), *h1 = ar.take<float>(nsd), *norm2 = ar.take<float>(nsd);
-  float *qflat = ar.take<float>(nq), *q = ar.take<float>(nq), *attn = ar.take<float>(nq),
+  // qkv [S][(Hq + 2 Hkv) Dq]: the q | k | v projections side by side;
+  // gu [S][2 Dff]: gate | up
+  float *qkv = ar.take<float>(nq + 2 * nkv), *q = ar.take<float>(nq), *attn = ar.take<float>(nq),
         *attnflat = ar.take<float>(nq);
-  float *kflat = ar.take<float>(nkv), *vflat = ar.take<float>(nkv), *k = ar.take<float>(nkv),
-        *v = ar.take<float>(nkv);
-  float *gate = ar.take<float>(nf), *up = ar.take<float>(nf);
+  float *k = ar.take<float>(nkv), *v = ar.take<float>(nkv);
+  float *gu = ar.take<float>(2 * nf);
   size_t gws = 0;
-  const int shapes[6][3] = {{Hq * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
-                            {Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
+  const int shapes[6][3] = {{(Hq + 2 * Hkv) * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
+                            {2 * Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
   for (auto &sh : shapes) {
     const size_t w = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, sh[0], sh[1], sh[2]);
     if (w > gws) gws = w;
@@ -563,14 +600,19 @@ int rouge_b200_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, 
   // 1-2: RMSNorm, projections
   rmsnorm_kernel<<<rows_grid, kThreads, 0, st>>>(x, S, D, wrms1, rms_eps, norm);
   s = cuda_status(cudaGetLastError());
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, Hq * Dq, D, norm, wq, 0.0f, qflat, gw, gws, st);
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, Hkv * Dq, D, norm, wk, 0.0f, kflat, gw, gws, st);
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, Hkv * Dq, D, norm, wv, 0.0f, vflat, gw, gws, st);
+  const long long ldqkv = static_cast<long long>(Hq + 2 * Hkv) * Dq;
+  if (s == ROUGE_B200_OK) {
+    const float *wqkv[3] = {wq, wk, wv};
+    const int nqkv[3] = {Hq * Dq, Hkv * Dq, Hkv * Dq};
+    s = rowmajor_gemm_cat(S, D, norm, 3, wqkv, nqkv, qkv, gw, gws, st);
+  }
   // 3: [S][H*Dq] -> [H][S][Dq], RoPE on q and k (positions 0..S-1)
   if (s == ROUGE_B200_OK) {
-    relayout_rope_kernel<<<grid_of(nq), kThreads, 0, st>>>(qflat, S, Hq, Dq, 1, rope_theta, q);
-    relayout_rope_kernel<<<grid_of(nkv), kThreads, 0, st>>>(kflat, S, Hkv, Dq, 1, rope_theta, k);
-    relayout_rope_kernel<<<grid_of(nkv), kThreads, 0, st>>>(vflat, S, Hkv, Dq, 0, rope_theta, v);
+    relayout_rope_kernel<<<grid_of(nq), kThreads, 0, st>>>(qkv, ldqkv, S, Hq, Dq, 1, rope_theta, q);
+    relayout_rope_kernel<<<grid_of(nkv), kThreads, 0, st>>>(qkv + static_cast<size_t>(Hq) * Dq, ldqkv,
+                                                            S, Hkv, Dq, 1, rope_theta, k);
+    relayout_rope_kernel<<<grid_of(nkv), kThreads, 0, st>>>(
+        qkv + static_cast<size_t>(Hq + Hkv) * Dq, ldqkv, S, Hkv, Dq, 0, rope_theta, v);
     s = cuda_status(cudaGetLastError());
   }
   // 4: causal GQA attention
@@ -589,14 +631,17 @@ int rouge_b200_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, 
     rmsnorm_kernel<<<rows_grid, kThreads, 0, st>>>(h1, S, D, wrms2, rms_eps, norm2);
     s = cuda_status(cudaGetLastError());
   }
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, Dff, D, norm2, wgate, 0.0f, gate, gw, gws, st);
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, Dff, D, norm2, wup, 0.0f, up, gw, gws, st);
   if (s == ROUGE_B200_OK) {
-    swiglu_kernel<<<grid_of(nf), kThreads, 0, st>>>(gate, up, nf);
+    const float *wgu[2] = {wgate, wup};
+    const int ngu[2] = {Dff, Dff};
+    s = rowmajor_gemm_cat(S, D, norm2, 2, wgu, ngu, gu, gw, gws, st);
+  }
+  if (s == ROUGE_B200_OK) {
+    swiglu_rows_kernel<<<grid_of(nf), kThreads, 0, st>>>(gu, S, Dff);
     s = cuda_status(cudaGetLastError());
   }
   if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(out, h1, nsd * 4, cudaMemcpyDeviceToDevice, st));
-  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, D, Dff, gate, wdown, 1.0f, out, gw, gws, st);
+  if (s == ROUGE_B200_OK) s = rowmajor_gemm(S, D, Dff, gu, wdown, 1.0f, out, gw, gws, st, 2 * Dff);
   return s == ROUGE_B200_OK ? s : set_status(s);
 }
 
