@@ -73,6 +73,10 @@ def test_gqa_reference_test_shape(libs, causal, window):
     (100, 300, 64, 4, 4, 1, 0, 200),      # decode-like: a prefix of 200 cached keys
     (257, 257, 128, 4, 1, 1, 32, 0),      # MQA, sliding window
     (64, 1000, 40, 6, 3, 0, 0, 0),        # odd head size, no mask
+    # every group in one batched launch (group * S a multiple of 256) with
+    # ragged key counts: the last key tile reads the next head's rows
+    (256, 300, 64, 8, 2, 1, 0, 44),
+    (128, 200, 40, 4, 2, 0, 8, 0),
 ])
 def test_gqa_shapes(libs, S, Skv, Dh, Hq, Hkv, causal, window, kv_off):
     ours, ref = libs
