@@ -1,22 +1,32 @@
 """Benchmark of the rouge-numerics-b200 hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload w8a8|fp8|f16]
 
-Default workload (the one the headline metric is quoted
-on): W8A8 linear. X[4096][4096] f32 ~ N(0,1) with 1% of entries x20,
-W[4096][4096] f32 ~ N(0, 0.02) quantized once per output channel. One step
-= per-token int8 quantization of X + int8 x int8 -> int32 tcgen05 GEMM with
-the dequant ((float)acc * sx) * sw fused into the epilogue, f32 output.
-`value` = 2*M*N*K / step time (TOP/s), inputs resident in HBM and larger
-than L2 (four rotating device copies of the step's data), K steps launched
-back to back between one pair of CUDA events. `e2e` = the same metric through the drop-in host-pointer C
-ABI (rouge_quantize_i8_channel + rouge_gemm_i8) from pinned host buffers,
-copies included. With N > 1 every rank runs its own replica (weak scaling).
+One GPU (the configuration the headline metric is quoted
+on): the W8A8 linear step. X[4096][4096] f32 ~ N(0,1) with 1% of entries
+x20, W[4096][4096] f32 ~ N(0, 0.02) quantized once per output channel. One
+step = per-token int8 quantization of X + int8 x int8 -> int32 tcgen05 GEMM
+with the dequant ((float)acc * sx) * sw fused into the epilogue, f32 output,
+all in one launch. `value` = 2*M*N*K / step time (TOP/s), inputs resident in
+HBM and larger than L2 (four rotating device copies of the step's data), K
+steps launched back to back between one pair of CUDA events. `e2e` = the
+same metric through the drop-in host-pointer C ABI (rouge_quantize_i8_channel
++ rouge_gemm_i8) from pinned host buffers, copies included. The config-5 GEMM
+on one GPU is reported beside it (`config5_g1`).
+
+N GPUs (torchrun, one rank per GPU; BASELINE config 5, the sharded GEMM):
+M=16384, K=8192, N=28672 int8 W8A8 with W split N-wise over the N GPUs,
+bf16 output, the whole C[M][N] on every rank at the end of each step (the
+all-gather is fused into the GEMM epilogue). `value` = 2*M*N*K / step time
+of the whole job (strong scaling), max over ranks. `e2e` adds, every step,
+the copy of the int8 activations from pinned host memory and of a 1/N band
+of C's rows back to the host on every rank. N independent config-2 replicas
+are reported beside it (`config2_replicas`).
 
 --impl reference times the reference rouge-numerics CPU implementation
 (oracle/_ref, compiled from the reference sources) on this host's cores for
-the same workload and metric, on a bounded row sample per step.
+the same workload, metric and config, on a bounded row sample per step; its
+process loads only the checker libraries under oracle/.
 """
 from __future__ import annotations
 
@@ -112,10 +122,38 @@ SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
 FUSED_TRAFFIC = 116.7e6
 
 
-def make_inputs(rb):
-    X = rb.synth_normal(1, (M, K), 0.0, 1.0)
-    rb.synth_outliers(1, X, 0.01, 20.0)
-    W = rb.synth_normal(2, (N, K), 0.0, 0.02)
+M5, N5, K5 = 16384, 28672, 8192
+METRIC = "W8A8 int8 GEMM TOP/s (int8 x int8 -> int32 tcgen05 GEMM, fused dequant)"
+
+
+def workload_config(world):
+    """The `config` of the JSON line, shared by both arms (same dict)."""
+    if world == 1:
+        return {"workload": "w8a8_linear_4096 (BASELINE config 2): per-token int8 quantization "
+                            "of X + int8 GEMM + fused dequant, f32 out",
+                "M": M, "N": N, "K": K, "out": "f32",
+                "weights": "pre-quantized per output channel (setup)",
+                "l2": f"inputs larger than L2: {SETS} rotating device copies of X, codes, "
+                      "quantized W and C (160 MB per step, 640 MB in all); K steps launched "
+                      "back to back between one pair of CUDA events",
+                "parallelism": "single GPU"}
+    return {"workload": f"sharded_w8a8 (BASELINE config 5): M={M5} K={K5} N={N5} int8 "
+                        f"activations and weights, W split N-wise over {world} GPUs, int32 "
+                        "accumulation, bf16 out, C[M][N] complete on every rank",
+            "M": M5, "N": N5, "K": K5, "out": "bf16",
+            "weights": "pre-quantized per output channel (setup), each rank its column block",
+            "l2": "inputs larger than L2 (every step writes the 939.5 MB C on every rank); K "
+                  "steps launched back to back between one pair of CUDA events",
+            "parallelism": f"N-sharded x{world} over output columns, all-gather fused into the "
+                           "GEMM epilogue (NVLink)"}
+
+
+def make_inputs(gen):
+    """Config-2 inputs from `gen` (the product library's generator, or the
+    checker library's bit-identical copy in the reference arm)."""
+    X = gen.synth_normal(1, (M, K), 0.0, 1.0)
+    gen.synth_outliers(1, X, 0.01, 20.0)
+    W = gen.synth_normal(2, (N, K), 0.0, 0.02)
     return X, W
 
 
@@ -133,12 +171,14 @@ def torch_int32():
     return torch.int32
 
 
-def run_ours(args, rank, world, local_rank):
+def run_config2(args, rank, world, local_rank):
+    """BASELINE config 2 on this rank's GPU (one replica per rank): the
+    W8A8 step timed as one fused launch and as two launches, its parity on
+    sampled rows and, on request, its drop-in end-to-end number."""
     import torch
     import rouge_b200 as rb
 
     dev = torch.device("cuda", local_rank)
-    torch.cuda.set_device(dev)
     peaks, peak_src = load_peaks()
     X, W = make_inputs(rb)
     Xh = torch.from_numpy(X).pin_memory()
@@ -160,7 +200,6 @@ def run_ours(args, rank, world, local_rank):
                      "ws": rb.w8a8_workspace(M, dev)})
     del qw0
     busy = torch.zeros(512 << 20, dtype=torch.uint8, device=dev)
-    flush = busy
 
     def step(s):
         # one launch: the per-row quantizer fused into the CTA-pair GEMM
@@ -187,9 +226,10 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    time.sleep(0.3)
+    clocks = ClockSampler(local_rank) if world == 1 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
     # Timed region: K steps launched back to back, one event pair around all.
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -201,7 +241,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
-    clk = clocks.stop()
+    clk = clocks.stop() if clocks else None
     rb.sync_status()
     t_step = e0.elapsed_time(e1) / args.steps
 
@@ -223,10 +263,13 @@ def run_ours(args, rank, world, local_rank):
     rb.sync_status()
     t_quant = sum(evs[2 * i].elapsed_time(evs[2 * i + 1]) for i in range(args.steps)) / args.steps
     t_gemm = sum(evs[2 * i + 1].elapsed_time(evs[2 * i + 2]) for i in range(args.steps)) / args.steps
+    # the quantizer alone, after an L2 flush (no write-back of a previous
+    # GEMM's output in its interval)
+    t_quant_alone = time_launch(torch, lambda: quant(sets[0]), busy)
     if dist:
-        t = torch.tensor([t_step, t_gemm, t_quant], device=dev)
+        t = torch.tensor([t_step, t_gemm, t_quant, t_quant_alone], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_gemm, t_quant = t.tolist()
+        t_step, t_gemm, t_quant, t_quant_alone = t.tolist()
     # parity on the fused launch's own outputs
     last = sets[0]
     step(last)
@@ -238,35 +281,11 @@ def run_ours(args, rank, world, local_rank):
     gemm_tops = ops / (t_gemm * 1e-3) / 1e12
     quant_bytes = M * K * 5 + M * 4
     quant_gbs = quant_bytes / (t_quant * 1e-3) / 1e9
-
-    if args.profile:  # kernels only: keeps ncu captures short
-        parity, e2e = None, None
-    else:
-        # parity of this run's output against the oracle on sampled rows
-        parity = check_parity(rb, X, qx, sx, qw, sw, C)
-        # e2e through the drop-in C ABI from pinned host buffers
-        e2e = run_e2e(args, rb, torch, Xh, qw, sw, dev, dist)
-
+    quant_alone_gbs = quant_bytes / (t_quant_alone * 1e-3) / 1e9
     int8_peak = 2.0 * peaks["bf16_tflops"]
-    line = {
-        "metric": "W8A8 linear int8 TOP/s (per-token quant + int8 tcgen05 GEMM + fused dequant)",
-        "value": round(value, 2),
-        "unit": "TOP/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(t_step, 5),
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int8",
-        "data": "synthetic (seeded splitmix64/Box-Muller, BASELINE config 2 distributions)",
-        "config": {"workload": "w8a8_linear_4096 (BASELINE config 2)", "M": M, "N": N, "K": K,
-                   "out": "f32", "weights": "pre-quantized per output channel (setup)",
-                   "l2": f"inputs larger than L2: {SETS} rotating device copies of X, codes, "
-                         "quantized W and C (160 MB per step, 640 MB in all); K steps launched "
-                         "back to back between one pair of CUDA events",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+
+    res = {
+        "value": round(value, 2), "ms_per_step": round(t_step, 5),
         # the step is one launch: its average duration is ms_per_step
         "roofline": {"bound": "tensor",
                      "kernel": "gemm_tc2_kernel<I8, fused row quantizer> (2-CTA pairs, 256x256 "
@@ -286,40 +305,121 @@ def run_ours(args, rank, world, local_rank):
                     "gemm_frac": round(gemm_tops / int8_peak, 4),
                     "gemm_traffic": 56.28e6,
                     "quant_ms": round(t_quant, 5), "quant_gbs": round(quant_gbs, 1),
-                    "quant_hbm_frac": round(quant_gbs / peaks["hbm_gbs"], 4)},
-        "parity": parity,
-        "e2e": e2e,
+                    "quant_hbm_frac": round(quant_gbs / peaks["hbm_gbs"], 4),
+                    "quant_alone_ms": round(t_quant_alone, 5),
+                    "quant_alone_hbm_frac": round(quant_alone_gbs / peaks["hbm_gbs"], 4),
+                    "quant_note": "quant_ms: inside the two-launch step (absorbs the previous "
+                                  "GEMM's 64 MB f32 write-back); quant_alone: after an L2 flush"},
         "clocks": clk,
+    }
+    if not args.profile:
+        # parity of this run's output against the oracle on sampled rows
+        res["parity"] = check_parity(rb, X, qx, sx, qw, sw, C)
+        if args.e2e:
+            # e2e through the drop-in C ABI from pinned host buffers
+            res["e2e"] = run_e2e(args, rb, torch, Xh, qw, sw, dev, dist)
+    del Xh, Wh, qx, qw, C, sets, last, busy
+    return res, X, W
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import rouge_b200 as rb
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    peaks, peak_src = load_peaks()
+    if world > 1:
+        return run_sharded_headline(args, rank, world, local_rank, peaks, peak_src)
+
+    args.e2e = not args.profile
+    c2, X, W = run_config2(args, rank, world, local_rank)
+    line = {
+        "metric": METRIC,
+        "value": c2["value"],
+        "unit": "TOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": c2["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded splitmix64/Box-Muller, BASELINE config 2 distributions)",
+        "config": workload_config(world),
+        "roofline": c2["roofline"],
+        "kernels": c2["kernels"],
+        "parity": c2.get("parity"),
+        "e2e": c2.get("e2e"),
+        "clocks": c2["clocks"],
         "gpu_launches": args.steps,
     }
-    if rank == 0 and world == 1 and not args.profile:
-        line["cpu_baseline"] = cpu_baseline(X, W)
-    del X, W, Xh, Wh, qx, qw, C, sets, last
-    if not args.profile:
-        # every rank takes part (same collectives in the same order)
-        line["sharded_config5"] = run_sharded(args, rank, world, local_rank, flush)
-        if world == 1:
-            line["other_configs"] = other_configs(rb, torch, dev, peaks, peak_src, flush)
+    if args.profile:
+        return line
+    line["cpu_baseline"] = cpu_baseline(X, W)
+    del X, W
+    flush = torch.zeros(512 << 20, dtype=torch.uint8, device=dev)
+    # the config-5 GEMM on this one GPU (g = 1), before the long tail of
+    # other configurations
+    line["config5_g1"] = run_config5(args, rank, world, local_rank, peaks, flush, compact=True)
+    line["other_configs"] = other_configs(rb, torch, dev, peaks, peak_src, flush)
+    return line
+
+
+def run_sharded_headline(args, rank, world, local_rank, peaks, peak_src):
+    """N > 1: the headline is BASELINE config 5 sharded over the N ranks
+    (strong scaling, whole-job TOP/s); N config-2 replicas beside it."""
+    import torch
+    dev = torch.device("cuda", local_rank)
+    flush = torch.zeros(512 << 20, dtype=torch.uint8, device=dev)
+    c5 = run_config5(args, rank, world, local_rank, peaks, flush, compact=False)
+    args.e2e = False
+    c2, X, W = run_config2(args, rank, world, local_rank)
+    del X, W
+    line = {
+        "metric": METRIC,
+        "value": c5["value"],
+        "unit": "TOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": c5["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded splitmix64/Box-Muller, BASELINE config 5 distributions)",
+        "config": workload_config(world),
+        "roofline": c5["roofline"],
+        "parity": c5["parity"],
+        "e2e": c5["e2e"],
+        "clocks": c5["clocks"],
+        "gpu_launches": args.steps,
+        "config5": c5["detail"],
+        "config2_replicas": {"value": c2["value"], "ms_per_step": c2["ms_per_step"],
+                             "scaling": "weak", "note": f"{world} independent config-2 steps, "
+                             "one per GPU, no collective (sum over ranks)",
+                             "frac_per_gpu": c2["roofline"]["frac"], "parity": c2.get("parity")},
+    }
     return line
 
 
 # ------------------------------------------------------------------ config 5 (sharded)
 
-M5, N5, K5 = 16384, 28672, 8192
 
-
-def run_sharded(args, rank, world, local_rank, flush):
+def run_config5(args, rank, world, local_rank, peaks, flush, compact):
     """W8A8 GEMM M=16384, K=8192, N=28672 with W split
     N-wise over the `world` GPUs, int32 accumulation, dequant to bf16, the
-    output assembled row-major C[M][N] on every rank. Strong scaling. Two
-    implementations, each timed and checked:
-      fused  the all-gather fused into the GEMM epilogue: every tile is
-             written to every rank's C with NVLink multicast stores
-             (multimem, one per 16 bytes) into symmetric memory, then a
-             device-side barrier across the ranks;
-      nccl   the GEMM in row bands, each band's shard all-gathered by NCCL on
-             a communication stream (overlapping the next band), then a
-             layout kernel (unshard) into C."""
+    output assembled row-major C[M][N] on every rank. Strong scaling.
+
+    The product form (fused: each epilogue tile is written into every
+    rank's C, through NVLink multicast stores or TMA stores to each peer,
+    then a device-side barrier) is timed over K back-to-back steps between
+    one event pair, max over ranks; its e2e adds the host copies. With
+    compact=False the other fused form and the NCCL form (the GEMM in row
+    bands, each band all-gathered by NCCL on a communication stream, then a
+    layout kernel) are timed too, as baselines."""
     import torch
     import rouge_b200 as rb
     from rouge_b200.sharded import FusedShardedW8A8, ShardedW8A8, shard_columns
@@ -327,11 +427,11 @@ def run_sharded(args, rank, world, local_rank, flush):
     if world > 1:
         import torch.distributed as dist
     dev = torch.device("cuda", local_rank)
-    peaks, peak_src = load_peaks()
     ns, ranges = shard_columns(N5, world)
     n0, n1 = ranges[rank]
     ncols = n1 - n0
-    # activations: full X on every rank, quantized per token (setup)
+    # activations: full X on every rank, quantized per token (setup: the
+    # config's inputs are int8)
     x = torch.from_numpy(rb.synth_normal(8, (M5, K5), 0.0, 1.0))
     rb.synth_outliers(8, x.numpy(), 0.01, 20.0)
     xd = x.to(dev)
@@ -355,7 +455,9 @@ def run_sharded(args, rank, world, local_rank, flush):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     orc = O.Oracle()
-    rows = np.array([0, 1, 2047, 2048, 8191, 16383], np.int32)
+    # rows at the first, middle and last row bands of C and at NCCL band
+    # edges; every rank checks its own columns (both shard edges included)
+    rows = np.array([0, 1, 127, 128, 2047, 2048, 8191, 16383], np.int32)
     want = None
     if ncols > 0:
         _, c = orc.gemm_i8(qx[rows.tolist()].cpu().numpy(), qw[:ncols].cpu().numpy(), True,
@@ -365,43 +467,13 @@ def run_sharded(args, rank, world, local_rank, flush):
     tc8 = 2.0 * peaks["bf16_tflops"]
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
 
-    def measure(sh, reserve):
-        prev = rb.lib().rouge_b200_set_sm_budget(max(0, sms - reserve) if reserve else 0)
-        try:
-            for _ in range(2):
-                sh(qx, sx, qw, sw)
-            torch.cuda.synchronize()
-            if dist:
-                dist.barrier()
-            steps = max(3, min(args.steps, 10))
-            g_ms, t_ms = [], []
-            for _ in range(steps):
-                l2_flush(flush)
-                e0 = torch.cuda.Event(enable_timing=True)
-                e1 = torch.cuda.Event(enable_timing=True)
-                evd = {}
-                e0.record()
-                out = sh(qx, sx, qw, sw, events=evd)
-                e1.record()
-                torch.cuda.synchronize()
-                g_ms.append(e0.elapsed_time(evd["gemm_done"]))
-                t_ms.append(e0.elapsed_time(e1))
-            rb.sync_status()
-        finally:
-            rb.lib().rouge_b200_set_sm_budget(prev)
-        gm = sum(g_ms) / len(g_ms)
-        tm = sum(t_ms) / len(t_ms)
-        if dist:
-            t = torch.tensor([gm, tm], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            gm, tm = t.tolist()
-        # parity: this rank's columns of sampled rows, bit-exact
+    def check(out):
+        """Bit-exact columns of this rank on sampled rows; placement of every
+        rank's block in this rank's output (per-row checksums over NCCL)."""
         ok = True
         if ncols > 0:
             got = out[rows.tolist(), n0:n1].view(torch.int16).cpu().numpy().view(np.uint16)
             ok = bool((got == want).all())
-        # placement: every rank's block in this rank's output equals the
-        # block that rank computed (per-row checksums exchanged over NCCL)
         placed = True
         if dist:
             mine = torch.zeros((M5, ns), dtype=torch.float32, device=dev)
@@ -416,63 +488,161 @@ def run_sharded(args, rank, world, local_rank, flush):
             flags = torch.tensor([int(ok), int(placed)], device=dev)
             dist.all_reduce(flags, op=dist.ReduceOp.MIN)
             ok, placed = bool(flags[0].item()), bool(flags[1].item())
-        return {
-            "gemm_ms": round(gm, 4), "total_ms": round(tm, 4),
-            "gemm_tops_per_gpu": round(2.0 * M5 * ns * K5 / (gm * 1e-3) / 1e12, 1),
-            "gemm_frac_per_gpu": round(2.0 * M5 * ns * K5 / (gm * 1e-3) / 1e12 / tc8, 4),
-            "e2e_tops": round(ops / (tm * 1e-3) / 1e12, 1),
-            "sms_for_gemm": sms - reserve,
-            "parity_rows_bit_exact": ok, "placement_checksum_ok": placed,
-        }
+        return {"rows_checked": int(rows.size), "columns_per_rank": ncols,
+                "bf16_bit_exact_sampled_rows": ok, "placement_checksum_ok": placed}
 
-    res = {
-        "workload": "sharded W8A8 GEMM (BASELINE config 5): M=16384 K=8192 N=28672, "
-                    f"W split N-wise over {world} GPU(s), bf16 out, row-major C[M][N] on every rank",
-        "scaling": "strong", "g": world, "shard_cols": ns,
-        "output_bytes_per_gpu_sent": int(M5 * ns * 2) if world > 1 else 0,
-    }
-    notes = {"multimem": "epilogue stages 128-byte row segments and stores them into every rank's "
-                         "C through the NVLink multicast address (multimem.st, 16 B each), then a "
-                         "device-side barrier",
-             "peer-stores": "epilogue stores every 32x32 tile into every rank's C with one TMA "
-                            "tile store per rank (peer pointers), then a device-side barrier",
-             "local": "one GPU: the GEMM writes C directly"}
-    # "fused": the form the library picks for this rank count (TMA stores to
-    # each peer at 2 ranks, multicast from 4); "fused_alt": the other form.
-    auto_mc = world >= 4
-    for key, use_mc in (("fused", auto_mc), ("fused_alt", not auto_mc)):
-        if key == "fused_alt" and world == 1:
-            continue
-        fused = FusedShardedW8A8(M5, N5, K5, rank, world, dev, use_multicast=use_mc)
-        r = measure(fused, 0)
-        r["mode"] = fused.mode
-        r["note"] = notes[fused.mode]
-        res[key] = r
-        fused.close()
-        del fused
+    def max_ranks(vals):
+        if not dist:
+            return vals
+        t = torch.tensor(vals, device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.tolist()
+
+    def timed_steps(sh, steps, clocks=None):
+        """`steps` calls back to back between one event pair (inputs larger
+        than L2), an event after every call and one after every GEMM: total
+        and GEMM-part milliseconds per step, max over ranks."""
+        for _ in range(max(3, args.warmup)):
+            sh(qx, sx, qw, sw)
+        rb.sync_status()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        if clocks:
+            clocks.start()
+            time.sleep(0.3)
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        gd = [dict() for _ in range(steps)]
+        evs[0].record()
+        for i in range(steps):
+            sh(qx, sx, qw, sw, events=gd[i])
+            evs[i + 1].record()
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
-    sh = ShardedW8A8(M5, N5, K5, rank, world, dev, R=2048)
-    r = measure(sh, 8 if world > 1 else 0)
-    r["mode"] = "nccl all-gather per 2048-row band + unshard"
-    if world > 1:
-        r["nvlink_gbs_per_gpu"] = round(M5 * N5 * 2 * (world - 1) / world /
-                                        max(r["total_ms"] - r["gemm_ms"], 1e-6) / 1e6, 1)
-    res["nccl"] = r
-    del sh
-    res["e2e_tops"] = max(v["e2e_tops"] for k, v in res.items() if isinstance(v, dict))
-    # Roofline of the fused compute + collective step: the slower of the
-    # GEMM at the measured tensor peak and the NVLink ingress every GPU must
-    # receive ((g-1)/g of C) at the pool's measured 770 GB/s peer bandwidth.
+        clk = clocks.stop() if clocks else None
+        rb.sync_status()
+        total = evs[0].elapsed_time(evs[steps]) / steps
+        gemm = sum(evs[i].elapsed_time(gd[i]["gemm_done"]) for i in range(steps)) / steps
+        total, gemm = max_ranks([total, gemm])
+        return total, gemm, clk
+
+    def summary(total, gemm):
+        return {"total_ms": round(total, 4), "gemm_ms": round(gemm, 4),
+                "tops": round(ops / (total * 1e-3) / 1e12, 1),
+                "gemm_tops_per_gpu": round(2.0 * M5 * ns * K5 / (gemm * 1e-3) / 1e12, 1),
+                "gemm_frac_per_gpu": round(2.0 * M5 * ns * K5 / (gemm * 1e-3) / 1e12 / tc8, 4)}
+
+    # Roofline of the compute + collective step: the slower of the GEMM at
+    # the measured tensor peak and the NVLink ingress every GPU must receive
+    # ((g-1)/g of C) at the pool's measured 770 GB/s peer bandwidth.
     ingress = M5 * N5 * 2 * (world - 1) / world
-    bound_ms = max(ops / world / (tc8 * 1e12), ingress / 770e9) * 1e3
-    res["roofline"] = {"bound_ms": round(bound_ms, 4),
-                       "bound": "nvlink ingress" if ingress / 770e9 > ops / world / (tc8 * 1e12)
-                       else "tensor",
-                       "ingress_bytes_per_gpu": int(ingress),
-                       "frac_fused": round(bound_ms / res["fused"]["total_ms"], 4),
-                       "peaks": "GEMM 2 x measured bf16; NVLink 770 GB/s measured peer copy"}
+    t_tensor = ops / world / (tc8 * 1e12)
+    t_link = ingress / 770e9
+    bound_ms = max(t_tensor, t_link) * 1e3
+
+    # the product form: the library's choice of fused broadcast for `world`
+    fused = FusedShardedW8A8(M5, N5, K5, rank, world, dev)
+    steps = args.steps if not compact else max(3, min(args.steps, 10))
+    clocks = ClockSampler(local_rank) if not compact and rank == 0 else None
+    total, gemm, clk = timed_steps(fused, steps, clocks)
+    out = fused(qx, sx, qw, sw)
+    parity = check(out)
+    value = ops / (total * 1e-3) / 1e12
+    res = {"value": round(value, 2), "ms_per_step": round(total, 5), "parity": parity,
+           "clocks": clk}
+    prim = summary(total, gemm)
+    prim["mode"] = fused.mode
+    res["roofline"] = {
+        "bound": "nvlink ingress" if t_link > t_tensor else "tensor",
+        "kernel": "gemm_tc2_kernel<I8> with the all-gather fused into its epilogue "
+                  f"({fused.mode}); one launch per step plus a device barrier",
+        "achieved": round(value / world, 2), "peak": round(ops / world / (bound_ms * 1e-3) / 1e12, 2),
+        "unit": "TOP/s per GPU", "frac": round(bound_ms / total, 4),
+        "bound_ms": round(bound_ms, 4), "ingress_bytes_per_gpu": int(ingress),
+        "traffic": None,
+        "peak_source": "the slower of the GEMM at 2 x measured dense bf16 and the NVLink "
+                       "ingress at the pool's measured 770 GB/s peer bandwidth"}
+    if compact:
+        res.update(prim)
+        res["frac_of_int8_peak"] = round(value / tc8, 4)
+        fused.close()
+        del fused, qx, qw, out
+        torch.cuda.synchronize()
+        return res
+
+    # e2e: every step copies the int8 activations (and scales) in from pinned
+    # host memory and a band of 1/world of C's rows (all N columns, so every
+    # rank's block is read on some rank) back to the host.
+    r0, r1 = rank * M5 // world, (rank + 1) * M5 // world
+    qx_h = qx.cpu().pin_memory()
+    sx_h = sx.cpu().pin_memory()
+    c_h = torch.empty((r1 - r0, N5), dtype=torch.bfloat16).pin_memory()
+    cur = torch.cuda.current_stream(dev)
+
+    def e2e_once():
+        qx.copy_(qx_h, non_blocking=True)
+        sx.copy_(sx_h, non_blocking=True)
+        o = fused(qx, sx, qw, sw)
+        c_h.copy_(o[r0:r1], non_blocking=True)
+        cur.synchronize()
+
+    for _ in range(2):
+        e2e_once()
+    if dist:
+        dist.barrier()
+    reps = max(3, min(args.steps, 10))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        e2e_once()
+    dt = max_ranks([(time.perf_counter() - t0) / reps])[0]
+    e2e_ok = bool(torch.equal(c_h.to(dev), out[r0:r1]))
+    if dist:
+        f = torch.tensor([int(e2e_ok)], device=dev)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN)
+        e2e_ok = bool(f.item())
+    res["e2e"] = {"value": round(ops / dt / 1e12, 3), "unit": "TOP/s",
+                  "h2d_bytes_per_step": M5 * K5 + M5 * 4,
+                  "d2h_bytes_per_step": (r1 - r0) * N5 * 2,
+                  "ms_per_step": round(dt * 1e3, 3), "copied_band_matches_device": e2e_ok,
+                  "path": "FusedShardedW8A8 (rouge_b200_gemm_i8_bcast + device barrier); "
+                          "pinned host int8 activations in, a 1/N row band of C out, per rank"}
+    fused.close()
+    del fused, out
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+
+    detail = {"fused": prim, "roofline_note": "frac = bound_ms / total_ms"}
+    # the other fused form (TMA stores to every peer vs multicast stores)
+    alt = FusedShardedW8A8(M5, N5, K5, rank, world, dev,
+                           use_multicast=not FusedShardedW8A8.default_multicast(world))
+    if alt.mode != prim["mode"]:
+        t_a, g_a, _ = timed_steps(alt, max(3, min(args.steps, 10)))
+        r = summary(t_a, g_a)
+        r["mode"] = alt.mode
+        r["parity"] = check(alt(qx, sx, qw, sw))
+        detail["fused_alt"] = r
+    alt.close()
+    del alt
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    # the NCCL baseline: bands of 2048 rows, each all-gathered on a
+    # communication stream while the next band computes (GEMM on SMs - 8)
+    prev = rb.lib().rouge_b200_set_sm_budget(max(0, sms - 8))
+    try:
+        sh = ShardedW8A8(M5, N5, K5, rank, world, dev, R=2048)
+        t_n, g_n, _ = timed_steps(sh, max(3, min(args.steps, 10)))
+        r = summary(t_n, g_n)
+        r["mode"] = "nccl all-gather per 2048-row band + unshard"
+        r["nvlink_gbs_per_gpu"] = round(ingress / max(t_n - g_n, 1e-6) / 1e6, 1)
+        r["parity"] = check(sh(qx, sx, qw, sw))
+        detail["nccl"] = r
+        del sh
+    finally:
+        rb.lib().rouge_b200_set_sm_budget(prev)
+    res["detail"] = detail
     return res
 
 
@@ -1019,58 +1189,104 @@ def ref_lib():
     return O.Reference(), None
 
 
-def ref_sample_step(R, X, Wq_kn, sw, rows, threads):
-    """Reference quantize + int8 GEMM on a row slice of X; returns seconds."""
+def ref_rows(world, threads):
+    """Rows of A per sampled step of the reference CPU path: the same sample
+    for `cpu_baseline` and for the reference arm (about a second of work)."""
+    return min(M, 64 * threads) if world == 1 else min(M5, 32 * threads)
+
+
+def ref_inputs(R, world, threads):
+    """The reference arm's inputs, made by the checker library's copy of the
+    benchmark generator (bit-identical; the product library is not loaded):
+    the sampled rows of A and the whole quantized weight matrix in the
+    reference's B[K][N] layout."""
+    rows = ref_rows(world, threads)
+    if world == 1:
+        X, W = make_inputs(R)
+        qw, sw = R.quantize_i8_channel(W, threads=threads)
+        return {"x": X[:rows], "wq_kn": np.ascontiguousarray(qw.T), "sw": sw, "rows": rows,
+                "N": N, "K": K, "M": M}
+    # config 5: the first rows of the activation stream (counter-based, so
+    # they equal the first rows of the full matrix), quantized per token at
+    # setup as on the GPU side, and all of W quantized per output channel
+    x = R.synth_normal(8, (rows, K5), 0.0, 1.0)
+    R.synth_outliers(8, x, 0.01, 20.0)
+    qx, sx = R.quantize_i8_channel(x, threads=threads)
+    W = R.synth_normal(9, (N5, K5), 0.0, 0.02)
+    qw, sw = R.quantize_i8_channel(W, threads=threads)
+    del W
+    return {"qx": qx, "sx": sx, "wq_kn": np.ascontiguousarray(qw.T), "sw": sw, "rows": rows,
+            "N": N5, "K": K5, "M": M5}
+
+
+def ref_step(R, inp, threads):
+    """One sampled step of the reference CPU path; returns seconds.
+    Config 2: rouge_quantize_i8_channel of the rows + rouge_gemm_i8.
+    Config 5: rouge_gemm_i8 of the int8 rows + rouge_quantize_bf16 of C."""
     t0 = time.perf_counter()
-    q, s = R.quantize_i8_channel(X[:rows], threads=threads)
-    R.gemm_i8(q, Wq_kn, s, 1, sw, 1, threads=threads)
+    if "x" in inp:
+        q, s = R.quantize_i8_channel(inp["x"], threads=threads)
+        R.gemm_i8(q, inp["wq_kn"], s, 1, inp["sw"], 1, threads=threads)
+    else:
+        c = R.gemm_i8(inp["qx"], inp["wq_kn"], inp["sx"], 1, inp["sw"], 1, threads=threads)
+        R.bf16_encode(c, threads=threads)
     return time.perf_counter() - t0
 
 
+def ref_sample_text(inp, threads):
+    what = ("rouge_quantize_i8_channel + rouge_gemm_i8" if "x" in inp
+            else "rouge_gemm_i8 + rouge_quantize_bf16")
+    return (f"{inp['rows']} of {inp['M']} rows of A per step: {what} (row-sliced std::thread over "
+            f"{threads} threads; N={inp['N']}, K={inp['K']})")
+
+
 def cpu_baseline(X, W):
+    """The reference library on this host's cores, on the same row sample as
+    the reference arm (mean of three samples)."""
     R, why = ref_lib()
     if R is None:
         return {"value": None, "unavailable": why}
     threads = R.lib.ref_hw_threads()
     qw, sw = R.quantize_i8_channel(W, threads=threads)
-    Wq_kn = np.ascontiguousarray(qw.T)
-    rows = min(M, 256 * threads)  # ~1 s per thread of reference GEMM work
-    dt = ref_sample_step(R, X, Wq_kn, sw, rows, threads)
+    rows = ref_rows(1, threads)
+    inp = {"x": X[:rows], "wq_kn": np.ascontiguousarray(qw.T), "sw": sw, "rows": rows,
+           "N": N, "K": K, "M": M}
+    ref_step(R, inp, threads)
+    dt = sum(ref_step(R, inp, threads) for _ in range(3)) / 3
     return {"value": round(2.0 * rows * N * K / dt / 1e12, 5), "unit": "TOP/s", "cores": threads,
-            "kind": "reference",
-            "sample": f"{rows} of {M} rows of X: rouge_quantize_i8_channel + rouge_gemm_i8 "
-                      f"(row-sliced std::thread over {threads} threads), {dt:.2f} s"}
+            "kind": "reference", "sample": ref_sample_text(inp, threads) + f", {dt:.3f} s"}
 
 
 def run_reference(args, rank, world):
+    """The reference CPU implementation (oracle/_ref, built from the
+    reference sources) on this host's cores, rank 0 only. Its process loads
+    only the checker libraries under oracle/."""
     if rank != 0:
         return None
     R, why = ref_lib()
     if R is None:
         return {"impl": "reference", "unavailable": why}
-    import rouge_b200 as rb
-    X, W = make_inputs(rb)
     threads = R.lib.ref_hw_threads()
-    qw, sw = R.quantize_i8_channel(W, threads=threads)
-    Wq_kn = np.ascontiguousarray(qw.T)
-    rows = min(M, 64 * threads)
+    inp = ref_inputs(R, world, threads)
     for _ in range(max(1, min(args.warmup, 1))):
-        ref_sample_step(R, X, Wq_kn, sw, rows, threads)
-    times = [ref_sample_step(R, X, Wq_kn, sw, rows, threads) for _ in range(args.steps)]
+        ref_step(R, inp, threads)
+    times = [ref_step(R, inp, threads) for _ in range(args.steps)]
     dt = sum(times) / len(times)
-    value = 2.0 * rows * N * K / dt / 1e12
+    rows, n_, k_, m_ = inp["rows"], inp["N"], inp["K"], inp["M"]
+    value = 2.0 * rows * n_ * k_ / dt / 1e12
     return {
         "impl": "reference",
-        "metric": "W8A8 linear int8 TOP/s (per-token quant + int8 tcgen05 GEMM + fused dequant)",
+        "metric": METRIC,
         "value": round(value, 5), "unit": "TOP/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * M / rows, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
-        "data": "synthetic (seeded, BASELINE config 2 distributions)",
-        "config": {"workload": "w8a8_linear_4096 (BASELINE config 2)", "M": M, "N": N, "K": K,
-                   "out": "f32", "weights": "pre-quantized per output channel (setup)"},
+        "warmup": args.warmup, "ms_per_step": round(dt * 1e3 * m_ / rows, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded splitmix64/Box-Muller, BASELINE config "
+                f"{2 if world == 1 else 5} distributions)",
+        "config": workload_config(world),
         "cpu_baseline": {"value": round(value, 5), "unit": "TOP/s", "cores": threads,
                          "kind": "reference",
-                         "sample": f"{rows} of {M} rows per step (ms_per_step extrapolated to all rows)"},
+                         "sample": ref_sample_text(inp, threads) +
+                         " (ms_per_step extrapolated to all rows)"},
         "e2e": {"value": round(value, 5), "unit": "TOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

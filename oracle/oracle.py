@@ -297,12 +297,37 @@ class Reference:
             ("ref_e4m3_encode_n", None, [_P, _SZ, _P]),
             ("ref_f16_encode_n", None, [_P, _SZ, _P]),
             ("ref_bf16_encode_n", None, [_P, _SZ, _P]),
+            ("ref_bf16_encode_mt", None, [_P, _SZ, _P, _I]),
+            ("ref_synth_uniform", _I, [C.c_uint64, _SZ, _F, _F, _P]),
+            ("ref_synth_normal_at", _I, [C.c_uint64, _SZ, _SZ, _F, _F, _P]),
+            ("ref_synth_outliers_at", C.c_longlong, [C.c_uint64, _SZ, _SZ, _F, _F, _P]),
             ("ref_e4m3_decode_n", None, [_P, _SZ, _P]),
             ("ref_f16_decode_n", None, [_P, _SZ, _P]),
         ]:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+
+    # -- seeded inputs (the benchmark's generator, without its library) -----
+    def synth_uniform(self, seed, shape, lo, hi):
+        out = np.empty(shape, np.float32)
+        assert self.lib.ref_synth_uniform(seed, out.size, lo, hi, _ptr(out)) == 0
+        return out
+
+    def synth_normal(self, seed, shape, mean, std, offset=0):
+        out = np.empty(shape, np.float32)
+        assert self.lib.ref_synth_normal_at(seed, offset, out.size, mean, std, _ptr(out)) == 0
+        return out
+
+    def synth_outliers(self, seed, x, frac, mult, offset=0):
+        assert x.dtype == np.float32 and x.flags.c_contiguous
+        return int(self.lib.ref_synth_outliers_at(seed, offset, x.size, frac, mult, _ptr(x)))
+
+    def bf16_encode(self, x, threads=1):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        out = np.empty(x.shape, np.uint16)
+        self.lib.ref_bf16_encode_mt(_ptr(x), x.size, _ptr(out), threads)
+        return out
 
     def quantize_i8_channel(self, x, threads=1):
         x = np.ascontiguousarray(x, dtype=np.float32)

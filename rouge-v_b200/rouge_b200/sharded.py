@@ -156,11 +156,8 @@ class FusedShardedW8A8:
         g = group if group is not None else dist.group.WORLD
         self.out = symm.empty((M, N), dtype=torch.bfloat16, device=self.device)
         self.handle = symm.rendezvous(self.out, g)
-        # Multicast sends each tile once whatever the rank count; peer TMA
-        # stores send it world - 1 times but move it in larger writes. At 2
-        # ranks the TMA form is faster, from 4 ranks on the multicast form.
         if use_multicast is None:
-            use_multicast = world >= 4
+            use_multicast = self.default_multicast(world)
         has_mc = use_multicast and bool(symm._SymmetricMemory.has_multicast_support(
             symm.DeviceType.CUDA, self.device.index or 0))
         # The handle's pointers address the start of each rank's allocation;
@@ -175,6 +172,13 @@ class FusedShardedW8A8:
         else:
             self.peers = tuple(int(p) + delta for p in self.handle.buffer_ptrs)
             self.mode = "peer-stores"
+
+    @staticmethod
+    def default_multicast(world: int) -> bool:
+        """Multicast sends each tile once whatever the rank count; peer TMA
+        stores send it world - 1 times but move it in larger writes. At 2
+        ranks the TMA form is faster, from 4 ranks on the multicast form."""
+        return world >= 4
 
     @property
     def columns(self) -> Tuple[int, int]:

@@ -89,3 +89,20 @@ def test_conv_vs_reference(orc, ref):
         want = ref.conv2d_f32(x, w, b, stride, pad)
         got = orc.conv2d_nhwc(x.transpose(0, 2, 3, 1), w.transpose(0, 2, 3, 1), b, stride, pad)
         assert rel_l2(got, want.transpose(0, 2, 3, 1).reshape(-1, 24)) < 1e-6
+
+
+def test_reference_arm_inputs_match_the_library_generator(rb, ref):
+    # bench.py's reference arm builds its inputs with the checker library's
+    # copy of the generator (so its process never maps librouge_b200.so);
+    # both arms must see the same bits.
+    a = ref.synth_normal(1, (300, 129), 0.0, 1.0)
+    na = ref.synth_outliers(1, a, 0.01, 20.0)
+    b = rb.synth_normal(1, (300, 129), 0.0, 1.0)
+    nb = rb.synth_outliers(1, b, 0.01, 20.0)
+    assert na == nb and (a.view(np.uint32) == b.view(np.uint32)).all()
+    a = ref.synth_normal(9, (6, 8192), 0.0, 0.02, offset=4 * 8192)
+    b = rb.synth_normal_at(9, 4 * 8192, (6, 8192), 0.0, 0.02)
+    assert (a.view(np.uint32) == b.view(np.uint32)).all()
+    a = ref.synth_uniform(0, (77, 33), -1.0, 1.0)
+    b = rb.synth_uniform(0, (77, 33), -1.0, 1.0)
+    assert (a.view(np.uint32) == b.view(np.uint32)).all()
