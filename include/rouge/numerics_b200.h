@@ -43,9 +43,10 @@ extern "C" {
  * the reference header. */
 #ifndef ROUGE_B200_WITH_REFERENCE_HEADER
 
-/* Replaces RougeGemmConfig, numerics.h:35-41. Accepted and ignored by the
- * GPU entries except as a hint; garbage values never cause out-of-bounds
- * work (the reference normalises them at gemm.cpp:254-275). */
+/* Replaces RougeGemmConfig, numerics.h:35-41. rouge_gemm_f32 reads it as a
+ * tile-shape hint; the other GPU entries accept and ignore it. Garbage
+ * values never cause out-of-bounds work (the reference normalises them at
+ * gemm.cpp:254-275). */
 typedef struct RougeGemmConfig {
   int tile_m;
   int tile_n;
@@ -53,6 +54,15 @@ typedef struct RougeGemmConfig {
   int unroll;
   int split_k;
 } RougeGemmConfig;
+
+/* Replaces RougeGemmProfile, numerics.h:44-48: the configuration a tuning
+ * run chose, its GFLOP/s (2*M*N*K / best wall-clock of a whole call) and
+ * the number of calls made. */
+typedef struct RougeGemmProfile {
+  RougeGemmConfig cfg;
+  double gflops;
+  long long iters;
+} RougeGemmProfile;
 
 #endif /* ROUGE_B200_WITH_REFERENCE_HEADER */
 
@@ -187,13 +197,50 @@ void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B,
  * M*Kp + Kp*Np + 4*(M+N) + 4*M*N bytes (Kp, Np = K, N rounded up to 16, plus
  * alignment) must fit, otherwise ROUGE_B200_ETOOBIG and C is not written.
  * The first call on a device does a one-time set-up (the device address of
- * the array); make it before any stream capture. Calls share the array:
+ * the array); make it before any stream capture. Memory is still reserved
+ * once, by the CUDA driver, outside the calls that follow: the array when
+ * the driver loads its module and the GEMM kernel's code when it is first
+ * launched, which under CUDA's default lazy loading is during the first
+ * call on a device (and the first call of a shape that needs another kernel
+ * variant: single-CTA tiles for small problems, CTA pairs for large ones).
+ * Make one call of each shape class before reserving the GPU's memory for
+ * another allocator or entering a loop that must not allocate (or set
+ * CUDA_MODULE_LOADING=EAGER). Calls share the array:
  * they are serialised by a lock and synchronise before returning; GPU work
  * that overlapped a call's use of the array would race with it. Returns a
  * status (ROUGE_B200_OK on success). */
 int rouge_gemm_i8_noalloc(int M, int N, int K, const int8_t *A, const int8_t *B,
                           const float *scales_a, int a_rows, const float *scales_b,
                           int b_cols, float *C);
+
+/* Replaces rouge_gemm_f32, numerics.h:54-55 (gemm.cpp:291-383).
+ * C[M][N] = A[M][K] * B[K][N], all f32 row-major; C is overwritten, not
+ * accumulated. Computed on tf32 tensor cores with split operands (hi + lo,
+ * three products per element pair: f32 accuracy). cfg selects the tile
+ * shape: tile_m >= 256 CTA pairs on 256 x 256 tiles; tile_m >= 128 one CTA
+ * per 128 x 256 tile (tile_n >= 256) or 128 x 128 tile; otherwise, or NULL,
+ * the library's choice. Every shape gives identical results. Sizes <= 0 or
+ * NULL pointers: no-op. */
+void rouge_gemm_f32(int M, int N, int K, const float *A, const float *B, float *C,
+                    const RougeGemmConfig *cfg);
+
+/* Replace the tuner, numerics.h:311-324 (autotune.cpp:32-127).
+ * rouge_gemm_candidate_count / rouge_gemm_candidate: the candidate
+ * configurations (the default one and the three tile shapes above); an
+ * index out of range gives rouge_gemm_default_config().
+ * rouge_gemm_flops_per_sec: one warm-up call of rouge_gemm_f32 with cfg,
+ * then 2*M*N*K / the best wall-clock of three calls, in GFLOP/s (host
+ * copies included: the time a caller of the drop-in waits); the product is
+ * left in C. 0.0 on invalid arguments or a device failure.
+ * rouge_gemm_tuned: every candidate timed the same way (each call counted in
+ * iters), then the best one's result computed again into C; its config and
+ * GFLOP/s are returned. Invalid arguments: the default config, 0 GFLOP/s,
+ * 0 iterations, C untouched. */
+int rouge_gemm_candidate_count(void);
+RougeGemmConfig rouge_gemm_candidate(int index);
+double rouge_gemm_flops_per_sec(int M, int N, int K, const float *A, const float *B, float *C,
+                                const RougeGemmConfig *cfg);
+RougeGemmProfile rouge_gemm_tuned(int M, int N, int K, const float *A, const float *B, float *C);
 
 /* Replaces rouge_gemm_e4m3, numerics.h:68-69 (fp8.cpp:116-124).
  * A[M][K], B[K][N] OCP E4M3 codes; C f32 = dec(A) * dec(B), f32 accumulate. */

@@ -22,9 +22,9 @@
 
 namespace rb200 {
 
-int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
-                     long long ldb, int b_layout, float alpha, float beta, float *Cp,
-                     long long ldc, cudaStream_t st);
+int launch_gemm_blas_tiles(int kind, int M, int N, int K, const void *A, long long lda,
+                           const void *B, long long ldb, int b_layout, float alpha, float beta,
+                           float *Cp, long long ldc, int tile_hint, cudaStream_t st);
 int launch_gemm_i8(int M, int N, int K, const int8_t *A, long long lda, const int8_t *B,
                    long long ldb, int b_layout, const float *sa, int a_rows, const float *sb,
                    int b_cols, void *Cp, long long ldc, int out_type, cudaStream_t st);
@@ -71,19 +71,22 @@ int padded_k(int type, int k) {
 
 using namespace rb200;
 
-extern "C" {
-
-size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k) {
+extern "C" size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k) {
   const int es = esize_of(ab_type);
   if (!es || m <= 0 || n <= 0 || k <= 0) return 0;
   const size_t kp = padded_k(ab_type, k) * (ab_type == ROUGE_B200_T_F32 ? 3 : 1);
   return rup(static_cast<size_t>(n) * kp * es, 256) + rup(static_cast<size_t>(m) * kp * es, 256);
 }
 
-int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
-                             const void *A, int lda, const void *B, int ldb, float beta, void *C,
-                             int c_type, int ldc, void *workspace, size_t workspace_bytes,
-                             void *stream) {
+namespace rb200 {
+
+// rouge_b200_gemm_colmajor with the tile shape of the call fixed by
+// tile_hint (0: the library's choice; 1 one CTA per 128 x 128 tile, 2 one
+// CTA per 128 x 256, 3 CTA pairs on 256 x 256).
+int gemm_colmajor_tiles(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
+                        const void *A, int lda, const void *B, int ldb, float beta, void *C,
+                        int c_type, int ldc, void *workspace, size_t workspace_bytes,
+                        int tile_hint, void *stream) {
   const int es = esize_of(ab_type);
   if (!es || (transa != 0 && transa != 1) || (transb != 0 && transb != 1))
     return set_status(ROUGE_B200_EINVAL);
@@ -141,8 +144,21 @@ int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab
                           nullptr, 0, C, ldc, ROUGE_B200_OUT_I32, st);
   const int kind = ab_type == ROUGE_B200_T_E4M3 ? 0 : ab_type == ROUGE_B200_T_F16 ? 1
                    : ab_type == ROUGE_B200_T_BF16 ? 2 : 3;
-  return launch_gemm_blas(kind, n, m, static_cast<int>(kp_row), Ap, kp_row, Bp, kp_row,
-                          ROUGE_B200_B_NK, alpha, beta, static_cast<float *>(C), ldc, st);
+  return launch_gemm_blas_tiles(kind, n, m, static_cast<int>(kp_row), Ap, kp_row, Bp, kp_row,
+                                ROUGE_B200_B_NK, alpha, beta, static_cast<float *>(C), ldc,
+                                tile_hint, st);
+}
+
+}  // namespace rb200
+
+extern "C" {
+
+int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
+                             const void *A, int lda, const void *B, int ldb, float beta, void *C,
+                             int c_type, int ldc, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+  return gemm_colmajor_tiles(transa, transb, m, n, k, ab_type, alpha, A, lda, B, ldb, beta, C,
+                             c_type, ldc, workspace, workspace_bytes, 0, stream);
 }
 
 }  // extern "C"

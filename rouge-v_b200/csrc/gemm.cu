@@ -109,7 +109,16 @@ struct GemmArgs {
   // [i*N, +N) into C rows [i*item_m, +item_m). item_m is a multiple of
   // 256, so no tile spans two items.
   int item_m;
+  // Tile shape of this call (kTileHint*): 0 follows the process-wide
+  // rouge_b200_set_tile_mode; the others fix it for this call only (the
+  // RougeGemmConfig of the drop-in float GEMMs).
+  int tile_hint;
 };
+
+constexpr int kTileHintAuto = 0;
+constexpr int kTileHintSingle128 = 1;  // one CTA per 128 x 128 tile
+constexpr int kTileHintSingle256 = 2;  // one CTA per 128 x 256 tile
+constexpr int kTileHintPair = 3;       // CTA pairs, 256 x 256 tiles
 
 constexpr int kStageBytes = 4096;  // one epilogue staging buffer (32 rows x 128 B)
 
@@ -1590,7 +1599,8 @@ bool use_pair_tiles(int M, int N) {
 template <MmaKind KIND>
 int launch_kind(const void *A, long long lda, const void *B, long long ldb, int b_layout,
                 GemmArgs args, int out_type, cudaStream_t st) {
-  const bool pair = use_pair_tiles(args.M, args.N);
+  const bool pair = args.tile_hint != kTileHintAuto ? args.tile_hint == kTileHintPair
+                                                    : use_pair_tiles(args.M, args.N);
   // Single-CTA tiles: BN = 256 unless that leaves most SMs idle; then 128.
   const long long tiles256 =
       static_cast<long long>((args.M + kBM - 1) / kBM) * ((args.N + 255) / 256);
@@ -1598,7 +1608,10 @@ int launch_kind(const void *A, long long lda, const void *B, long long ldb, int 
   const int bn = pair ? 256 : RB200_FORCE_BN;
   (void)tiles256;
 #else
-  const int bn = (pair || tiles256 >= current_sm_count()) ? 256 : 128;
+  const int bn = pair ? 256
+                 : args.tile_hint == kTileHintSingle128 ? 128
+                 : args.tile_hint == kTileHintSingle256 ? 256
+                 : (tiles256 >= current_sm_count() ? 256 : 128);
 #endif
   const int bm = pair ? 2 * kBM : kBM;
   args.num_m = (args.M + bm - 1) / bm;
@@ -1888,11 +1901,14 @@ int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const
 // BLAS-form GEMM on the f16 / bf16 / tf32 / e4m3 kinds:
 // C[M][N] (f32, row pitch ldc) = alpha * A[M][K] . B^T + beta * C, A K-major
 // (row pitch lda), B per b_layout (tf32 needs ROUGE_B200_B_NK).
-// kind: 0 e4m3, 1 f16, 2 bf16, 3 tf32.
-int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
-                     long long ldb, int b_layout, float alpha, float beta, float *Cp,
-                     long long ldc, cudaStream_t st) {
+// kind: 0 e4m3, 1 f16, 2 bf16, 3 tf32. tile_hint (kTileHint*) fixes the
+// tile shape of this call; kTileHintAuto keeps the process-wide choice.
+int launch_gemm_blas_tiles(int kind, int M, int N, int K, const void *A, long long lda,
+                           const void *B, long long ldb, int b_layout, float alpha, float beta,
+                           float *Cp, long long ldc, int tile_hint, cudaStream_t st) {
+  if (tile_hint < kTileHintAuto || tile_hint > kTileHintPair) return set_status(ROUGE_B200_EINVAL);
   GemmArgs g{};
+  g.tile_hint = tile_hint;
   g.M = M; g.N = N; g.K = K;
   g.C = Cp; g.ldc = ldc;
   g.blas = 1;
@@ -1913,6 +1929,13 @@ int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda
     default:
       return set_status(ROUGE_B200_EINVAL);
   }
+}
+
+int launch_gemm_blas(int kind, int M, int N, int K, const void *A, long long lda, const void *B,
+                     long long ldb, int b_layout, float alpha, float beta, float *Cp,
+                     long long ldc, cudaStream_t st) {
+  return launch_gemm_blas_tiles(kind, M, N, K, A, lda, B, ldb, b_layout, alpha, beta, Cp, ldc,
+                                kTileHintAuto, st);
 }
 
 // launch_gemm_blas over `batch` items stacked by rows (K-major B only):

@@ -10,6 +10,7 @@
 // status is kept for rouge_b200_last_error().
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -38,6 +39,10 @@ int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const
 int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const uint16_t *B,
                     long long ldb, int b_layout, int is_bf16, void *Cp, long long ldc,
                     int out_type, cudaStream_t st);
+int gemm_colmajor_tiles(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
+                        const void *A, int lda, const void *B, int ldb, float beta, void *C,
+                        int c_type, int ldc, void *workspace, size_t workspace_bytes,
+                        int tile_hint, void *stream);
 
 namespace {
 
@@ -173,6 +178,74 @@ void gemm_codes_host(int kind, int M, int N, int K, const void *A, const void *B
   };
   run_bands(ctx, M, step, in, comp, out);
   finish_bands(ctx);
+}
+
+// Tile shape of the f32 GEMM named by a RougeGemmConfig. The reference's
+// fields block a CPU cache (gemm.cpp:254-275); on the GPU the config picks
+// the tensor-core tile shape instead: tile_m >= 256 -> CTA pairs on 256 x 256
+// tiles (3); tile_m >= 128 -> one CTA per 128 x 256 tile when tile_n >= 256
+// (2), else per 128 x 128 tile (1); anything smaller, or no config, leaves
+// the choice to the library (0). Every shape gives the same sums: each
+// output element is accumulated over K in the same order.
+int tile_hint_of(const RougeGemmConfig *cfg) {
+  if (!cfg) return 0;
+  if (cfg->tile_m >= 256) return 3;
+  if (cfg->tile_m >= 128) return cfg->tile_n >= 256 ? 2 : 1;
+  return 0;
+}
+
+// The autotuner's candidates (autotune.cpp:32-40 lists CPU blockings):
+// the library's own choice and the three tensor-core tile shapes.
+const RougeGemmConfig kCandidates[] = {
+    {64, 64, 32, 2, 1},    // the default configuration: tile shape chosen per problem
+    {128, 128, 32, 1, 1},  // one CTA per 128 x 128 tile
+    {128, 256, 32, 1, 1},  // one CTA per 128 x 256 tile
+    {256, 256, 32, 1, 1},  // CTA pairs on 256 x 256 tiles
+};
+constexpr int kCandidateCount = static_cast<int>(sizeof(kCandidates) / sizeof(kCandidates[0]));
+
+// C[M][N] = A[M][K] . B[K][N] in f32 accuracy on the tensor cores: the
+// column-major BLAS engine computes C^T = B^T A^T straight into C's memory,
+// packing both operands into split [hi | lo] tf32 form ("3xTF32"). Host
+// pointers; synchronous. Returns a status.
+int gemm_f32_host(int M, int N, int K, const float *A, const float *B, float *C, int hint) {
+  HostCallContext *ctx = host_context();
+  if (!ctx) return rouge_b200_last_error() ? rouge_b200_last_error() : ROUGE_B200_ENODEV;
+  std::lock_guard<std::mutex> g(ctx->lock);
+  const size_t mk = static_cast<size_t>(M) * K, kn = static_cast<size_t>(K) * N,
+               mn = static_cast<size_t>(M) * N;
+  const size_t pack = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, N, M, K);
+  const size_t need = Carve::need(mk * 4) + Carve::need(kn * 4) + Carve::need(mn * 4) +
+                      Carve::need(pack);
+  int s = ensure_workspace(ctx, need);
+  if (s != ROUGE_B200_OK) return s;
+  Carve cv(ctx->ws);
+  float *dA = cv.take<float>(mk);
+  float *dB = cv.take<float>(kn);
+  float *dC = cv.take<float>(mn);
+  uint8_t *dP = cv.take<uint8_t>(pack);
+  cudaStream_t st = ctx->stream;
+  s = cuda_status(cudaMemcpyAsync(dA, A, mk * 4, cudaMemcpyHostToDevice, st));
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(dB, B, kn * 4, cudaMemcpyHostToDevice, st));
+  // column-major view: C^T (N x M, ld N) = B^T (N x K, ld N) . A^T (K x M, ld K)
+  if (s == ROUGE_B200_OK)
+    s = gemm_colmajor_tiles(0, 0, N, M, K, ROUGE_B200_T_F32, 1.0f, dB, N, dA, K, 0.0f, dC,
+                            ROUGE_B200_T_F32, N, dP, pack, hint, st);
+  if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(C, dC, mn * 4, cudaMemcpyDeviceToHost, st));
+  const int f = finish(st);
+  return s != ROUGE_B200_OK ? s : f;
+}
+
+using Clock = std::chrono::steady_clock;
+
+// Wall-clock seconds of one rouge_gemm_f32 call with this tile shape
+// (copies included: what a caller of the drop-in waits for); < 0 on a
+// device failure.
+double time_f32_call(int M, int N, int K, const float *A, const float *B, float *C, int hint) {
+  const Clock::time_point t0 = Clock::now();
+  const int s = gemm_f32_host(M, N, K, A, B, C, hint);
+  const Clock::time_point t1 = Clock::now();
+  return s == ROUGE_B200_OK ? std::chrono::duration<double>(t1 - t0).count() : -1.0;
 }
 
 }  // namespace
@@ -385,6 +458,66 @@ void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, const 
   };
   run_bands(ctx, M, step, in, comp, out);
   finish_bands(ctx);
+}
+
+void rouge_gemm_f32(int M, int N, int K, const float *A, const float *B, float *C,
+                    const RougeGemmConfig *cfg) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return;  // gemm.cpp:293-294
+  gemm_f32_host(M, N, K, A, B, C, tile_hint_of(cfg));
+}
+
+int rouge_gemm_candidate_count(void) { return kCandidateCount; }
+
+RougeGemmConfig rouge_gemm_candidate(int index) {
+  if (index < 0 || index >= kCandidateCount) return rouge_gemm_default_config();  // autotune.cpp:64-66
+  return kCandidates[index];
+}
+
+double rouge_gemm_flops_per_sec(int M, int N, int K, const float *A, const float *B, float *C,
+                                const RougeGemmConfig *cfg) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return 0.0;
+  const int hint = tile_hint_of(cfg);
+  // one untimed warm-up call, then the best of three (autotune.cpp:74-91)
+  if (time_f32_call(M, N, K, A, B, C, hint) < 0.0) return 0.0;
+  double best = 0.0;
+  for (int r = 0; r < 3; ++r) {
+    const double dt = time_f32_call(M, N, K, A, B, C, hint);
+    if (dt < 0.0) return 0.0;
+    if (best == 0.0 || dt < best) best = dt;
+  }
+  const double flops = 2.0 * static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K);
+  return best > 0.0 ? flops / best / 1e9 : 0.0;
+}
+
+RougeGemmProfile rouge_gemm_tuned(int M, int N, int K, const float *A, const float *B, float *C) {
+  RougeGemmProfile prof;
+  prof.cfg = rouge_gemm_default_config();
+  prof.gflops = 0.0;
+  prof.iters = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return prof;
+  // every candidate: one warm-up call and three timed calls, each counted
+  // as a run; the best wall-clock wins (autotune.cpp:93-127)
+  double best = 0.0;
+  for (int i = 0; i < kCandidateCount; ++i) {
+    const int hint = tile_hint_of(&kCandidates[i]);
+    prof.iters += 1;
+    if (time_f32_call(M, N, K, A, B, C, hint) < 0.0) return prof;
+    for (int r = 0; r < 3; ++r) {
+      prof.iters += 1;
+      const double dt = time_f32_call(M, N, K, A, B, C, hint);
+      if (dt < 0.0) return prof;
+      if (best == 0.0 || dt < best) {
+        best = dt;
+        prof.cfg = kCandidates[i];
+      }
+    }
+  }
+  const double flops = 2.0 * static_cast<double>(M) * static_cast<double>(N) * static_cast<double>(K);
+  // C holds the chosen configuration's result (here every candidate's
+  // result is the same, but the reference recomputes it, and so do we)
+  if (gemm_f32_host(M, N, K, A, B, C, tile_hint_of(&prof.cfg)) != ROUGE_B200_OK) return prof;
+  prof.gflops = best > 0.0 ? flops / best / 1e9 : 0.0;
+  return prof;
 }
 
 void rouge_gemm_e4m3(int M, int N, int K, const uint8_t *A, const uint8_t *B, float *C,

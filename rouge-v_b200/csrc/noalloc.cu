@@ -17,8 +17,20 @@
 //    the process exits.
 //  * Host code sees the array's name only as a host-side stand-in, not as a
 //    device address. The first call on a device (with that device current)
-//    looks the device address up with cudaGetSymbolAddress and caches it;
-//    make that first call before any stream capture.
+//    looks the device address up with cudaGetSymbolAddress and caches it
+//    (only a successful lookup is cached; a failed one is retried by the
+//    next call). Make that first call before any stream capture.
+//  * Allocation happens once, outside the caller's loop, if the caller
+//    orders it so: the array's memory is reserved by the CUDA driver when
+//    it loads this file's module, and the GEMM kernel's code when it is
+//    first launched. With CUDA's default lazy module loading both happen
+//    during the first call on a device (and a call whose shape needs a
+//    kernel variant not launched before -- 128-wide single-CTA tiles for
+//    small problems, 256 x 256 CTA pairs for large ones -- loads that
+//    variant's code). A caller that reserves the GPU's memory for its own
+//    allocator, or enters a loop that must not allocate, makes one call of
+//    each shape class it will use before that point (or runs with
+//    CUDA_MODULE_LOADING=EAGER, which loads everything with the library).
 //  * All calls share the array and leave their data in it. The padding and
 //    the status word, which must start at zero, are cleared on every call.
 //    Calls from several host threads are serialised by a lock and each call
@@ -46,9 +58,8 @@ constexpr size_t kNoAllocScratchBytes = size_t(64) << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 struct ScratchSlot {
-  std::once_flag once;
-  void *ptr = nullptr;
-  int status = ROUGE_B200_ENODEV;
+  std::mutex m;
+  void *ptr = nullptr;  // set once a lookup succeeded
 };
 
 std::array<ScratchSlot, 64> &scratch_slots() {
@@ -61,8 +72,10 @@ std::mutex &scratch_lock() {
   return m;
 }
 
-// Device address of the current device's copy of the array (looked up once
-// per device, with that device current).
+// Device address of the current device's copy of the array, looked up with
+// that device current and cached once the lookup has succeeded. A failed
+// lookup (for example the driver could not reserve the array's memory while
+// loading the module) is reported and tried again on the next call.
 void *scratch_for_current_device(int *status) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -71,19 +84,17 @@ void *scratch_for_current_device(int *status) {
     return nullptr;
   }
   ScratchSlot &slot = scratch_slots()[dev];
-  std::call_once(slot.once, [&] {
-    void *p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      cudaGetLastError();
-      slot.status = ROUGE_B200_ECUDA;
-      return;
-    }
-    slot.ptr = p;
-    slot.status = ROUGE_B200_OK;
-  });
-  if (!slot.ptr) *status = set_status(slot.status);
-  return slot.ptr;
+  std::lock_guard<std::mutex> g(slot.m);
+  if (slot.ptr) return slot.ptr;
+  void *p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    cudaGetLastError();
+    *status = set_status(e == cudaErrorMemoryAllocation ? ROUGE_B200_ENOMEM : ROUGE_B200_ECUDA);
+    return nullptr;
+  }
+  slot.ptr = p;
+  return p;
 }
 
 inline size_t up256(size_t b) { return round_up(b, 256); }

@@ -58,6 +58,19 @@ _F = C.c_float
 _SZ = C.c_size_t
 _U64 = C.c_uint64
 
+
+class GemmConfig(C.Structure):
+    """RougeGemmConfig (numerics.h:35-41)."""
+    _fields_ = [("tile_m", _I), ("tile_n", _I), ("tile_k", _I), ("unroll", _I), ("split_k", _I)]
+
+    def astuple(self):
+        return (self.tile_m, self.tile_n, self.tile_k, self.unroll, self.split_k)
+
+
+class GemmProfile(C.Structure):
+    """RougeGemmProfile (numerics.h:44-48)."""
+    _fields_ = [("cfg", GemmConfig), ("gflops", C.c_double), ("iters", C.c_longlong)]
+
 _SIGS = {
     "rouge_b200_last_error": (_I, []),
     "rouge_b200_clear_error": (None, []),
@@ -87,6 +100,12 @@ _SIGS = {
     "rouge_gemm_i8": (None, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
     "rouge_gemm_i8_noalloc": (_I, [_I, _I, _I, _P, _P, _P, _I, _P, _I, _P]),
     "rouge_gemm_e4m3": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_gemm_f32": (None, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_gemm_default_config": (GemmConfig, []),
+    "rouge_gemm_candidate_count": (_I, []),
+    "rouge_gemm_candidate": (GemmConfig, [_I]),
+    "rouge_gemm_flops_per_sec": (C.c_double, [_I, _I, _I, _P, _P, _P, _P]),
+    "rouge_gemm_tuned": (GemmProfile, [_I, _I, _I, _P, _P, _P]),
     "rouge_gemm_f16": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_gemm_bf16": (None, [_I, _I, _I, _P, _P, _P, _P]),
     "rouge_conv2d_f32": (None, [_I] * 9 + [_P, _P, _P, _P, _P]),
@@ -562,6 +581,40 @@ def _host_gemm_codes(name, A, B_kn, dtype):
 
 def host_gemm_e4m3(A, B_kn):
     return _host_gemm_codes("rouge_gemm_e4m3", A, B_kn, np.uint8)
+
+
+def host_gemm_f32(A, B_kn, cfg=None, out=None):
+    """rouge_gemm_f32: A[M][K] . B[K][N] (f32, host arrays); cfg a
+    GemmConfig or None."""
+    A = np.ascontiguousarray(A, np.float32)
+    B_kn = np.ascontiguousarray(B_kn, np.float32)
+    M, K = A.shape
+    N = B_kn.shape[1]
+    out = np.empty((M, N), np.float32) if out is None else out
+    lib().rouge_b200_clear_error()
+    lib().rouge_gemm_f32(M, N, K, _hp(A), _hp(B_kn), _hp(out),
+                         None if cfg is None else C.cast(C.pointer(cfg), _P))
+    _last_error("rouge_gemm_f32")
+    return out
+
+
+def gemm_candidates():
+    """The tuner's candidate configurations (rouge_gemm_candidate)."""
+    return [lib().rouge_gemm_candidate(i) for i in range(lib().rouge_gemm_candidate_count())]
+
+
+def gemm_tuned(A, B_kn, out):
+    """rouge_gemm_tuned on host arrays; returns the GemmProfile."""
+    M, K = A.shape
+    N = B_kn.shape[1]
+    return lib().rouge_gemm_tuned(M, N, K, _hp(A), _hp(B_kn), _hp(out))
+
+
+def gemm_flops_per_sec(A, B_kn, out, cfg=None):
+    M, K = A.shape
+    N = B_kn.shape[1]
+    return lib().rouge_gemm_flops_per_sec(M, N, K, _hp(A), _hp(B_kn), _hp(out),
+                                          None if cfg is None else C.cast(C.pointer(cfg), _P))
 
 
 def host_conv2d_f32(x, w, bias, stride, pad, implicit=False):

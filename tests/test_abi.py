@@ -22,7 +22,9 @@ def test_drop_in_names_match_reference_header(rb):
               "rouge_dequantize_i8_tensor", "rouge_dequantize_i8_channel",
               "rouge_quantize_e4m3", "rouge_dequantize_e4m3", "rouge_quantize_f16",
               "rouge_dequantize_f16", "rouge_quantize_bf16", "rouge_dequantize_bf16",
-              "rouge_gemm_isa_variant", "rouge_gemm_default_config"):
+              "rouge_gemm_isa_variant", "rouge_gemm_default_config", "rouge_gemm_f32",
+              "rouge_gemm_candidate_count", "rouge_gemm_candidate", "rouge_gemm_flops_per_sec",
+              "rouge_gemm_tuned"):
         assert n in rb.declared_symbols()
     assert rb.lib().rouge_gemm_isa_variant() == b"sm_100a+tcgen05"
 
@@ -140,3 +142,44 @@ def test_cublas_shim_exports_declared_api():
     import torch
     if not torch.cuda.is_available():
         assert L.cublasCreate_v2(C.byref(h)) == 1   # CUBLAS_STATUS_NOT_INITIALIZED
+
+
+def test_tuner_candidates_and_default_config(rb):
+    # numerics.h:307-312: the default configuration, the candidate list, and
+    # the default for an index out of range (autotune.cpp:64-66)
+    L = rb.lib()
+    d = L.rouge_gemm_default_config().astuple()
+    assert d == (64, 64, 32, 2, 1)
+    n = L.rouge_gemm_candidate_count()
+    assert n >= 2
+    cands = [L.rouge_gemm_candidate(i).astuple() for i in range(n)]
+    assert len(set(cands)) == n and d in cands
+    assert L.rouge_gemm_candidate(-1).astuple() == d
+    assert L.rouge_gemm_candidate(n).astuple() == d
+
+
+def test_gemm_f32_entries_without_device_or_arguments(rb):
+    import torch
+    L = rb.lib()
+    p = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+    A = np.ones((3, 5), np.float32)
+    B = np.ones((5, 4), np.float32)
+    out = np.full((3, 4), -7.0, np.float32)
+    # invalid sizes / NULL: no-op, zero profile (gemm.cpp:293-294, autotune.cpp:80,101)
+    L.rouge_gemm_f32(0, 4, 5, p(A), p(B), p(out), None)
+    L.rouge_gemm_f32(3, 4, 5, None, p(B), p(out), None)
+    assert (out == -7.0).all()
+    assert L.rouge_gemm_flops_per_sec(3, 4, 0, p(A), p(B), p(out), None) == 0.0
+    prof = L.rouge_gemm_tuned(3, 4, 5, p(A), None, p(out))
+    assert prof.gflops == 0.0 and prof.iters == 0 and prof.cfg.astuple() == (64, 64, 32, 2, 1)
+    if torch.cuda.is_available():
+        return
+    # no device: nothing computed on the CPU, ENODEV kept, zero speed
+    L.rouge_b200_clear_error()
+    L.rouge_gemm_f32(3, 4, 5, p(A), p(B), p(out), None)
+    assert (out == -7.0).all()
+    assert L.rouge_b200_last_error() == rb.ENODEV
+    assert L.rouge_gemm_flops_per_sec(3, 4, 5, p(A), p(B), p(out), None) == 0.0
+    prof = L.rouge_gemm_tuned(3, 4, 5, p(A), p(B), p(out))
+    assert prof.gflops == 0.0 and (out == -7.0).all()
+    L.rouge_b200_clear_error()

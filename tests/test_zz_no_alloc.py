@@ -3,9 +3,11 @@ library allocate device memory (for example a process that reserves the
 GPU's memory for its own allocator at start-up, or a loop that must not
 allocate once it runs). It stages everything in a fixed 64 MiB device array
 instead of an allocated workspace. Checked through the C ABI against the
-existing entry point rouge_gemm_i8 on two calls in a row (the second call
-reuses the array the first one left behind, with a different shape), with
-the same tolerance as the other int8 GEMM tests: bit-exact f32 outputs.
+existing entry point rouge_gemm_i8 and against the oracle on two calls in a
+row (the second call reuses the array the first one left behind, with a
+different shape), with the same tolerance as the other int8 GEMM tests:
+bit-exact f32 outputs. A call after the first ones of its shape class must
+leave the device's free memory unchanged: that is what such a caller needs.
 
 This file is collected last, so a run that stops at the first failure has
 already run every other test; it also passes alone in a fresh process."""
@@ -35,10 +37,12 @@ def _noalloc(rb, A, B, sa, a_rows, sb, b_cols):
     return st, out
 
 
-def test_noalloc_matches_rouge_gemm_i8_on_two_calls(rb, cuda):
-    # an unaligned shape (K, N padded inside the array) and then a larger one
-    for (M, N, K), (a_rows, b_cols), seed in (((300, 200, 100), (1, 1), 1),
-                                              ((1024, 768, 512), (0, 1), 2)):
+CASES = (((300, 200, 100), (1, 1), 1),       # K, N padded inside the array
+         ((1024, 768, 512), (0, 1), 2))      # a larger one, single row scale
+
+
+def test_noalloc_matches_rouge_gemm_i8_on_two_calls(rb, orc, cuda):
+    for (M, N, K), (a_rows, b_cols), seed in CASES:
         A, B, sa, sb = _operands(M, N, K, seed)
         if not a_rows:
             sa = sa[:1].copy()
@@ -46,6 +50,23 @@ def test_noalloc_matches_rouge_gemm_i8_on_two_calls(rb, cuda):
         assert st == rb.OK, rb.lib().rouge_b200_status_string(st)
         want = rb.host_gemm_i8(A, B, sa, a_rows, sb, b_cols)
         assert (got.view(np.uint32) == want.view(np.uint32)).all()
+        # the oracle's ((float)acc * sa) * sb (quant_int8.cpp:189-211), B[K][N]
+        _, oc = orc.gemm_i8(A, B, False, sa, a_rows, sb, b_cols)
+        assert (got.view(np.uint32) == oc.view(np.uint32)).all()
+
+
+def test_noalloc_warm_call_allocates_nothing(rb, cuda):
+    import torch
+    for (M, N, K), (a_rows, b_cols), seed in CASES:
+        A, B, sa, sb = _operands(M, N, K, seed + 10)
+        st, first = _noalloc(rb, A, B, sa, 1, sb, 1)    # the set-up call of this shape class
+        assert st == rb.OK
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        st, again = _noalloc(rb, A, B, sa, 1, sb, 1)
+        assert st == rb.OK
+        assert torch.cuda.mem_get_info()[0] == free0     # the driver reserved nothing more
+        assert (again.view(np.uint32) == first.view(np.uint32)).all()
 
 
 def test_noalloc_refuses_problems_beyond_its_array(rb, cuda):
