@@ -71,22 +71,19 @@ int padded_k(int type, int k) {
 
 using namespace rb200;
 
-extern "C" size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k) {
+extern "C" {
+
+size_t rouge_b200_gemm_colmajor_workspace(int ab_type, int m, int n, int k) {
   const int es = esize_of(ab_type);
   if (!es || m <= 0 || n <= 0 || k <= 0) return 0;
   const size_t kp = padded_k(ab_type, k) * (ab_type == ROUGE_B200_T_F32 ? 3 : 1);
   return rup(static_cast<size_t>(n) * kp * es, 256) + rup(static_cast<size_t>(m) * kp * es, 256);
 }
 
-namespace rb200 {
-
-// rouge_b200_gemm_colmajor with the tile shape of the call fixed by
-// tile_hint (0: the library's choice; 1 one CTA per 128 x 128 tile, 2 one
-// CTA per 128 x 256, 3 CTA pairs on 256 x 256).
-int gemm_colmajor_tiles(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
-                        const void *A, int lda, const void *B, int ldb, float beta, void *C,
-                        int c_type, int ldc, void *workspace, size_t workspace_bytes,
-                        int tile_hint, void *stream) {
+int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
+                             const void *A, int lda, const void *B, int ldb, float beta, void *C,
+                             int c_type, int ldc, void *workspace, size_t workspace_bytes,
+                             void *stream) {
   const int es = esize_of(ab_type);
   if (!es || (transa != 0 && transa != 1) || (transb != 0 && transb != 1))
     return set_status(ROUGE_B200_EINVAL);
@@ -145,20 +142,73 @@ int gemm_colmajor_tiles(int transa, int transb, int m, int n, int k, int ab_type
   const int kind = ab_type == ROUGE_B200_T_E4M3 ? 0 : ab_type == ROUGE_B200_T_F16 ? 1
                    : ab_type == ROUGE_B200_T_BF16 ? 2 : 3;
   return launch_gemm_blas_tiles(kind, n, m, static_cast<int>(kp_row), Ap, kp_row, Bp, kp_row,
-                                ROUGE_B200_B_NK, alpha, beta, static_cast<float *>(C), ldc,
-                                tile_hint, st);
-}
-
-}  // namespace rb200
-
-extern "C" {
-
-int rouge_b200_gemm_colmajor(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
-                             const void *A, int lda, const void *B, int ldb, float beta, void *C,
-                             int c_type, int ldc, void *workspace, size_t workspace_bytes,
-                             void *stream) {
-  return gemm_colmajor_tiles(transa, transb, m, n, k, ab_type, alpha, A, lda, B, ldb, beta, C,
-                             c_type, ldc, workspace, workspace_bytes, 0, stream);
+                                ROUGE_B200_B_NK, alpha, beta, static_cast<float *>(C), ldc, 0, st);
 }
 
 }  // extern "C"
+
+namespace rb200 {
+
+// Row-major f32 GEMM in K-chunks (the engine of the drop-in
+// rouge_gemm_f32): C[M][N] = A[M][K] . B[K][N], device pointers, row
+// pitches K, N and N. The tensor cores accumulate each MMA into f32 with a
+// rounding that loses up to an ulp of the accumulator per step, so an
+// error that grows with the number of steps into one accumulator; here
+// every chunk of kF32ChunkK elements of K is one 3xTF32 GEMM of its own
+// (at most 3 * 256 / 8 = 96 MMA steps), and the chunks are summed in C by
+// the epilogue (C = acc + C, one round-to-nearest add per chunk).
+// Operands are packed chunk by chunk, each chunk's [hi | hi | lo] (A) and
+// [hi | lo | hi] (B^T) blocks side by side in a row of kp_row floats.
+constexpr int kF32ChunkK = 256;
+
+long long f32_chunk_row(int K) {
+  const long long full = K / kF32ChunkK, rest = K % kF32ChunkK;
+  return 3 * (full * kF32ChunkK + static_cast<long long>(rup(rest, 32)));
+}
+
+size_t gemm_f32_rowmajor_workspace(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const size_t row = static_cast<size_t>(f32_chunk_row(K)) * 4;
+  return rup(static_cast<size_t>(M) * row, 256) + rup(static_cast<size_t>(N) * row, 256);
+}
+
+int gemm_f32_rowmajor(int M, int N, int K, const float *A, const float *B, float *C,
+                      void *workspace, size_t workspace_bytes, int tile_hint, cudaStream_t st) {
+  if (M <= 0 || N <= 0 || K <= 0 || !A || !B || !C) return set_status(ROUGE_B200_EINVAL);
+  if (!workspace || workspace_bytes < gemm_f32_rowmajor_workspace(M, N, K) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u))
+    return set_status(ROUGE_B200_ETOOBIG);
+  const long long kp_row = f32_chunk_row(K);
+  uint32_t *Ap = static_cast<uint32_t *>(workspace);                        // [M][kp_row]
+  uint32_t *Bp = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(workspace) +
+                                              rup(static_cast<size_t>(M) * kp_row * 4, 256));
+  const int full = K / kF32ChunkK, rest = K % kF32ChunkK;
+  const long long cw = 3LL * kF32ChunkK;  // packed width of a whole chunk
+  // A rows are contiguous along K (sr = K, sp = 1); B^T row n = column n of
+  // B (sr = 1, sp = N). Whole chunks as one batched pack, then the rest.
+  int s = ROUGE_B200_OK;
+  if (full > 0) {
+    s = pack_launch<uint32_t>(A, kF32ChunkK, K, 1, M, kF32ChunkK, kF32ChunkK, 1, Ap, cw, kp_row,
+                              full, st);
+    if (s == ROUGE_B200_OK)
+      s = pack_launch<uint32_t>(B, static_cast<long long>(kF32ChunkK) * N, 1, N, N, kF32ChunkK,
+                                kF32ChunkK, 2, Bp, cw, kp_row, full, st);
+  }
+  if (s == ROUGE_B200_OK && rest > 0) {
+    const int rp = static_cast<int>(rup(rest, 32));
+    const long long k0 = static_cast<long long>(full) * kF32ChunkK;
+    s = pack_launch<uint32_t>(A + k0, 0, K, 1, M, rest, rp, 1, Ap + full * cw, 0, kp_row, 1, st);
+    if (s == ROUGE_B200_OK)
+      s = pack_launch<uint32_t>(B + k0 * N, 0, 1, N, N, rest, rp, 2, Bp + full * cw, 0, kp_row, 1,
+                                st);
+  }
+  const int chunks = full + (rest > 0 ? 1 : 0);
+  for (int c = 0; s == ROUGE_B200_OK && c < chunks; ++c) {
+    const int kc = c < full ? 3 * kF32ChunkK : 3 * static_cast<int>(rup(rest, 32));
+    s = launch_gemm_blas_tiles(3, M, N, kc, Ap + c * cw, kp_row, Bp + c * cw, kp_row,
+                               ROUGE_B200_B_NK, 1.0f, c == 0 ? 0.0f : 1.0f, C, N, tile_hint, st);
+  }
+  return s;
+}
+
+}  // namespace rb200

@@ -39,10 +39,9 @@ int launch_gemm_e4m3(int M, int N, int K, const uint8_t *A, long long lda, const
 int launch_gemm_f16(int M, int N, int K, const uint16_t *A, long long lda, const uint16_t *B,
                     long long ldb, int b_layout, int is_bf16, void *Cp, long long ldc,
                     int out_type, cudaStream_t st);
-int gemm_colmajor_tiles(int transa, int transb, int m, int n, int k, int ab_type, float alpha,
-                        const void *A, int lda, const void *B, int ldb, float beta, void *C,
-                        int c_type, int ldc, void *workspace, size_t workspace_bytes,
-                        int tile_hint, void *stream);
+size_t gemm_f32_rowmajor_workspace(int M, int N, int K);
+int gemm_f32_rowmajor(int M, int N, int K, const float *A, const float *B, float *C,
+                      void *workspace, size_t workspace_bytes, int tile_hint, cudaStream_t st);
 
 namespace {
 
@@ -204,17 +203,17 @@ const RougeGemmConfig kCandidates[] = {
 };
 constexpr int kCandidateCount = static_cast<int>(sizeof(kCandidates) / sizeof(kCandidates[0]));
 
-// C[M][N] = A[M][K] . B[K][N] in f32 accuracy on the tensor cores: the
-// column-major BLAS engine computes C^T = B^T A^T straight into C's memory,
-// packing both operands into split [hi | lo] tf32 form ("3xTF32"). Host
-// pointers; synchronous. Returns a status.
+// C[M][N] = A[M][K] . B[K][N] in f32 accuracy on the tensor cores: both
+// operands packed into split [hi | lo] tf32 form ("3xTF32") and multiplied
+// in K-chunks summed in C (gemm_f32_rowmajor). Host pointers; synchronous.
+// Returns a status.
 int gemm_f32_host(int M, int N, int K, const float *A, const float *B, float *C, int hint) {
   HostCallContext *ctx = host_context();
   if (!ctx) return rouge_b200_last_error() ? rouge_b200_last_error() : ROUGE_B200_ENODEV;
   std::lock_guard<std::mutex> g(ctx->lock);
   const size_t mk = static_cast<size_t>(M) * K, kn = static_cast<size_t>(K) * N,
                mn = static_cast<size_t>(M) * N;
-  const size_t pack = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, N, M, K);
+  const size_t pack = gemm_f32_rowmajor_workspace(M, N, K);
   const size_t need = Carve::need(mk * 4) + Carve::need(kn * 4) + Carve::need(mn * 4) +
                       Carve::need(pack);
   int s = ensure_workspace(ctx, need);
@@ -227,10 +226,7 @@ int gemm_f32_host(int M, int N, int K, const float *A, const float *B, float *C,
   cudaStream_t st = ctx->stream;
   s = cuda_status(cudaMemcpyAsync(dA, A, mk * 4, cudaMemcpyHostToDevice, st));
   if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(dB, B, kn * 4, cudaMemcpyHostToDevice, st));
-  // column-major view: C^T (N x M, ld N) = B^T (N x K, ld N) . A^T (K x M, ld K)
-  if (s == ROUGE_B200_OK)
-    s = gemm_colmajor_tiles(0, 0, N, M, K, ROUGE_B200_T_F32, 1.0f, dB, N, dA, K, 0.0f, dC,
-                            ROUGE_B200_T_F32, N, dP, pack, hint, st);
+  if (s == ROUGE_B200_OK) s = gemm_f32_rowmajor(M, N, K, dA, dB, dC, dP, pack, hint, st);
   if (s == ROUGE_B200_OK) s = cuda_status(cudaMemcpyAsync(C, dC, mn * 4, cudaMemcpyDeviceToHost, st));
   const int f = finish(st);
   return s != ROUGE_B200_OK ? s : f;
