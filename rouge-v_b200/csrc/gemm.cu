@@ -798,10 +798,10 @@ struct Cfg2 {
   static constexpr int TMEM_COLS = MX ? 512 : 2 * BN;
   static constexpr int B_CHUNKS = (HALF_N * ESIZE) / kBKBytes;
   static constexpr int B_CHUNK_BYTES = B_MN ? BK * kBKBytes : B_BYTES;
-  // fused quantization: two 16 KB row slots (warps 2-3) and 12 more
+  // fused quantization: the prologue's 12 row slots of 16 KB (one per
+  // warp) are stage memory, so the kernel keeps 6 stages; 12 more
   // mbarriers (one per warp's row slot)
   static constexpr int QSLOT = 16384;
-  static constexpr int QSLOT_BYTES = FQ ? 2 * QSLOT : 0;
   static constexpr int BAR_BYTES = FQ ? 512 : 256;
 #ifndef RB200_PAIR_EPI_BUFS  // staging buffers per epilogue warp (tuning builds)
 #define RB200_PAIR_EPI_BUFS 1
@@ -809,18 +809,18 @@ struct Cfg2 {
   static constexpr int EPI_BUFS = RB200_PAIR_EPI_BUFS;
   static constexpr int EPI_BYTES = 8 * EPI_BUFS * kStageBytes;
   static constexpr int STAGE_ROOM =
-      (232448 - 1024 - EPI_BYTES - QSLOT_BYTES - BAR_BYTES) / STAGE_BYTES;
+      (232448 - 1024 - EPI_BYTES - BAR_BYTES) / STAGE_BYTES;
 #ifdef RB200_PAIR_STAGES  // stage-count override for tuning builds
   static constexpr int STAGES = RB200_PAIR_STAGES;
 #else
   static constexpr int STAGES = STAGE_ROOM > 8 ? 8 : STAGE_ROOM;
 #endif
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES + EPI_BYTES + QSLOT_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES + EPI_BYTES;
   static constexpr int SMEM = 1024 + BAR_OFF + BAR_BYTES;
   static_assert(SMEM <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
   static_assert(STAGE_BYTES % 1024 == 0, "stages keep the 1024-byte swizzle alignment");
-  // the prologue's 12 row slots: 10 in stage memory, the 2 quantizer slots
-  static_assert(!FQ || (KIND == MmaKind::I8 && STAGES * STAGE_BYTES >= 10 * QSLOT), "FQ");
+  // the prologue's 12 row slots, all in stage memory
+  static_assert(!FQ || (KIND == MmaKind::I8 && STAGES * STAGE_BYTES >= 12 * QSLOT), "FQ");
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "BN");
   static_assert(!B_MN || B_CHUNKS >= 1, "MN-major B needs whole 128-byte chunks per CTA");
   static_assert(TMEM_COLS == 128 || TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM columns");
@@ -1091,20 +1091,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if constexpr (FQ) {
     // ------------------------------------------------------------ fused quantizer
     // Every warp quantizes its rows of the first round's A blocks through a
-    // row slot of stage memory (warps 2-3: their own slots); the producer
-    // waits on named barrier 1 until the other nine warps that own stage
-    // memory have arrived on it, before its first TMA load into it. Warps
-    // 2-3 go on with the remaining rows meanwhile.
+    // 16 KB row slot of stage memory; the producer waits on named barrier 1
+    // until the other eleven warps have arrived on it, before its first TMA
+    // load into it. Warps 2-3 then go on with the remaining rows.
     const bool qwarp = warp == 2 || warp == 3;
-    uint8_t *slot = qwarp ? smem + C::STAGES * C::STAGE_BYTES + C::EPI_BYTES + (warp - 2) * C::QSLOT
-                          : smem + (warp < 2 ? warp : warp - 2) * C::QSLOT;
+    uint8_t *slot = smem + warp * C::QSLOT;
     fq_rows_first(args, slot, &qbar[warp], warp, lane);
     if (qwarp) {
+      asm volatile("bar.arrive 1, 384;" ::: "memory");  // its slot is free
       for (int r = fq_claim(args, lane); r < args.M; r = fq_claim(args, lane)) fq_row_direct(args, r, lane);
     } else if (warp == 0) {
-      asm volatile("bar.sync 1, 320;" ::: "memory");  // the producer: every stage slot is free
+      asm volatile("bar.sync 1, 384;" ::: "memory");  // the producer: every stage slot is free
     } else {
-      asm volatile("bar.arrive 1, 320;" ::: "memory");
+      asm volatile("bar.arrive 1, 384;" ::: "memory");
     }
   }
 
