@@ -145,15 +145,19 @@ __global__ void __launch_bounds__(384, 1)
   const int r_end = r_beg + per + (b < extra ? 1 : 0);
   uint8_t *slot = qsm + static_cast<size_t>(warp) * row_bytes;
   uint64_t *bar = &bars[warp];
-  // The GEMM that consumes these codes may start its prologue now; it waits
-  // for this grid's completion before it reads them.
-  grid_launch_dependents();
   if (threadIdx.x == 0) {
     next_row = r_beg + static_cast<int>(blockDim.x >> 5);
     for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mbar_init(&bars[w], 1);
     mbar_init_fence();
   }
   __syncthreads();
+  // Launched with programmatic serialisation: the set-up above overlaps the
+  // previous kernel's tail; x (perhaps that kernel's output) is read, and
+  // the codes (perhaps still read by it) written, only after it completed.
+  grid_dependency_wait();
+  // The GEMM that consumes these codes may start its prologue now; it waits
+  // for this grid's completion before it reads them.
+  grid_launch_dependents();
   int r = r_beg + warp;
   if (lane == 0 && r < r_end) {
     mbar_arrive_expect_tx(bar, row_bytes);
@@ -631,9 +635,18 @@ int launch_quant_tma(const float *x, int rows, int cols, float *scales, int8_t *
     if (s != ROUGE_B200_OK) return s;
     attr_done.fetch_or(bit);
   }
-  kern<<<grid, 32 * kWarps, kWarps * cols * 4, st>>>(x, rows, cols, scales, out,
-                                                      device_error_word());
-  return cuda_status(cudaGetLastError());
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(32 * kWarps, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(kWarps) * cols * 4;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, kern, x, rows, cols, scales, out,
+                                        device_error_word()));
 }
 
 int launch_quant_i8_rows(const float *x, int rows, int cols, float *scales, int8_t *out,
