@@ -345,13 +345,19 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs &args, const uint3
     }
   }
 
-  if (args.bcast) {
+  if (args.bcast || (OUT == ROUGE_B200_OUT_BF16 && args.npeers)) {
     // Stage the chunk as row `lane` of the warp's line buffer: 32 rows of
     // 128 bytes (one 64-column bf16 line, chunk pairs in its two halves, or
-    // one 32-column f32 line), 16-byte units XOR-swizzled by row.
-    // bcast_flush writes the buffer out along rows.
+    // one 32-column f32 line), 16-byte units XOR-swizzled by row -- the
+    // layout of a 128-byte-swizzled TMA box. bcast_flush writes the buffer
+    // out along rows to the multicast address; peer_flush stores it as one
+    // 64 x 32 box into every rank's C.
     constexpr int kUnits = OUT == ROUGE_B200_OUT_BF16 ? 4 : 8;
     const int ubase = OUT == ROUGE_B200_OUT_BF16 ? ((col0 >> 5) & 1) * 4 : 0;
+    if (!args.bcast && ubase == 0) {  // a new line: the last line's stores have read the buffer
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
+    }
     const uint32_t rbase = smem_u32(buf) + static_cast<uint32_t>(lane) * 128u;
 #pragma unroll
     for (int q = 0; q < kUnits; ++q)
@@ -431,6 +437,20 @@ __device__ __forceinline__ void bcast_flush(const GemmArgs &args, const uint8_t 
   __syncwarp();
 }
 
+// Stores the warp's staged 64-column bf16 line (see epilogue_chunk) into
+// every rank's C: one 64 x 32 TMA box per rank (128-byte rows), clipped at
+// the M and N edges by the tensor maps.
+__device__ __forceinline__ void peer_flush(const uint8_t *buf, const OutMaps *om, int row0,
+                                           int line_col0, int M, int lane) {
+  fence_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (row0 < M)
+      for (int r = 0; r < om->n; ++r) tma_store_2d(&om->m[r], buf, line_col0, row0);
+    bulk_commit();
+  }
+}
+
 // One epilogue warp's share of one accumulator tile of `width` columns
 // (C columns col0 ..) held from TMEM column tcol: TMEM lanes
 // [32*quarter, +32) (C rows m0 + 32*quarter + lane) and column half `half`.
@@ -488,18 +508,23 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   if (ovl_n == 1) ovl_done();
   // staging buffer of this warp's seq-th chunk (the multicast output stages
   // whole lines in the first buffer)
+  const bool lines = args.bcast || (OUT == ROUGE_B200_OUT_BF16 && args.npeers);
   auto buf = [&]() {
-    return args.bcast ? stage : stage + (NBUF > 1 ? (seq++ & 1) * kStageBytes : 0);
+    return lines ? stage : stage + (NBUF > 1 ? (seq++ & 1) * kStageBytes : 0);
   };
-  // multicast output: flush after chunk c when its line is complete
+  // multicast or peer-store output: flush after chunk c when its line is
+  // complete
   uint32_t staged = 0;
   auto after = [&](int c) {
-    if (!args.bcast) return;
+    if (!lines) return;
     const int cc = col0 + c * 32;
     if (OUT == ROUGE_B200_OUT_BF16) {
       staged |= ((cc >> 5) & 1) ? 0xF0u : 0x0Fu;
       if (((cc >> 5) & 1) || c + 1 == c_end) {
-        bcast_flush<OUT>(args, stage, row0, cc & ~63, staged, lane);
+        if (args.bcast)
+          bcast_flush<OUT>(args, stage, row0, cc & ~63, staged, lane);
+        else
+          peer_flush(stage, om, row0, cc & ~63, args.M, lane);
         staged = 0;
       }
     } else {
@@ -1411,10 +1436,12 @@ int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_
   const CUtensorMapSwizzle osw = b16 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   const int oes = b16 ? 2 : 4;
   if (args.npeers) {
+    // bf16: whole 64-column lines (128-byte rows) per box, see peer_flush
     for (int r = 0; r < args.npeers; ++r) {
       s = make_tmap_2d(&tc.m[r], static_cast<uint8_t *>(args.peers[r]) +
                                      static_cast<size_t>(args.col_off) * oes,
-                       odt, args.N, args.M, static_cast<uint64_t>(args.bld) * oes, 32, 32, osw);
+                       odt, args.N, args.M, static_cast<uint64_t>(args.bld) * oes, b16 ? 64 : 32,
+                       32, CU_TENSOR_MAP_SWIZZLE_128B);
       if (s != ROUGE_B200_OK) return s;
     }
     tc.n = args.npeers;

@@ -122,10 +122,12 @@ class FusedShardedW8A8:
     GEMM: every rank's output C[M][N] is a symmetric-memory buffer (one
     allocation per rank, mapped into every rank's address space), and the
     GEMM epilogue writes each tile of this rank's column block [n0, n1) into
-    every rank's C at once -- either one TMA tile store per rank through the
-    peer pointers, or multimem stores (16 bytes each, staged so that every
-    store instruction covers whole 128-byte row segments) to the buffer's
-    NVLink multicast address, which the NVSwitch replicates to every GPU. No separate exchange, no layout step: the
+    every rank's C at once -- either one TMA store of a 64-column line
+    (128-byte rows) per rank through the peer pointers (the default), or
+    multimem stores (16 bytes each, staged so that every store instruction
+    covers whole 128-byte row segments) to the buffer's NVLink multicast
+    address, which the NVSwitch replicates to every GPU. No separate
+    exchange, no layout step: the
     tiles land row-major at their final place. A device-side barrier across
     the ranks (signal pads, system scope) ends each call, after which every
     rank's C is complete.
@@ -175,10 +177,14 @@ class FusedShardedW8A8:
 
     @staticmethod
     def default_multicast(world: int) -> bool:
-        """Multicast sends each tile once whatever the rank count; peer TMA
-        stores send it world - 1 times but move it in larger writes. At 2
-        ranks the TMA form is faster, from 4 ranks on the multicast form."""
-        return world >= 4
+        """The form used unless the caller chooses: peer TMA stores. A
+        multicast store is written into every bound GPU, the sender's own
+        copy included, so each GPU receives all of C over NVLink; peer
+        stores send a tile world - 1 times but each GPU receives only the
+        other ranks' (world - 1) / world of C. With whole 128-byte lines per
+        row the peer form is the faster one at 2 and at 8 ranks."""
+        del world
+        return False
 
     @property
     def columns(self) -> Tuple[int, int]:
