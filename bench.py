@@ -119,7 +119,7 @@ M = N = K = 4096
 SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
 # DRAM bytes (read + write) of one fused launch: dram__bytes_read.sum +
 # dram__bytes_write.sum of an ncu --set full capture of this workload
-FUSED_TRAFFIC = 116.7e6
+FUSED_TRAFFIC = 115.9e6
 
 
 M5, N5, K5 = 16384, 28672, 8192
@@ -217,19 +217,22 @@ def run_config2(args, rank, world, local_rank):
         # latency does not land inside it.
         busy.view(torch.int32).sum()
 
-    for i in range(args.warmup):
-        step(sets[i % SETS])
-    rb.sync_status()
-
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-    torch.cuda.synchronize()
+    # The clock sampler starts before the warm-up: an idle pause right
+    # before the timed region would let the GPU settle into a slower state
+    # for the first milliseconds of it.
     clocks = ClockSampler(local_rank) if world == 1 else None
     if clocks:
         clocks.start()
         time.sleep(0.3)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+    for i in range(args.warmup):
+        step(sets[i % SETS])
+    rb.sync_status()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
     # Timed region: K steps launched back to back, one event pair around all.
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -514,13 +517,15 @@ def run_config5(args, rank, world, local_rank, peaks, flush, compact):
         """`steps` calls back to back between one event pair (inputs larger
         than L2), an event after every call and one after every GEMM: total
         and GEMM-part milliseconds per step, max over ranks."""
-        for _ in range(max(3, args.warmup)):
-            sh(qx, sx, qw, sw)
-        rb.sync_status()
-        if clocks:  # before the barrier: every rank enters the loop together
+        if clocks:  # before the warm-up (no idle pause before the timed loop)
             clocks.start()
             time.sleep(0.3)
         if dist:
+            dist.barrier()
+        for _ in range(max(3, args.warmup)):
+            sh(qx, sx, qw, sw)
+        rb.sync_status()
+        if dist:  # every rank enters the timed loop together
             dist.barrier()
         torch.cuda.synchronize()
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
