@@ -356,17 +356,23 @@ int rowmajor_gemm(int M, int N, int K, const float *A, const float *W, float bet
                                   beta, C, ROUGE_B200_T_F32, N, ws, ws_bytes, st);
 }
 
+// Workspace of rowmajor_gemm_cat: A' [M][3 Kp] (256-byte aligned), then B'
+// [Nt][3 Kp], Kp = K rounded up to the 32-element k-block.
+size_t rowmajor_gemm_cat_workspace(int M, int K, int Nt) {
+  const size_t Kp = rup(K, 32);
+  return rup(static_cast<size_t>(M) * 3 * Kp * 4, 256) + static_cast<size_t>(Nt) * 3 * Kp * 4;
+}
+
 // Row-major C[M][sum Nw] = A[M][K] . [W_0 | W_1 | ...] for weights W_j
 // [K][Nw_j] (the reference's [in][out]) placed side by side: A packed once,
-// each weight packed into its rows of one B' operand, one GEMM -- the
-// operands and workspace layout of rowmajor_gemm's (A' then B').
+// each weight packed into its rows of one B' operand, one GEMM.
 int rowmajor_gemm_cat(int M, int K, const float *A, int nw, const float *const *W, const int *Nw,
                       float *C, void *ws, size_t ws_bytes, cudaStream_t st) {
   const int Kp = static_cast<int>(rup(K, 32));
   int Nt = 0;
   for (int j = 0; j < nw; ++j) Nt += Nw[j];
   const size_t a_bytes = rup(static_cast<size_t>(M) * 3 * Kp * 4, 256);
-  if (ws_bytes < a_bytes + static_cast<size_t>(Nt) * 3 * Kp * 4) return set_status(ROUGE_B200_ETOOBIG);
+  if (ws_bytes < rowmajor_gemm_cat_workspace(M, K, Nt)) return set_status(ROUGE_B200_ETOOBIG);
   uint32_t *Ap = static_cast<uint32_t *>(ws);
   uint32_t *Bp = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) + a_bytes);
   int s = pack_launch<uint32_t>(A, 0, K, 1, M, K, Kp, 1, Ap, 0, 3 * Kp, 1, st);
@@ -376,6 +382,19 @@ int rowmajor_gemm_cat(int M, int K, const float *A, int nw, const float *const *
   if (s != ROUGE_B200_OK) return s;
   return launch_gemm_blas(3, M, Nt, 3 * Kp, Ap, 3 * Kp, Bp, 3 * Kp, ROUGE_B200_B_NK, 1.0f, 0.0f,
                           C, Nt, st);
+}
+
+// GEMM workspace the transformer block needs: the largest of its
+// projections' (the q | k | v and gate | up GEMMs through
+// rowmajor_gemm_cat, the others through rowmajor_gemm), each sized by the
+// function that lays it out.
+size_t block_gemm_workspace(int S, int D, int Hq, int Hkv, int Dq, int Dff) {
+  size_t g = std::max(rowmajor_gemm_cat_workspace(S, D, (Hq + 2 * Hkv) * Dq),
+                      rowmajor_gemm_cat_workspace(S, D, 2 * Dff));
+  const int shapes[3][3] = {{Hkv * Dq, S, D}, {D, S, Hq * Dq}, {D, S, Dff}};
+  for (auto &sh : shapes)
+    g = std::max(g, rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, sh[0], sh[1], sh[2]));
+  return g;
 }
 
 }  // namespace
@@ -551,13 +570,7 @@ size_t rouge_b200_transformer_block_workspace(int S, int D, int Hq, int Hkv, int
   const size_t sq = rup(static_cast<size_t>(S) * Hq * Dq * 4, 256);
   const size_t skv = rup(static_cast<size_t>(S) * Hkv * Dq * 4, 256);
   const size_t sf = rup(static_cast<size_t>(S) * Dff * 4, 256);
-  size_t g = 0;
-  const int shapes[6][3] = {{(Hq + 2 * Hkv) * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
-                            {2 * Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
-  for (auto &sh : shapes) {
-    const size_t w = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, sh[0], sh[1], sh[2]);
-    if (w > g) g = w;
-  }
+  const size_t g = block_gemm_workspace(S, D, Hq, Hkv, Dq, Dff);
   return 3 * sd + 4 * sq + 4 * skv + 2 * sf + rup(g, 256) +
          attn_plan(S, S, Dq, Hq, Hkv, false).bytes;
 }
@@ -586,13 +599,7 @@ int rouge_b200_transformer_block(int S, int D, int Hq, int Hkv, int Dq, int Dk, 
         *attnflat = ar.take<float>(nq);
   float *k = ar.take<float>(nkv), *v = ar.take<float>(nkv);
   float *gu = ar.take<float>(2 * nf);
-  size_t gws = 0;
-  const int shapes[6][3] = {{(Hq + 2 * Hkv) * Dq, S, D}, {Hkv * Dq, S, D}, {D, S, Hq * Dq},
-                            {2 * Dff, S, D}, {D, S, Dff}, {Hkv * Dq, S, D}};
-  for (auto &sh : shapes) {
-    const size_t w = rouge_b200_gemm_colmajor_workspace(ROUGE_B200_T_F32, sh[0], sh[1], sh[2]);
-    if (w > gws) gws = w;
-  }
+  const size_t gws = block_gemm_workspace(S, D, Hq, Hkv, Dq, Dff);
   void *gw = ar.take<uint8_t>(gws);
   void *aw = ar.p + ar.used;
   const size_t aw_bytes = workspace_bytes - ar.used;
