@@ -117,7 +117,6 @@ class ClockSampler:
 
 M = N = K = 4096
 SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
-PREWARM_STEPS = 40  # untimed steps before the warm-up steps (config-2 loop)
 # DRAM bytes (read + write) of one fused launch: dram__bytes_read.sum +
 # dram__bytes_write.sum of an ncu --set full capture of this workload
 FUSED_TRAFFIC = 115.9e6
@@ -137,7 +136,6 @@ def workload_config(world):
                 "l2": f"inputs larger than L2: {SETS} rotating device copies of X, codes, "
                       "quantized W and C (160 MB per step, 640 MB in all); K steps launched "
                       "back to back between one pair of CUDA events",
-                "prewarm": f"{PREWARM_STEPS} untimed steps before the W warm-up steps",
                 "parallelism": "single GPU"}
     return {"workload": f"sharded_w8a8 (BASELINE config 5): M={M5} K={K5} N={N5} int8 "
                         f"activations and weights, W split N-wise over {world} GPUs, int32 "
@@ -229,12 +227,11 @@ def run_config2(args, rank, world, local_rank):
     dist = None
     if world > 1:
         import torch.distributed as dist
-    # Untimed pre-warm: PREWARM_STEPS steps (about 3 ms of work) before the W
-    # warm-up steps. After an idle stretch (input set-up, the sampler's start)
-    # the GPU runs the first milliseconds of work about 5 % slower; the W
-    # warm-up steps alone (0.36 ms at W = 5) do not cover that.
-    for i in range(PREWARM_STEPS):
-        step(sets[i % SETS])
+    # The device read that precedes the timed region is launched once here:
+    # its first launch in a process loads its kernel, which left the GPU idle
+    # for ~30 us inside the timed region when it happened there.
+    keep_busy()
+    torch.cuda.synchronize()
     for i in range(args.warmup):
         step(sets[i % SETS])
     rb.sync_status()
