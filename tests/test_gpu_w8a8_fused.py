@@ -5,8 +5,10 @@ replaces (rouge_b200_quantize_i8_rows, then rouge_b200_gemm_i8 with per-row
 and per-column scales), which the other tests pin to the oracle; sampled
 rows are also checked against the oracle directly. Cases: the BASELINE
 config-2 shape, ragged M and N, short K, special values (NaN, +-Inf, zero
-and subnormal rows), each output type, repeated calls on one workspace
-(left zeroed every time), and the two-launch path for K > 4096."""
+and subnormal rows), each output type, shapes whose last round of tiles is
+cut N-wise (more tiles than the 74 CTA pairs, not a multiple of them),
+repeated calls on one workspace (left zeroed every time), one workspace
+used for several M, and the two-launch path for K > 4096."""
 import numpy as np
 import pytest
 
@@ -70,7 +72,9 @@ def _weights(rb, torch, rng, N, K, cuda):
 @pytest.mark.parametrize("M,N,K,pair", [(4096, 4096, 4096, False), (1000, 1000, 1024, True),
                                         (384, 512, 48, True), (260, 256, 4096, True),
                                         (128, 4096, 256, True), (1, 272, 16, True),
-                                        (129, 300, 2064, True), (8192, 2048, 1024, False)])
+                                        (129, 300, 2064, True), (8192, 2048, 1024, False),
+                                        (2560, 4096, 4096, True), (4100, 4096, 1024, True),
+                                        (4352, 2816, 384, True), (4096, 4096, 16, True)])
 def test_fused_equals_two_calls(rb, orc, cuda, M, N, K, pair):
     import torch
     rng = np.random.default_rng(M * 7 + N + K)
@@ -100,11 +104,11 @@ def test_fused_equals_two_calls(rb, orc, cuda, M, N, K, pair):
     assert (c.cpu().numpy()[rows].view(np.uint32) == oc.view(np.uint32)).all()
 
 
-def test_repeated_calls_one_workspace(rb, cuda):
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 2048), (4096, 4096, 512)])
+def test_repeated_calls_one_workspace(rb, cuda, M, N, K):
     """Back-to-back launches on one stream reuse the workspace: each must
     see it zeroed by the previous one, with inputs that change every call."""
     import torch
-    M = N = K = 2048
     rng = np.random.default_rng(3)
     wq, sw = _weights(rb, torch, rng, N, K, cuda)
     ws = rb.w8a8_workspace(M, cuda)
@@ -120,6 +124,25 @@ def test_repeated_calls_one_workspace(rb, cuda):
                 for g, w in zip(outs[j], want):
                     assert (_bits(g) == _bits(w)).all()
     assert int(ws.abs().sum()) == 0
+
+
+def test_one_workspace_for_several_m(rb, cuda):
+    """A workspace sized for the largest M serves calls of smaller M in any
+    order: each call leaves the counts it used zeroed."""
+    import torch
+    N, K = 4096, 1024
+    rng = np.random.default_rng(5)
+    wq, sw = _weights(rb, torch, rng, N, K, cuda)
+    ws = rb.w8a8_workspace(8192, cuda)
+    with rb.tile_mode(rb.TILES_PAIR):
+        for M in (8192, 2560, 4096, 384, 8192, 4352):
+            xd = torch.from_numpy(_x(rng, M, K, special=False)).to(cuda)
+            got = _fused(rb, torch, xd, wq, sw, rb.OUT_F32, ws, cuda)
+            want = _two_calls(rb, torch, xd, wq, sw, rb.OUT_F32, cuda)
+            rb.sync_status()
+            for g, w in zip(got, want):
+                assert (_bits(g) == _bits(w)).all()
+            assert int(ws.abs().sum()) == 0
 
 
 def test_long_rows_take_two_launches(rb, cuda):
