@@ -23,12 +23,15 @@ def dev_tensor(a, device):
 
 # ---------------------------------------------------------------- int8 quant
 
-# Row counts of 600 and more take the warp-per-row kernel (one per register
+# Row counts of 296 and more take the warp-per-row kernel (one per register
 # size: rows up to 1024, 2048 and 4096 elements), fewer rows and longer
-# rows the CTA-per-row kernels.
+# rows the CTA-per-row kernels. The warp-per-row cases cover 1 to 24 rows
+# per SM (148 SMs), so that every count of rows left after whole rounds of
+# an SM's 12 warps occurs.
 @pytest.mark.parametrize("shape", [(1, 4), (3, 8), (48, 40), (257, 1028), (64, 8192), (16, 12288),
                                    (1024, 1024), (700, 2044), (1200, 4096), (4096, 4096),
-                                   (640, 4100), (800, 12)])
+                                   (640, 4100), (800, 12), (1924, 12), (1924, 4096), (2072, 1028),
+                                   (592, 1020), (3552, 256)])
 def test_quantize_i8_rows(rb, orc, cuda, shape):
     rng = np.random.default_rng(shape[0] * 7 + shape[1])
     x = rng.standard_normal(shape).astype(np.float32)
@@ -53,7 +56,7 @@ def test_quantize_i8_rows_golden(rb, cuda, golden):
     assert (s.cpu().numpy().view(np.uint32) == golden["q8_scales"].view(np.uint32)).all()
 
 
-@pytest.mark.parametrize("reps", [1, 200])
+@pytest.mark.parametrize("reps", [1, 200, 250])
 def test_quantize_i8_rows_special_values(rb, orc, cuda, reps):
     x = np.zeros((8, 16), np.float32)
     x[1] = np.inf                        # scale inf, codes from NaN products
@@ -73,7 +76,7 @@ def test_quantize_i8_rows_special_values(rb, orc, cuda, reps):
     assert (s.cpu().numpy().view(np.uint32) == os_.view(np.uint32)).all()
 
 
-@pytest.mark.parametrize("reps", [1, 30])
+@pytest.mark.parametrize("reps", [1, 30, 60])
 def test_quantize_i8_rows_near_ties(rb, orc, cuda, reps):
     # Values a few ulps around k + 1/2 under several scales: the products the
     # single-precision fast path must hand to the exact double path.
