@@ -509,7 +509,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tco
   const uint32_t tbase = tcol + (static_cast<uint32_t>(quarter * 32) << 16);
   const int cols_left = args.N - col0;
   const int nchunks = cols_left >= width ? width / 32 : (cols_left + 31) / 32;  // warp-uniform
-  const int per_half = width / 64;
+  const int per_half = width >= 64 ? width / 64 : 1;  // (a 32-wide tile: the first half's warps)
   const int c_end = min(nchunks, (half + 1) * per_half);
   const int c_beg = half * per_half;
   // The fused W8A8 step's column scales: one load per tile instead of one
@@ -1668,7 +1668,8 @@ int launch_out(const void *A, long long lda, const void *B, long long ldb, GemmA
 // Tile shape chooser. A wave of 256 x 256 CTA-pair tiles whenever the
 // 128 x 256 tiles fill every SM at least once (same tile count per SM, half
 // the operand reads per output); otherwise 128 x 128 single-CTA tiles, which
-// spread a small problem over more SMs. rouge_b200_set_tile_mode overrides.
+// spread a small problem over more SMs (128 x 64 or 128 x 32 when even those
+// leave most SMs idle, launch_kind). rouge_b200_set_tile_mode overrides.
 std::atomic<int> g_tile_mode{ROUGE_B200_TILES_AUTO};
 
 bool use_pair_tiles(int M, int N) {
@@ -1709,6 +1710,18 @@ int launch_kind(const void *A, long long lda, const void *B, long long ldb, int 
   if (bn == 256)
     return mn ? launch_out<KIND, 256, true, false>(A, lda, B, ldb, args, out_type, st)
               : launch_out<KIND, 256, false, false>(A, lda, B, ldb, args, out_type, st);
+  // Few 128 x 128 tiles (at most one per two SMs): 128 x 64 or 128 x 32
+  // tiles (K-major B, plain output) put two or four times as many SMs on
+  // the operand feed, shrink each CTA's epilogue and keep a K of up to 8
+  // k-blocks in flight at once in the stage ring.
+  if (!mn && args.tile_hint == kTileHintAuto && !args.bcast && !args.npeers &&
+      2 * args.num_tiles <= current_sm_count()) {
+    const bool n32 = 4 * args.num_tiles <= current_sm_count();
+    args.num_n = (args.N + (n32 ? 31 : 63)) / (n32 ? 32 : 64);
+    args.num_tiles = args.num_m * args.num_n;
+    return n32 ? launch_out<KIND, 32, false, false>(A, lda, B, ldb, args, out_type, st)
+               : launch_out<KIND, 64, false, false>(A, lda, B, ldb, args, out_type, st);
+  }
   return mn ? launch_out<KIND, 128, true, false>(A, lda, B, ldb, args, out_type, st)
             : launch_out<KIND, 128, false, false>(A, lda, B, ldb, args, out_type, st);
 }

@@ -194,7 +194,13 @@ def _check(fn: str, status: int) -> None:
 
 
 def _stream():
+    """The current CUDA stream of the current device, as a handle. torch's
+    raw-handle accessor costs ~0.1 us against ~3 us for building a Stream
+    object; the public call is the fallback where the accessor is absent."""
     import torch
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return C.c_void_p(raw(torch.cuda.current_device()))
     return C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
