@@ -265,8 +265,11 @@ def test_absmax_all_zero(rb, cuda):
 
 # ---------------------------------------------------------------- GEMMs
 
+# Tile widths the shapes take (148 SMs): 32 for the small ones, 64 for
+# (1024, 1024, 1024), (256, 4096, 512) and (600, 1000, 128) (ragged N), 128
+# and CTA pairs for the rest.
 GEMM_SHAPES = [(128, 256, 128), (7, 5, 16), (300, 200, 96), (130, 96, 64), (1024, 1024, 1024),
-               (256, 4096, 512), (4096, 128, 256)]
+               (256, 4096, 512), (4096, 128, 256), (600, 1000, 128), (1000, 1200, 640)]
 
 
 def gemm_operands(rng, M, N, K):
@@ -366,7 +369,8 @@ def test_gemm_e4m3_integer_data_exact(rb, orc, cuda, golden):
     assert (c.cpu().numpy() == want).all()
 
 
-@pytest.mark.parametrize("shape", [(128, 256, 64), (40, 56, 72), (512, 512, 512), (777, 640, 320)])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (40, 56, 72), (512, 512, 512), (777, 640, 320),
+                                   (600, 1000, 128)])
 @pytest.mark.parametrize("bf16", [False, True])
 @pytest.mark.parametrize("layout", ["nk", "kn"])
 def test_gemm_f16(rb, orc, cuda, shape, bf16, layout):
