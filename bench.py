@@ -119,7 +119,7 @@ M = N = K = 4096
 SETS = 4   # rotating device copies of the step's data (inputs larger than L2)
 # DRAM bytes (read + write) of one fused launch: dram__bytes_read.sum +
 # dram__bytes_write.sum of an ncu --set full capture of this workload
-FUSED_TRAFFIC = 115.9e6
+FUSED_TRAFFIC = 116.4e6
 
 
 M5, N5, K5 = 16384, 28672, 8192
