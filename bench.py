@@ -289,6 +289,24 @@ def run_config2(args, rank, world, local_rank):
         t = torch.tensor([t_step, t_gemm, t_quant, t_quant_alone], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         t_step, t_gemm, t_quant, t_quant_alone = t.tolist()
+    # The SM clock the fused launch itself runs at, from its CTAs' own
+    # %clock64 / %globaltimer stamps (rouge_b200_set_clock_probe), on an
+    # untimed repeat of the timed loop: nvidia-smi samples the clock every
+    # 200 ms and so mostly between launches. Same collective steps on every
+    # rank (none inside).
+    with rb.clock_probe(2 * torch.cuda.get_device_properties(dev).multi_processor_count,
+                        dev) as probe:
+        keep_busy()
+        for i in range(args.steps):
+            step(sets[i % SETS])
+        torch.cuda.synchronize()
+        mhz = probe.sm_mhz()
+    rb.sync_status()
+    kernel_clock = {"sm_mhz_median": round(float(np.median(mhz)), 1) if len(mhz) else None,
+                    "sm_mhz_min": round(float(np.min(mhz)), 1) if len(mhz) else None,
+                    "ctas": int(len(mhz)),
+                    "how": "per-CTA %clock64 / %globaltimer stamps of the last fused launch of an "
+                           "untimed repeat of the timed loop (rouge_b200_set_clock_probe)"}
     # parity on the fused launch's own outputs
     last = sets[0]
     step(last)
@@ -331,6 +349,7 @@ def run_config2(args, rank, world, local_rank):
                                   "GEMM's 64 MB f32 write-back); quant_alone: K launches back "
                                   "to back over the rotating input sets"},
         "clocks": clk,
+        "sm_clock_in_kernel": kernel_clock,
     }
     if not args.profile:
         # parity of this run's output against the oracle on sampled rows
@@ -373,6 +392,7 @@ def run_ours(args, rank, world, local_rank):
         "parity": c2.get("parity"),
         "e2e": c2.get("e2e"),
         "clocks": c2["clocks"],
+        "sm_clock_in_kernel": c2["sm_clock_in_kernel"],
         "gpu_launches": args.steps,
     }
     if args.profile:

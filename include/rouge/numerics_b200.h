@@ -106,7 +106,9 @@ int rouge_b200_set_sm_budget(int sms);
  * RougeGemmConfig blocking is a CPU cache blocking and is ignored).
  *   AUTO   256 x 256 tiles computed by 2-SM CTA pairs when 128 x 256 tiles
  *          would fill every SM, else 128 x 128 tiles on single CTAs
- *   SINGLE single-CTA tiles only (128 x 256 or 128 x 128)
+ *          (128 x 64 or 128 x 32 when those would fill at most half or a
+ *          quarter of the SMs)
+ *   SINGLE single-CTA tiles only (128 x 256 down to 128 x 32)
  *   PAIR   CTA-pair tiles only (256 x 256)
  * int8 results are identical in every mode (exact int32 accumulation).
  * Process-wide; returns the previous
@@ -115,6 +117,21 @@ int rouge_b200_set_sm_budget(int sms);
 #define ROUGE_B200_TILES_SINGLE 1
 #define ROUGE_B200_TILES_PAIR 2
 int rouge_b200_set_tile_mode(int mode);
+
+/* Clock probe (a measurement aid; no reference counterpart). With `stamps`
+ * non-NULL, every later GEMM / convolution launch on the current device
+ * (the one current when this is called) has each of its first `ctas` CTAs
+ * write four 64-bit words at stamps + 4 * cta: the SM cycle counter
+ * (%clock64) and the global nanosecond timer (%globaltimer) when the CTA
+ * starts, then both again when it ends. (w[2] - w[0]) / (w[3] - w[1]) is
+ * the SM clock in GHz that the CTA ran at -- under the power cap often
+ * well below the clock that nvidia-smi samples between launches.
+ * `stamps`: 32 * ctas bytes of that device's memory; every launch
+ * overwrites it, so read it after the launch of interest. NULL or ctas == 0
+ * switches the probe off (the default). Process-wide; change it only while
+ * no launch is being issued. Returns ROUGE_B200_OK, or ROUGE_B200_EINVAL
+ * for ctas < 0. */
+int rouge_b200_set_clock_probe(unsigned long long *stamps, int ctas);
 
 /* Synchronises `stream`, then reads and clears the current device's error
  * word, which kernels set when a bounded device-side wait runs out.

@@ -113,7 +113,21 @@ struct GemmArgs {
   // rouge_b200_set_tile_mode; the others fix it for this call only (the
   // RougeGemmConfig of the drop-in float GEMMs).
   int tile_hint;
+  // Clock probe (rouge_b200_set_clock_probe): CTA b < clk_n writes
+  // %clock64 and %globaltimer at its start to clk[4b], clk[4b + 1] and at
+  // its end to clk[4b + 2], clk[4b + 3]. Null: no stamps.
+  unsigned long long *clk;
+  int clk_n;
 };
+
+__device__ __forceinline__ void clock_stamp(const GemmArgs &args, int slot) {
+  if (args.clk && static_cast<int>(blockIdx.x) < args.clk_n) {
+    unsigned long long c;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+    args.clk[4 * blockIdx.x + slot] = c;
+    args.clk[4 * blockIdx.x + slot + 1] = global_timer_ns();
+  }
+}
 
 constexpr int kTileHintAuto = 0;
 constexpr int kTileHintSingle128 = 1;  // one CTA per 128 x 128 tile
@@ -651,6 +665,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  if (threadIdx.x == 0) clock_stamp(args, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -821,6 +836,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after_sync();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+  if (threadIdx.x == 0) clock_stamp(args, 2);
 }
 
 // ----------------------------------------------------------- CTA-pair tiles
@@ -1130,6 +1146,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int nclusters = static_cast<int>(gridDim.x >> 1);
   const uint32_t peer_abort = mapa_shared(smem_u32(const_cast<int *>(abort)), rank ^ 1u);
 
+  if (threadIdx.x == 0) clock_stamp(args, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -1470,7 +1487,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   }
+  if (threadIdx.x == 0) clock_stamp(args, 2);
 }
+
+// The clock probe of rouge_b200_set_clock_probe: stamp buffer, its CTA
+// capacity and the device it lives on (launches on other devices skip it).
+std::atomic<unsigned long long *> g_clock_stamps{nullptr};
+std::atomic<int> g_clock_ctas{0};
+std::atomic<int> g_clock_dev{-1};
 
 // Builds the output map and launches one GEMM / convolution.
 // make_b(box_rows, map) encodes the B operand's tensor map with boxes of
@@ -1478,6 +1502,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 template <MmaKind KIND, int BN, bool B_MN, int OUT, bool CONV, bool PAIR, bool FQ = false, class MakeB>
 int launch_tiles(const CUtensorMap &ta, MakeB make_b, GemmArgs args, cudaStream_t st) {
   int s = ROUGE_B200_OK;
+  if (unsigned long long *stamps = g_clock_stamps.load()) {
+    if (g_clock_dev.load() == current_device()) {
+      args.clk = stamps;
+      args.clk_n = g_clock_ctas.load();
+    }
+  }
   CUtensorMap tb;
   s = make_b(PAIR ? BN / 2 : BN, &tb);
   if (s != ROUGE_B200_OK) return s;
@@ -2171,6 +2201,18 @@ int rouge_b200_gemm_mx(int M, int N, int K, const uint8_t *A, int fmt_a, const u
   if (s != ROUGE_B200_OK) return s;
   return launch_gemm_mx(M, N, K, A, K, fmt_a, sfa, B, K, fmt_b, sfb, C, ldc, out_type,
                         as_stream(stream));
+}
+
+int rouge_b200_set_clock_probe(unsigned long long *stamps, int ctas) {
+  if (ctas < 0) return set_status(ROUGE_B200_EINVAL);
+  if (!stamps || ctas == 0) {
+    g_clock_stamps.store(nullptr);
+    return ROUGE_B200_OK;
+  }
+  g_clock_dev.store(current_device());
+  g_clock_ctas.store(ctas);
+  g_clock_stamps.store(stamps);
+  return ROUGE_B200_OK;
 }
 
 int rouge_b200_set_tile_mode(int mode) {

@@ -83,6 +83,7 @@ _SIGS = {
     "rouge_b200_w8a8_linear": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P]),
     "rouge_b200_set_sm_budget": (_I, [_I]),
     "rouge_b200_set_tile_mode": (_I, [_I]),
+    "rouge_b200_set_clock_probe": (_I, [_P, _I]),
     "rouge_quantize_e4m3": (C.c_uint8, [_F]),
     "rouge_dequantize_e4m3": (_F, [C.c_uint8]),
     "rouge_quantize_f16": (C.c_uint16, [_F]),
@@ -482,6 +483,36 @@ class tile_mode:
     def __exit__(self, *exc):
         lib().rouge_b200_set_tile_mode(self.prev)
         return False
+
+
+class clock_probe:
+    """Context manager recording, for every GEMM / convolution launch on the
+    current device while it is active, each of the first `ctas` CTAs'
+    %clock64 and %globaltimer at its start and end
+    (rouge_b200_set_clock_probe). After the launch of interest,
+    `sm_mhz()` gives the SM clock each CTA ran at, from those stamps."""
+
+    def __init__(self, ctas: int, device=None):
+        import torch
+        self.ctas = int(ctas)
+        self.stamps = torch.zeros(4 * self.ctas, dtype=torch.int64, device=device or "cuda")
+
+    def __enter__(self):
+        _check("rouge_b200_set_clock_probe",
+               lib().rouge_b200_set_clock_probe(_dp(self.stamps), self.ctas))
+        return self
+
+    def __exit__(self, *exc):
+        lib().rouge_b200_set_clock_probe(None, 0)
+        return False
+
+    def sm_mhz(self):
+        """Per-CTA SM clock in MHz of the last launch (CTAs that wrote no
+        stamps are left out)."""
+        import numpy as np
+        w = self.stamps.view(-1, 4).cpu().numpy().astype(np.float64)
+        ok = (w[:, 3] > w[:, 1]) & (w[:, 2] > w[:, 0])
+        return (w[ok, 2] - w[ok, 0]) / (w[ok, 3] - w[ok, 1]) * 1000.0
 
 
 # ------------------------------------------------------------- host drop-in API
