@@ -285,10 +285,23 @@ def run_config2(args, rank, world, local_rank):
     torch.cuda.synchronize()
     rb.sync_status()
     t_quant_alone = q0.elapsed_time(q1) / args.steps
+    # the plain GEMM alone: K launches back to back over the rotating sets
+    # (the two-launch timing above puts an event between every two kernels,
+    # which keeps each GEMM's set-up from overlapping the kernel before it)
+    keep_busy()
+    g0 = torch.cuda.Event(enable_timing=True)
+    g1 = torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for i in range(args.steps):
+        gemm(sets[i % SETS])
+    g1.record()
+    torch.cuda.synchronize()
+    rb.sync_status()
+    t_gemm_alone = g0.elapsed_time(g1) / args.steps
     if dist:
-        t = torch.tensor([t_step, t_gemm, t_quant, t_quant_alone], device=dev)
+        t = torch.tensor([t_step, t_gemm, t_quant, t_quant_alone, t_gemm_alone], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_step, t_gemm, t_quant, t_quant_alone = t.tolist()
+        t_step, t_gemm, t_quant, t_quant_alone, t_gemm_alone = t.tolist()
     # The SM clock the fused launch itself runs at, from its CTAs' own
     # %clock64 / %globaltimer stamps (rouge_b200_set_clock_probe), on an
     # untimed repeat of the timed loop: nvidia-smi samples the clock every
@@ -341,13 +354,15 @@ def run_config2(args, rank, world, local_rank):
                     "gemm_ms": round(t_gemm, 5), "gemm_tops": round(gemm_tops, 2),
                     "gemm_frac": round(gemm_tops / int8_peak, 4),
                     "gemm_traffic": 56.28e6,
+                    "gemm_alone_ms": round(t_gemm_alone, 5),
+                    "gemm_alone_frac": round(ops / (t_gemm_alone * 1e-3) / 1e12 / int8_peak, 4),
                     "quant_ms": round(t_quant, 5), "quant_gbs": round(quant_gbs, 1),
                     "quant_hbm_frac": round(quant_gbs / peaks["hbm_gbs"], 4),
                     "quant_alone_ms": round(t_quant_alone, 5),
                     "quant_alone_hbm_frac": round(quant_alone_gbs / peaks["hbm_gbs"], 4),
                     "quant_note": "quant_ms: inside the two-launch step (absorbs the previous "
-                                  "GEMM's 64 MB f32 write-back); quant_alone: K launches back "
-                                  "to back over the rotating input sets"},
+                                  "GEMM's 64 MB f32 write-back); quant_alone / gemm_alone: K "
+                                  "launches back to back over the rotating input sets"},
         "clocks": clk,
         "sm_clock_in_kernel": kernel_clock,
     }
