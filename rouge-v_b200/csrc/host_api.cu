@@ -12,6 +12,7 @@
 
 #include <chrono>
 #include <cstdint>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -425,15 +426,13 @@ void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, const 
   float *dsa = cv.take<float>(na);
   float *dsb = cv.take<float>(nb);
   float *dC = cv.take<float>(static_cast<size_t>(M) * N);
-  // B, its padding and the scales first on the copy-in stream, then bands
+  // B's padding, the scales and B first on the copy-in stream, then bands
   // of A rows: while band b's output is copied out, band b+1 computes and
   // band b+2 is copied in.
   cudaStream_t sin = ctx->in_stream;
   if (Kp != static_cast<size_t>(K) || Np != static_cast<size_t>(N)) {
     if (cuda_status(cudaMemsetAsync(dB, 0, Kp * Np, sin)) != ROUGE_B200_OK) return;
   }
-  if (cuda_status(cudaMemcpy2DAsync(dB, Np, B, N, N, K, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
-    return;
   if (cuda_status(cudaMemcpyAsync(dsa, scales_a, na * 4, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
     return;
   if (cuda_status(cudaMemcpyAsync(dsb, scales_b, nb * 4, cudaMemcpyHostToDevice, sin)) != ROUGE_B200_OK)
@@ -452,9 +451,64 @@ void rouge_gemm_i8(int M, int N, int K, const int8_t *A, const int8_t *B, const 
                                        dC + static_cast<size_t>(r0) * N,
                                        static_cast<size_t>(n) * N * 4, cudaMemcpyDeviceToHost, s));
   };
-  run_bands(ctx, M, step, in, comp, out);
+  const int nbands = (M + step - 1) / step;
+  if (nbands < 2 || Kp * Np < (size_t(8) << 20) || Np < 2048 || 2 * nbands + 8 > kBandEvents) {
+    if (cuda_status(cudaMemcpy2DAsync(dB, Np, B, N, N, K, cudaMemcpyHostToDevice, sin)) !=
+        ROUGE_B200_OK)
+      return;
+    run_bands(ctx, M, step, in, comp, out);
+    finish_bands(ctx);
+    return;
+  }
+  // A large B would hold every band back until all of it is on the device,
+  // and the copy-out (the longest PCIe leg) with it. So B comes in four
+  // column blocks, the first band's rows right after the first block, and
+  // that band is computed and copied out block by block as the blocks
+  // arrive; the other bands follow as above, with the whole of B.
+  const int n0 = step;  // the first band's rows (nbands >= 2: a whole band)
+  const size_t cbw = round_up((Np + 3) / 4, 16);
+  cudaEvent_t *ev = ctx->ev + 2 * nbands;  // [0, 4): B blocks in, [4, 8): band-0 blocks done
+  cudaEvent_t e_a0 = ctx->ev[0];
+  int st = ROUGE_B200_OK;
+  int nblk = 0;
+  for (size_t c0 = 0; st == ROUGE_B200_OK && c0 < static_cast<size_t>(N); c0 += cbw, ++nblk) {
+    const size_t w = std::min(cbw, static_cast<size_t>(N) - c0);
+    st = cuda_status(cudaMemcpy2DAsync(dB + c0, Np, B + c0, N, w, K, cudaMemcpyHostToDevice, sin));
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaEventRecord(ev[nblk], sin));
+    if (st == ROUGE_B200_OK && nblk == 0) {
+      st = in(0, n0, sin);
+      if (st == ROUGE_B200_OK) st = cuda_status(cudaEventRecord(e_a0, sin));
+    }
+  }
+  if (st == ROUGE_B200_OK) st = cuda_status(cudaStreamWaitEvent(ctx->stream, e_a0, 0));
+  for (int j = 0; st == ROUGE_B200_OK && j < nblk; ++j) {
+    const size_t c0 = j * cbw, w = std::min(cbw, static_cast<size_t>(N) - c0);
+    st = cuda_status(cudaStreamWaitEvent(ctx->stream, ev[j], 0));
+    if (st == ROUGE_B200_OK)
+      st = launch_gemm_i8(n0, static_cast<int>(w), static_cast<int>(Kp), dA, Kp, dB + c0, Np,
+                          ROUGE_B200_B_KN, dsa, a_rows ? 1 : 0, b_cols ? dsb + c0 : dsb,
+                          b_cols ? 1 : 0, dC + c0, N, ROUGE_B200_OUT_F32, ctx->stream);
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaEventRecord(ev[4 + j], ctx->stream));
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaStreamWaitEvent(ctx->out_stream, ev[4 + j], 0));
+    if (st == ROUGE_B200_OK)
+      st = cuda_status(cudaMemcpy2DAsync(C + c0, static_cast<size_t>(N) * 4, dC + c0,
+                                         static_cast<size_t>(N) * 4, w * 4, n0,
+                                         cudaMemcpyDeviceToHost, ctx->out_stream));
+  }
+  for (int b = 1; st == ROUGE_B200_OK && b < nbands; ++b) {
+    const int r0 = b * step, n = M - r0 < step ? M - r0 : step;
+    cudaEvent_t e_in = ctx->ev[2 * b], e_comp = ctx->ev[2 * b + 1];
+    st = in(r0, n, sin);
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaEventRecord(e_in, sin));
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaStreamWaitEvent(ctx->stream, e_in, 0));
+    if (st == ROUGE_B200_OK) st = comp(r0, n, ctx->stream);
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaEventRecord(e_comp, ctx->stream));
+    if (st == ROUGE_B200_OK) st = cuda_status(cudaStreamWaitEvent(ctx->out_stream, e_comp, 0));
+    if (st == ROUGE_B200_OK) st = out(r0, n, ctx->out_stream);
+  }
   finish_bands(ctx);
 }
+
 
 void rouge_gemm_f32(int M, int N, int K, const float *A, const float *B, float *C,
                     const RougeGemmConfig *cfg) {

@@ -116,9 +116,12 @@ def test_quantize_i8_channel_banded(rb, orc, cuda, rows, cols):
 
 
 # Ragged last bands, per-row and single scales on either side; the last
-# case is below the banding threshold.
+# of the first four is below the banding threshold. The last two have a B
+# of 8 MB and more, which comes in four column blocks that the first band
+# is computed and copied out by (a ragged last block in the last case).
 @pytest.mark.parametrize("M,N,K,a_rows,b_cols", [(1000, 2048, 1024, 1, 1), (1100, 2000, 1000, 0, 1),
-                                                 (1300, 1700, 528, 1, 0), (700, 600, 256, 1, 1)])
+                                                 (1300, 1700, 528, 1, 0), (700, 600, 256, 1, 1),
+                                                 (1024, 4096, 2048, 1, 1), (600, 4100, 2064, 0, 1)])
 def test_gemm_i8_banded(rb, orc, cuda, M, N, K, a_rows, b_cols):
     rng = np.random.default_rng(M + N + K)
     A = rng.integers(-127, 128, (M, K), dtype=np.int8)
